@@ -1,0 +1,125 @@
+/*
+ * fa_b200.h -- C ABI of the B200 (sm_100a) FlashAttention-2 library.
+ *
+ * Plain pointers, sizes and element strides; no torch types.  Every entry
+ * point is stateless and re-entrant, launches on the given CUDA stream
+ * (cudaStream_t passed as void*, NULL = legacy default stream) and returns 0
+ * on success or a nonzero FA_ERR_* code.  No exceptions cross this boundary.
+ *
+ * Layouts: q, o, dO, dq are (B, Hq, Nq, D) fp16; k, v, dk, dv are
+ * (B, Hkv, Nk, D) fp16, each with element strides {batch, head, seq} and a
+ * unit stride over D.  lse and delta are (B, Hq, Nq) fp32, contiguous.
+ * D is 32, 64 or 128.  Hq % Hkv == 0; query head h reads K/V head
+ * h / (Hq / Hkv).  TMA needs 16-byte aligned base pointers and strides.
+ *
+ * lse holds the base-2 log-sum-exp of each query row in the scaled domain:
+ * lse2_i = log2(sum_j exp2(scale * log2(e) * q_i . k_j)), the same unit the
+ * reference saves (triton_flash_attention/attention.py:177,230).
+ *
+ * Positions: query row i sits at global position q_offset + i and key row j
+ * at k_offset + j.  With causal != 0 a key is visible iff its position is
+ * <= the query's.  Zero offsets and Nq == Nk give the reference's
+ * self-attention mask (attention.py:65,300,343); nonzero offsets serve ring
+ * context parallelism, where one call sees one K/V chunk.  A query row with
+ * no visible key gets o = 0 and lse = -inf.
+ *
+ * accumulate_fp32 (backward only): 0 writes the gradient as fp16; nonzero
+ * treats the gradient pointers as fp32 buffers with the same element strides
+ * and adds this call's contribution to them (ring context parallelism sums a
+ * chunk's gradient over the ranks this way).
+ */
+#ifndef FA_B200_H
+#define FA_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FA_OK = 0,
+  FA_ERR_UNSUPPORTED_HEAD_DIM = 1, /* D not in {32, 64, 128} */
+  FA_ERR_BAD_SHAPE = 2,            /* a size <= 0, Hq % Hkv != 0, ... */
+  FA_ERR_MISALIGNED = 3,           /* pointer or stride breaks TMA's 16-byte rule */
+  FA_ERR_LAUNCH = 4,               /* the CUDA launch itself failed */
+  FA_ERR_TENSOR_MAP = 5,           /* cuTensorMapEncodeTiled refused a descriptor */
+  FA_ERR_DRIVER = 6,               /* the driver entry point could not be resolved */
+  FA_ERR_DEVICE_TIMEOUT = 7,       /* a kernel's bounded wait gave up (see fa_device_status) */
+  FA_ERR_NO_DEVICE = 8             /* no sm_100 device is current */
+};
+
+/* Forward: O = softmax(scale * Q K^T [+ causal mask]) V and the base-2 LSE.
+ * Replaces TritonAttention.forward's launch of _attn_fwd
+ * (triton_flash_attention/attention.py:676-722, kernel :90-234). */
+FA_API int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+           int B, int Hq, int Hkv, int Nq, int Nk, int D,
+           const int64_t* q_strides, const int64_t* k_strides,
+           const int64_t* v_strides, const int64_t* o_strides,
+           float softmax_scale, int causal, int q_offset, int k_offset,
+           void* stream);
+
+/* Backward preprocess: delta[b,h,i] = sum_d O[b,h,i,d] * dO[b,h,i,d] (fp32).
+ * Replaces the _attn_bwd_preprocess launch (attention.py:731-744, kernel
+ * :237-255). */
+FA_API int fa_bwd_delta(const void* o, const void* dO, float* delta,
+                 int B, int H, int N, int D,
+                 const int64_t* o_strides, const int64_t* do_strides,
+                 void* stream);
+
+/* Backward dQ: dQ = scale * sum_j dS_ij K_j with P rebuilt from lse and
+ * dS = P (dO V^T - delta).  Replaces the dQ half of _attn_bwd
+ * (attention.py:507-573, inner loop :311-350). */
+FA_API int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO,
+              const float* lse, const float* delta, void* dq,
+              int B, int Hq, int Hkv, int Nq, int Nk, int D,
+              const int64_t* q_strides, const int64_t* k_strides,
+              const int64_t* v_strides, const int64_t* do_strides,
+              const int64_t* dq_strides,
+              float softmax_scale, int causal, int q_offset, int k_offset,
+              int accumulate_fp32, void* stream);
+
+/* Backward dK/dV: dV = sum_i P^T dO, dK = scale * sum_i dS^T Q, summed over
+ * the Hq/Hkv query heads of each K/V head inside one CTA (deterministic, no
+ * atomics).  Replaces the dK/dV half of _attn_bwd and its GQA atomics
+ * (attention.py:428-505, inner loop :258-308). */
+FA_API int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO,
+                const float* lse, const float* delta, void* dk, void* dv,
+                int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, const int64_t* do_strides,
+                const int64_t* dk_strides, const int64_t* dv_strides,
+                float softmax_scale, int causal, int q_offset, int k_offset,
+                int accumulate_fp32, void* stream);
+
+/* Merge a partial attention result into a running one (ring context
+ * parallelism): with L = log2(2^lse_acc + 2^lse_part),
+ * o_acc = o_acc 2^(lse_acc - L) + o_part 2^(lse_part - L), lse_acc = L.
+ * o_acc/o_part are (B, H, N, D) fp32/fp16 contiguous, lse (B, H, N) fp32.
+ * No counterpart in the reference (single GPU only). */
+FA_API int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part,
+                     const float* lse_part, int B, int H, int N, int D,
+                     void* stream);
+
+/* Reads (and with reset != 0 clears) the device status word that kernels set
+ * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
+ * low byte and the barrier site in bits 8..15.  Synchronises the device. */
+FA_API int fa_device_status(int reset);
+
+/* Human-readable text of an FA_ERR_* code. */
+FA_API const char* fa_status_string(int code);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+FA_API int fa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H */

@@ -1,0 +1,37 @@
+"""B200-native (sm_100a) FlashAttention-2 behind the public surface of
+AmanPandey28/triton-flash-attention (triton_flash_attention/__init__.py:3-15).
+
+The package directory is ``triton-flash-attention_b200/``; it is imported as
+``triton_flash_attention_b200`` (through the loader module of that name at
+the repository root, or an install that maps the name to this directory).
+"""
+
+from .attention import (
+    B200Attention,
+    DispatchDecision,
+    SUPPORTED_HEAD_DIMS,
+    TritonAttention,
+    attention_backward_dkdv,
+    attention_backward_dq,
+    attention_delta,
+    attention_forward,
+    explain_dispatch,
+    scaled_dot_product_attention,
+)
+from .flops import attention_flops, delta_bytes, memory_model
+
+__all__ = [
+    "B200Attention",
+    "DispatchDecision",
+    "SUPPORTED_HEAD_DIMS",
+    "TritonAttention",
+    "attention_backward_dkdv",
+    "attention_backward_dq",
+    "attention_delta",
+    "attention_flops",
+    "attention_forward",
+    "delta_bytes",
+    "explain_dispatch",
+    "memory_model",
+    "scaled_dot_product_attention",
+]

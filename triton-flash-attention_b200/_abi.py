@@ -1,0 +1,91 @@
+"""ctypes binding of the C ABI declared in ``include/fa_b200.h``.
+
+The shared library ``_lib/libfa_b200.so`` is built in-tree by ``build.py``.
+There is no fallback: if the library is missing or fails to load, every call
+raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libfa_b200.so")
+_lock = threading.Lock()
+_lib = None
+
+FA_OK = 0
+FA_ERR_UNSUPPORTED_HEAD_DIM = 1
+FA_ERR_BAD_SHAPE = 2
+FA_ERR_MISALIGNED = 3
+FA_ERR_LAUNCH = 4
+FA_ERR_TENSOR_MAP = 5
+FA_ERR_DRIVER = 6
+FA_ERR_DEVICE_TIMEOUT = 7
+FA_ERR_NO_DEVICE = 8
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_s = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes), in the order of include/fa_b200.h
+SIGNATURES = {
+    "fa_fwd": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _s, _s, _s, _s, _f, _i, _i, _i, _p]),
+    "fa_bwd_delta": (_i, [_p, _p, _p, _i, _i, _i, _i, _s, _s, _p]),
+    "fa_bwd_dq": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
+                       _s, _s, _s, _s, _s, _f, _i, _i, _i, _i, _p]),
+    "fa_bwd_dkdv": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
+                         _s, _s, _s, _s, _s, _s, _f, _i, _i, _i, _i, _p]),
+    "fa_merge_partial": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "fa_device_status": (_i, [_i]),
+    "fa_status_string": (ctypes.c_char_p, [_i]),
+    "fa_version": (_i, []),
+}
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise RuntimeError(
+                    "the B200 CUDA library is not built: expected " + _LIB_PATH
+                    + " (run `python -m triton_flash_attention_b200.build`)")
+            handle = ctypes.CDLL(_LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().fa_status_string(int(code)).decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FA_OK:
+        raise RuntimeError(f"{what} failed: {status_string(rc)} (code {rc})")
+
+
+def strides3(t) -> ctypes.Array:
+    """(batch, head, seq) element strides of a 4-D (B, H, N, D) tensor."""
+    s = t.stride()
+    if s[3] != 1:
+        raise ValueError("the head dimension must be contiguous (unit stride)")
+    return (ctypes.c_int64 * 3)(s[0], s[1], s[2])
+
+
+def device_status(reset: bool = False) -> int:
+    """The device status word (0 = healthy); synchronises the device."""
+    return int(lib().fa_device_status(1 if reset else 0))

@@ -1,0 +1,239 @@
+"""Public attention API, mirroring the reference's surface
+(triton_flash_attention/attention.py:576-845) on top of the B200 kernels.
+
+Same names, argument meaning and validation messages as the reference.  The
+one deliberate difference is dispatch: the reference falls back to
+``torch.nn.functional.scaled_dot_product_attention`` for inputs its kernel
+does not serve; this package has a single backend -- the hand-written
+sm_100a CUDA kernels -- and raises ``RuntimeError`` for every ineligible
+input instead of falling back.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from numbers import Real
+from typing import Literal
+
+import torch
+
+from . import _abi
+
+SUPPORTED_HEAD_DIMS = (32, 64, 128)
+Backend = Literal["auto", "triton", "cuda"]
+_BACKENDS = ("auto", "triton", "cuda")
+
+
+@dataclass(frozen=True)
+class DispatchDecision:
+    """The selected backend and the concrete reason for the decision
+    (attention.py:576-581).  ``backend`` is ``"cuda"`` when the B200 kernels
+    serve the inputs and ``"unsupported"`` otherwise."""
+
+    backend: Literal["cuda", "unsupported"]
+    reason: str
+
+
+def _validate_inputs(query, key, value, *, enable_gqa: bool) -> None:
+    """Shape/device/dtype checks with the reference's messages
+    (attention.py:584-626)."""
+    tensors = {"query": query, "key": key, "value": value}
+    for name, tensor in tensors.items():
+        if not isinstance(tensor, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if tensor.ndim != 4:
+            raise ValueError(
+                f"{name} must have shape (batch, heads, sequence, head_dim); "
+                f"got {tuple(tensor.shape)}")
+        if any(dimension == 0 for dimension in tensor.shape):
+            raise ValueError(f"{name} dimensions must all be greater than zero")
+    if query.device != key.device or query.device != value.device:
+        raise ValueError("query, key, and value must be on the same device")
+    if query.dtype != key.dtype or query.dtype != value.dtype:
+        raise ValueError("query, key, and value must have the same dtype")
+    if query.shape[0] != key.shape[0] or key.shape[0] != value.shape[0]:
+        raise ValueError("query, key, and value batch dimensions must match")
+    if key.shape[:3] != value.shape[:3]:
+        raise ValueError("key and value batch, head, and sequence dimensions must match")
+    if query.shape[3] != key.shape[3]:
+        raise ValueError("query and key head dimensions must match")
+    q_heads, kv_heads = query.shape[1], key.shape[1]
+    if q_heads != kv_heads and not enable_gqa:
+        raise ValueError(
+            "query has a different number of heads from key/value; pass "
+            "enable_gqa=True to use grouped-query attention")
+    if q_heads % kv_heads != 0:
+        raise ValueError(
+            "the number of query heads must be divisible by the number of "
+            "key/value heads")
+
+
+def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> DispatchDecision:
+    """Explain whether the B200 kernels can serve these inputs
+    (attention.py:629-670).  Query and key lengths may differ (the causal
+    mask is then top-left aligned, as in PyTorch's SDPA)."""
+    _validate_inputs(query, key, value, enable_gqa=enable_gqa)
+    if value.shape[3] != query.shape[3]:
+        return DispatchDecision(
+            "unsupported", "the custom kernel requires equal query/key and value head sizes")
+    if query.device.type != "cuda":
+        return DispatchDecision("unsupported", "the B200 kernel requires a CUDA tensor")
+    if torch.version.hip is not None:
+        return DispatchDecision("unsupported", "this project targets NVIDIA CUDA, not ROCm")
+    if query.dtype != torch.float16:
+        return DispatchDecision(
+            "unsupported", "the custom mixed-precision path currently supports float16")
+    if query.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        supported = ", ".join(str(dim) for dim in SUPPORTED_HEAD_DIMS)
+        return DispatchDecision(
+            "unsupported", f"head_dim must be one of ({supported}) for the B200 path")
+    major, minor = torch.cuda.get_device_capability(query.device)
+    if (major, minor) != (10, 0):
+        return DispatchDecision(
+            "unsupported", "the kernels are built for sm_100a (B200) GPUs only")
+    return DispatchDecision(
+        "cuda", "CUDA float16 attention on sm_100a with a supported head dimension")
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def attention_forward(q, k, v, causal: bool, softmax_scale: float, *, q_offset: int = 0, k_offset: int = 0):
+    """Launch the forward kernel: returns (o, lse2) with lse2 the base-2
+    log-sum-exp per query row in the scaled domain (attention.py:230)."""
+    b, hq, nq, d = q.shape
+    hkv, nk = k.shape[1], k.shape[2]
+    o = torch.empty_like(q)
+    lse = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
+    lib = _abi.lib()
+    rc = lib.fa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                    b, hq, hkv, nq, nk, d,
+                    _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(o),
+                    float(softmax_scale), 1 if causal else 0, int(q_offset), int(k_offset),
+                    _stream_handle(q.device))
+    _abi.check(rc, "fa_fwd")
+    return o, lse
+
+
+def attention_delta(o, do):
+    """Delta = rowsum(O * dO) in fp32 (attention.py:237-255)."""
+    b, h, n, d = o.shape
+    delta = torch.empty((b, h, n), device=o.device, dtype=torch.float32)
+    rc = _abi.lib().fa_bwd_delta(o.data_ptr(), do.data_ptr(), delta.data_ptr(), b, h, n, d,
+                                 _abi.strides3(o), _abi.strides3(do), _stream_handle(o.device))
+    _abi.check(rc, "fa_bwd_delta")
+    return delta
+
+
+def attention_backward_dq(q, k, v, do, lse, delta, causal: bool, softmax_scale: float, *,
+                          dq=None, q_offset: int = 0, k_offset: int = 0):
+    """dQ for one key/value block.  With ``dq`` given as an fp32 tensor the
+    result is added into it; otherwise a new fp16 tensor is returned."""
+    b, hq, nq, d = q.shape
+    hkv, nk = k.shape[1], k.shape[2]
+    acc = dq is not None
+    if acc:
+        if dq.dtype != torch.float32 or dq.shape != q.shape:
+            raise ValueError("dq accumulator must be an fp32 tensor shaped like q")
+    else:
+        dq = torch.empty_like(q)
+    rc = _abi.lib().fa_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                              lse.data_ptr(), delta.data_ptr(), dq.data_ptr(),
+                              b, hq, hkv, nq, nk, d,
+                              _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(do),
+                              _abi.strides3(dq), float(softmax_scale), 1 if causal else 0,
+                              int(q_offset), int(k_offset), 1 if acc else 0, _stream_handle(q.device))
+    _abi.check(rc, "fa_bwd_dq")
+    return dq
+
+
+def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale: float, *,
+                            dk=None, dv=None, q_offset: int = 0, k_offset: int = 0):
+    """dK, dV for one key/value block (GQA groups summed in-kernel).  With
+    ``dk``/``dv`` given as fp32 tensors the results are added into them."""
+    b, hq, nq, d = q.shape
+    hkv, nk = k.shape[1], k.shape[2]
+    acc = dk is not None or dv is not None
+    if acc:
+        if dk is None or dv is None:
+            raise ValueError("pass both dk and dv accumulators or neither")
+        for name, t in (("dk", dk), ("dv", dv)):
+            if t.dtype != torch.float32 or t.shape != k.shape:
+                raise ValueError(f"{name} accumulator must be an fp32 tensor shaped like k")
+    else:
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+    rc = _abi.lib().fa_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                lse.data_ptr(), delta.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                b, hq, hkv, nq, nk, d,
+                                _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(do),
+                                _abi.strides3(dk), _abi.strides3(dv), float(softmax_scale),
+                                1 if causal else 0, int(q_offset), int(k_offset), 1 if acc else 0,
+                                _stream_handle(q.device))
+    _abi.check(rc, "fa_bwd_dkdv")
+    return dk, dv
+
+
+class B200Attention(torch.autograd.Function):
+    """Autograd bridge for the B200 forward and backward kernels
+    (counterpart of ``TritonAttention``, attention.py:673-771).
+
+    ``apply(q, k, v, causal, softmax_scale)`` saves (q, k, v, O, LSE) with one
+    fp32 base-2 log-sum-exp per query row and returns 5 gradients."""
+
+    @staticmethod
+    def forward(ctx, query, key, value, causal, softmax_scale):
+        output, lse = attention_forward(query, key, value, bool(causal), float(softmax_scale))
+        ctx.save_for_backward(query, key, value, output, lse)
+        ctx.softmax_scale = float(softmax_scale)
+        ctx.causal = bool(causal)
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        query, key, value, output, lse = ctx.saved_tensors
+        grad_output = grad_output.contiguous()
+        delta = attention_delta(output, grad_output)
+        grad_query = attention_backward_dq(query, key, value, grad_output, lse, delta,
+                                           ctx.causal, ctx.softmax_scale)
+        grad_key, grad_value = attention_backward_dkdv(query, key, value, grad_output, lse, delta,
+                                                       ctx.causal, ctx.softmax_scale)
+        return grad_query, grad_key, grad_value, None, None
+
+
+# The reference's name for the autograd Function (attention.py:673).
+TritonAttention = B200Attention
+
+
+def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, scale: float | None = None,
+                                 enable_gqa: bool = False, backend: Backend = "auto") -> torch.Tensor:
+    """Scaled dot-product attention on the B200 kernels (attention.py:789-845).
+
+    Forward and backward, causal and bidirectional attention, arbitrary
+    positive sequence lengths, GQA.  ``backend`` is kept for drop-in
+    compatibility: ``"auto"``, ``"triton"`` (the reference's name for its
+    custom kernel) and ``"cuda"`` all select the B200 kernels.  Inputs they
+    cannot serve raise ``RuntimeError`` -- there is no PyTorch fallback."""
+    if backend == "torch":
+        raise RuntimeError(
+            "backend='torch' (the PyTorch SDPA fallback) is not part of this package; "
+            "call torch.nn.functional.scaled_dot_product_attention directly")
+    if backend not in _BACKENDS:
+        raise ValueError("backend must be one of: 'auto', 'triton', 'cuda'")
+    if not isinstance(is_causal, bool):
+        raise TypeError("is_causal must be a bool")
+    if not isinstance(enable_gqa, bool):
+        raise TypeError("enable_gqa must be a bool")
+    if scale is not None and (not isinstance(scale, Real) or not math.isfinite(float(scale))):
+        raise ValueError("scale must be a finite real number or None")
+    _validate_inputs(query, key, value, enable_gqa=enable_gqa)
+    decision = explain_dispatch(query, key, value, enable_gqa=enable_gqa)
+    if decision.backend != "cuda":
+        raise RuntimeError(f"B200 CUDA backend is unavailable: {decision.reason}")
+    query_c = query.contiguous()
+    key_c = key.contiguous()
+    value_c = value.contiguous()
+    softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
+    return B200Attention.apply(query_c, key_c, value_c, is_causal, softmax_scale)

@@ -1,0 +1,158 @@
+// fa_bwd_aux.cu -- the HBM-bound helpers of the attention path.
+//
+//  * fa_delta_kernel: Delta_i = sum_d O_id * dO_id in fp32, the backward
+//    preprocess of the reference (triton_flash_attention/attention.py:237-255).
+//    Each row is read once with 16-byte loads, D/8 lanes per row, and reduced
+//    with warp shuffles; a grid-stride loop sized to the SM count keeps every
+//    SM streaming.
+//  * fa_merge_kernel: the log-sum-exp merge of ring context parallelism
+//    (no counterpart in the reference).
+#include "fa_kernels.h"
+
+namespace fa {
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float dot8_h(uint4 a, uint4 b) {
+  const __half2* ha = reinterpret_cast<const __half2*>(&a);
+  const __half2* hb = reinterpret_cast<const __half2*>(&b);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 fa = __half22float2(ha[i]);
+    const float2 fb = __half22float2(hb[i]);
+    acc = fmaf(fa.x, fb.x, acc);
+    acc = fmaf(fa.y, fb.y, acc);
+  }
+  return acc;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) fa_delta_kernel(const __half* __restrict__ o, long long o_sb, long long o_sh,
+                                                       long long o_sn, const __half* __restrict__ dO, long long do_sb,
+                                                       long long do_sh, long long do_sn, float* __restrict__ delta,
+                                                       int H, int N, long long rows) {
+  constexpr int TPR = D / 8;  // lanes per row, 8 fp16 each
+  const long long total = rows * TPR;
+  const long long nthreads = (long long)gridDim.x * blockDim.x;
+  for (long long base = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total;
+       base += nthreads) {
+    const long long idx = base + (threadIdx.x & 31);
+    const bool valid = idx < total;
+    float acc = 0.f;
+    long long row = 0;
+    int part = 0;
+    if (valid) {
+      row = idx / TPR;
+      part = int(idx % TPR);
+      const int n = int(row % N);
+      const long long bh = row / N;
+      const int h = int(bh % H);
+      const long long b = bh / H;
+      const __half* po = o + b * o_sb + h * o_sh + n * o_sn + part * 8;
+      const __half* pd = dO + b * do_sb + h * do_sh + n * do_sn + part * 8;
+      acc = dot8_h(ld_nc_v4(po), ld_nc_v4(pd));
+    }
+#pragma unroll
+    for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (valid && part == 0) delta[row] = acc;
+  }
+}
+
+int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long o_sn, const __half* dO,
+                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
+                     cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long rows = (long long)B * H * N;
+  const long long work = rows * (D / 8);
+  long long blocks = (work + 255) / 256;
+  const long long cap = (long long)sms * 8;  // 8 x 256 threads resident per SM
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  switch (D) {
+    case 32:
+      fa_delta_kernel<32><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                 delta, H, N, rows);
+      break;
+    case 64:
+      fa_delta_kernel<64><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                 delta, H, N, rows);
+      break;
+    case 128:
+      fa_delta_kernel<128><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                  delta, H, N, rows);
+      break;
+    default:
+      return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+// o_acc (rows x D fp32), lse_acc (rows) <- merge with o_part (fp16), lse_part.
+__global__ void __launch_bounds__(256) fa_merge_kernel(float* __restrict__ o_acc, float* __restrict__ lse_acc,
+                                                       const __half* __restrict__ o_part,
+                                                       const float* __restrict__ lse_part, long long rows, int D) {
+  const int vec_per_row = D / 8;
+  const long long total = rows * vec_per_row;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long row = idx / vec_per_row;
+    const int part = int(idx % vec_per_row);
+    const float a = lse_acc[row];
+    const float bq = lse_part[row];
+    const float mx = fmaxf(a, bq);
+    float wa = 0.f, wb = 0.f, L = -INFINITY;
+    if (mx != -INFINITY) {
+      const float ea = exp2f(a - mx), eb = exp2f(bq - mx);
+      const float tot = ea + eb;
+      L = mx + log2f(tot);
+      wa = ea / tot;
+      wb = eb / tot;
+    }
+    float* po = o_acc + row * D + part * 8;
+    const uint4 pk = *reinterpret_cast<const uint4*>(o_part + row * D + part * 8);
+    const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
+    float4 x0 = reinterpret_cast<float4*>(po)[0];
+    float4 x1 = reinterpret_cast<float4*>(po)[1];
+    const float2 p0 = __half22float2(h2[0]), p1 = __half22float2(h2[1]);
+    const float2 p2 = __half22float2(h2[2]), p3 = __half22float2(h2[3]);
+    x0.x = x0.x * wa + p0.x * wb;
+    x0.y = x0.y * wa + p0.y * wb;
+    x0.z = x0.z * wa + p1.x * wb;
+    x0.w = x0.w * wa + p1.y * wb;
+    x1.x = x1.x * wa + p2.x * wb;
+    x1.y = x1.y * wa + p2.y * wb;
+    x1.z = x1.z * wa + p3.x * wb;
+    x1.w = x1.w * wa + p3.y * wb;
+    reinterpret_cast<float4*>(po)[0] = x0;
+    reinterpret_cast<float4*>(po)[1] = x1;
+    // Every lane of the row read lse_acc[row] before this point in its own
+    // iteration; the part-0 lane alone rewrites it after all lanes of the row
+    // (same warp, consecutive lanes) have used the old value.
+    __syncwarp(__activemask());
+    if (part == 0) lse_acc[row] = L;
+  }
+}
+
+int launch_merge_partial(float* o_acc, float* lse_acc, const __half* o_part, const float* lse_part, long long rows,
+                         int D, cudaStream_t stream) {
+  if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  long long blocks = (rows * (D / 8) + 255) / 256;
+  if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
+  if (blocks < 1) blocks = 1;
+  fa_merge_kernel<<<unsigned(blocks), 256, 0, stream>>>(o_acc, lse_acc, o_part, lse_part, rows, D);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace fa

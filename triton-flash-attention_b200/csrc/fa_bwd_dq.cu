@@ -1,0 +1,354 @@
+// fa_bwd_dq.cu -- FlashAttention-2 backward, dQ half, for B200 (sm_100a).
+//
+// Computes what the dQ half of the reference's _attn_bwd produces
+// (triton_flash_attention/attention.py:507-573, inner loop :311-350):
+//   P = exp2(scale*log2(e) * Q K^T - lse2),  dP = dO V^T,
+//   dS = P (dP - Delta),  dQ = scale * dS K.
+// Layout of the work:
+//  * one CTA owns 2 query tiles of 128 rows of one (batch, head) and sweeps
+//    the key tiles (64 keys each) that are visible to them;
+//  * warp 0 streams K/V tiles through shared-memory stages with TMA;
+//  * warp 1 (one thread) issues tcgen05.mma: S_t = Q_t K^T and dP_t = dO_t V^T
+//    into TMEM, then dQ_t += dS_t K with dS_t read from TMEM (fp16, aliasing
+//    S_t) and K read as an MN-major operand of the same shared tile;
+//  * warps 4-7 / 8-11 turn S_t, dP_t into dS_t, one thread per query row,
+//    with that row's lse2 and Delta held in registers;
+//  * the two query tiles ping-pong between the tensor core and the warps.
+// TMEM: S_t at cols [128t, 128t+64), dP_t at [128t+64, 128t+128),
+//       dQ_t at [256 + t*D, 256 + (t+1)*D).
+#include "fa_common.cuh"
+#include "fa_kernels.h"
+
+namespace fa {
+
+namespace bdq {
+
+constexpr int BM = dq_cfg::BM;  // query rows per tile
+constexpr int BN = dq_cfg::BN;  // keys per tile
+constexpr int QT = 2;
+constexpr int NUM_THREADS = 384;
+
+template <int D>
+struct Cfg {
+  using G = TileGeom<D>;
+  static constexpr int NST = D == 128 ? 2 : 4;
+  static constexpr int Q_TILE_BYTES = BM * D * 2;
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + QT * Q_TILE_BYTES;
+  static constexpr int OFF_K = OFF_DO + QT * Q_TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
+  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
+  // s_full[QT], ds_ready[QT], dq_full[QT], mma_done
+  static constexpr int NUM_BARS = 1 + 4 * NST + 3 * QT + 1;
+  static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_MISC = OFF_CTL + 16;
+  static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DQ_COL0 = 256;
+  static_assert(DQ_COL0 + QT * D <= TMEM_COLS, "TMEM budget");
+};
+
+}  // namespace bdq
+
+template <int D>
+__global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
+    fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                     const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                     const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
+                     void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh, const long long dq_sn,
+                     const int accumulate_fp32) {
+  using namespace bdq;
+  using C = Cfg<D>;
+  using G = TileGeom<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_saddr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
+  const uint32_t sbase = smem_u32(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + C::NST;
+  uint64_t* v_full = k_empty + C::NST;
+  uint64_t* v_empty = v_full + C::NST;
+  uint64_t* s_full = v_empty + C::NST;
+  uint64_t* ds_ready = s_full + QT;
+  uint64_t* dq_full = ds_ready + QT;
+  uint64_t* mma_done = dq_full + QT;
+  CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
+  volatile CtaCtl* ctl = ctl_w;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+
+  const int warp = int(warp_id());
+  const int lane = int(lane_id());
+
+  const int BH = shp.B * shp.Hq;
+  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
+  const int qblk = n_qblk - 1 - int(blockIdx.x) / BH;
+  const int bh = int(blockIdx.x) % BH;
+  const int b = bh / shp.Hq;
+  const int h = bh % shp.Hq;
+  const int kvh = h / (shp.Hq / shp.Hkv);
+  const int row0 = qblk * QT * BM;
+  int n_kv[QT];
+#pragma unroll
+  for (int t = 0; t < QT; ++t) n_kv[t] = kv_tiles_for_rows(shp, row0 + t * BM, BM, BN);
+  const int n_max = n_kv[0] > n_kv[1] ? n_kv[0] : n_kv[1];
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
+    }
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(ds_ready + t, 128);
+      mbar_init(dq_full + t, 1);
+    }
+    mbar_init(mma_done, 1);
+    ctl_w->abort = 0;
+    ctl_w->status = shp.status;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =================== TMA producer ===================
+    if (lane == 0 && n_max > 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_do);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      int q_bytes = 0;
+      for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? 2 * C::Q_TILE_BYTES : 0;
+      mbar_arrive_expect_tx(q_full, q_bytes);
+      for (int t = 0; t < QT; ++t) {
+        if (n_kv[t] == 0) continue;
+        for (int bx = 0; bx < G::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q, q_full, bx * G::BOX,
+                      row0 + t * BM, h, b);
+          tma_load_4d(smem + C::OFF_DO + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_do, q_full, bx * G::BOX,
+                      row0 + t * BM, h, b);
+        }
+      }
+      int nk_iss = 0, nv_iss = 0;
+      for (int j = 0; j < n_max; ++j) {
+        const int s = j % C::NST;
+        const uint32_t u = uint32_t(j / C::NST);
+        if (u > 0 && !mbar_wait(k_empty + s, (u - 1) & 1, ctl, 31)) break;
+        mbar_arrive_expect_tx(k_full + s, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + C::OFF_K + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_k, k_full + s, bx * G::BOX,
+                      j * BN, kvh, b);
+        ++nk_iss;
+        if (u > 0 && !mbar_wait(v_empty + s, (u - 1) & 1, ctl, 32)) break;
+        mbar_arrive_expect_tx(v_full + s, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + C::OFF_V + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_v, v_full + s, bx * G::BOX,
+                      j * BN, kvh, b);
+        ++nv_iss;
+      }
+      mbar_wait_drain(q_full, 0, ctl, 33);
+      for (int j = (nk_iss > C::NST ? nk_iss - C::NST : 0); j < nk_iss; ++j)
+        mbar_wait_drain(k_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 34);
+      for (int j = (nv_iss > C::NST ? nv_iss - C::NST : 0); j < nv_iss; ++j)
+        mbar_wait_drain(v_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 35);
+    }
+  } else if (warp == 1) {
+    // =================== tcgen05 MMA issuer ===================
+    if (lane == 0 && n_max > 0) {
+      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
+      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1);
+      const uint32_t q_s = sbase + C::OFF_Q;
+      const uint32_t do_s = sbase + C::OFF_DO;
+      const uint32_t k_s = sbase + C::OFF_K;
+      const uint32_t v_s = sbase + C::OFF_V;
+      auto issue_sdp = [&](int t, int j) {
+        const uint32_t qa = q_s + t * C::Q_TILE_BYTES;
+        const uint32_t da = do_s + t * C::Q_TILE_BYTES;
+        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
+        const uint32_t vb = v_s + (j % C::NST) * C::KV_TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + t * 128, desc_k_major<D, BM>(qa, ks), desc_k_major<D, BN>(kb, ks), IDESC_S, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + t * 128 + 64, desc_k_major<D, BM>(da, ks), desc_k_major<D, BN>(vb, ks), IDESC_S, ks > 0);
+        umma_commit(s_full + t);
+      };
+      auto issue_dq = [&](int t, int j) {
+        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_ts(tmem + C::DQ_COL0 + t * D, tmem + t * 128 + ks * 8, desc_mn_major<D, BN>(kb, ks), IDESC_DQ,
+                  (j > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, ctl, 40) && mbar_wait(k_full, 0, ctl, 41) && mbar_wait(v_full, 0, ctl, 42);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < QT; ++t)
+          if (n_kv[t] > 0) issue_sdp(t, 0);
+        umma_commit(v_empty);
+      }
+      for (int j = 0; j < n_max && ok; ++j) {
+        const bool more = j + 1 < n_max;
+        if (more) {
+          const int s1 = (j + 1) % C::NST;
+          const uint32_t par = uint32_t((j + 1) / C::NST) & 1;
+          if (!mbar_wait(k_full + s1, par, ctl, 43) || !mbar_wait(v_full + s1, par, ctl, 44)) { ok = false; break; }
+        }
+        tc_fence_after();
+        for (int t = 0; t < QT && ok; ++t) {
+          if (j >= n_kv[t]) continue;
+          if (!mbar_wait(ds_ready + t, uint32_t(j) & 1, ctl, 45)) { ok = false; break; }
+          tc_fence_after();
+          issue_dq(t, j);
+          if (j + 1 < n_kv[t]) issue_sdp(t, j + 1);
+        }
+        if (!ok) break;
+        umma_commit(k_empty + j % C::NST);
+        if (more) umma_commit(v_empty + (j + 1) % C::NST);
+      }
+      if (ok) {
+        for (int t = 0; t < QT; ++t)
+          if (n_kv[t] > 0) umma_commit(dq_full + t);
+      }
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, ctl, 46);
+    }
+  } else if (warp >= 4) {
+    // =================== dS warpgroups ===================
+    const int t = (warp - 4) / 4;
+    const int wq = warp & 3;
+    const int r = row0 + t * BM + wq * 32 + lane;
+    const int nt = n_kv[t];
+    int lim = shp.Nk - 1;
+    if (shp.causal) {
+      const long long c = (long long)r + shp.q_off - shp.k_off;
+      lim = c < lim ? int(c) : lim;
+    }
+    const bool row_ok = r < shp.Nq;
+    float lse_r = INFINITY, delta_r = 0.f;
+    if (row_ok) {
+      const float x = lse[(long long)bh * shp.Nq + r];
+      lse_r = x == -INFINITY ? INFINITY : x;  // no visible key: every P is 0
+      delta_r = delta[(long long)bh * shp.Nq + r];
+    }
+    const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(t * 128));
+    const uint32_t tQ = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::DQ_COL0 + t * D));
+    const float c2 = shp.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!mbar_wait_warp(s_full + t, uint32_t(j) & 1, ctl, 50 + t)) { ok = false; break; }
+      tc_fence_after();
+      float s[BN], dp[BN];
+      tmem_ld64(tS, s);
+      tmem_ld64(tS + 64, dp);
+      const int lim_j = lim - j * BN;
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c0 = cc * 32 + 2 * i;
+          float p0 = ex2(fmaf(s[c0], c2, -lse_r));
+          float p1 = ex2(fmaf(s[c0 + 1], c2, -lse_r));
+          p0 = c0 <= lim_j ? p0 : 0.f;
+          p1 = c0 + 1 <= lim_j ? p1 : 0.f;
+          packed[i] = pack_half2(p0 * (dp[c0] - delta_r), p1 * (dp[c0 + 1] - delta_r));
+        }
+        tmem_st16(tS + cc * 16, packed);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(ds_ready + t);
+    }
+    if (ok && nt > 0) ok = mbar_wait_warp(dq_full + t, 0, ctl, 52 + t);
+    if (ok && row_ok) {
+      if (nt > 0) tc_fence_after();
+    }
+    if (ok) {
+      const float sc = shp.scale;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float g[32];
+        if (nt > 0) {
+          tmem_ld32(tQ + cc * 32, g);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g[i] = 0.f;
+        }
+        if (!row_ok) continue;
+        const long long off = (long long)b * dq_sb + (long long)h * dq_sh + (long long)r * dq_sn + cc * 32;
+        if (accumulate_fp32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 x = dst[v4];
+            x.x += g[v4 * 4 + 0] * sc;
+            x.y += g[v4 * 4 + 1] * sc;
+            x.z += g[v4 * 4 + 2] * sc;
+            x.w += g[v4 * 4 + 3] * sc;
+            dst[v4] = x;
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(dq_out) + off);
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
+            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
+            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
+            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            dst[v8] = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch_bwd_dq_t(const BwdArgs& a) {
+  using C = bdq::Cfg<D>;
+  auto kern = fa_bwd_dq_kernel<D>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  const int n_qblk = (a.shape.Nq + bdq::QT * bdq::BM - 1) / (bdq::QT * bdq::BM);
+  dim3 grid(unsigned(n_qblk * a.shape.B * a.shape.Hq));
+  kern<<<grid, bdq::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse,
+                                                            a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
+                                                            a.accumulate_fp32);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int launch_bwd_dq(const BwdArgs& a, int D) {
+  switch (D) {
+    case 32: return launch_bwd_dq_t<32>(a);
+    case 64: return launch_bwd_dq_t<64>(a);
+    case 128: return launch_bwd_dq_t<128>(a);
+    default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+}
+
+}  // namespace fa

@@ -1,0 +1,245 @@
+// fa_capi.cu -- the extern "C" boundary (include/fa_b200.h): argument
+// validation, TMA descriptor encoding and kernel dispatch.  No exceptions and
+// no torch types cross it; every entry point returns an FA_ERR_* code.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "fa_kernels.h"
+
+namespace fa {
+namespace {
+
+__device__ int g_device_status;  // one word per device (each device loads its own copy)
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Device address of this device's status word (looked up once per device).
+int* status_ptr() {
+  static int* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool supported_d(int D) { return D == 32 || D == 64 || D == 128; }
+
+// 4-D fp16 tensor map over (B, H, N, D) with element strides {sb, sh, sn, 1}.
+// The box is {min(D, 64), rows, 1, 1} with the swizzle the kernels' shared
+// memory descriptors assume (128 B for D >= 64, 64 B for D = 32).
+int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, const int64_t* strides, int rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return FA_ERR_DRIVER;
+  if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] <= 0 || (strides[i] * 2) % 16 != 0) return FA_ERR_MISALIGNED;
+  const int box_d = D >= 64 ? 64 : 32;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t gstr[3] = {cuuint64_t(strides[2]) * 2, cuuint64_t(strides[1]) * 2, cuuint64_t(strides[0]) * 2};
+  cuuint32_t box[4] = {cuuint32_t(box_d), cuuint32_t(rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TENSOR_MAP;
+}
+
+int check_shape(int B, int Hq, int Hkv, int Nq, int Nk, int D) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Nq <= 0 || Nk <= 0) return FA_ERR_BAD_SHAPE;
+  if (Hq % Hkv != 0) return FA_ERR_BAD_SHAPE;
+  return FA_OK;
+}
+
+bool out_strides_ok(const void* p, const int64_t* s, int elem_bytes) {
+  if (!aligned16(p)) return false;
+  for (int i = 0; i < 3; ++i)
+    if (s[i] <= 0 || (s[i] * elem_bytes) % 16 != 0) return false;
+  return true;
+}
+
+AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int causal, int q_off, int k_off) {
+  AttnShape s;
+  s.B = B;
+  s.Hq = Hq;
+  s.Hkv = Hkv;
+  s.Nq = Nq;
+  s.Nk = Nk;
+  s.q_off = q_off;
+  s.k_off = k_off;
+  s.causal = causal ? 1 : 0;
+  s.scale = scale;
+  s.scale_log2 = float(double(scale) * 1.4426950408889634);
+  s.status = status_ptr();
+  return s;
+}
+
+}  // namespace
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                      int Nq, int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
+                      int q_offset, int k_offset, void* stream) {
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides || !o_strides) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
+  FwdArgs a;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, 128))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, 128))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, 128))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
+  a.o = static_cast<__half*>(o);
+  a.o_sb = o_strides[0];
+  a.o_sh = o_strides[1];
+  a.o_sn = o_strides[2];
+  a.lse = lse;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_fwd(a, D);
+}
+
+extern "C" int fa_bwd_delta(const void* o, const void* dO, float* delta, int B, int H, int N, int D,
+                            const int64_t* o_strides, const int64_t* do_strides, void* stream) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
+  if (!o || !dO || !delta || !o_strides || !do_strides) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2)) return FA_ERR_MISALIGNED;
+  return launch_bwd_delta(static_cast<const __half*>(o), o_strides[0], o_strides[1], o_strides[2],
+                          static_cast<const __half*>(dO), do_strides[0], do_strides[1], do_strides[2], delta, B, H,
+                          N, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                         const float* delta, void* dq, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                         const int64_t* do_strides, const int64_t* dq_strides, float softmax_scale, int causal,
+                         int q_offset, int k_offset, int accumulate_fp32, void* stream) {
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !dO || !lse || !delta || !dq) return FA_ERR_BAD_SHAPE;
+  if (!q_strides || !k_strides || !v_strides || !do_strides || !dq_strides) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(dq, dq_strides, accumulate_fp32 ? 4 : 2)) return FA_ERR_MISALIGNED;
+  BwdArgs a;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dq_cfg::BM))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dq_cfg::BM))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dq_cfg::BN))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dq_cfg::BN))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
+  a.lse = lse;
+  a.delta = delta;
+  a.dq = dq;
+  a.dq_sb = dq_strides[0];
+  a.dq_sh = dq_strides[1];
+  a.dq_sn = dq_strides[2];
+  a.dk = a.dv = nullptr;
+  a.dk_sb = a.dk_sh = a.dk_sn = a.dv_sb = a.dv_sh = a.dv_sn = 0;
+  a.accumulate_fp32 = accumulate_fp32 ? 1 : 0;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_bwd_dq(a, D);
+}
+
+extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                           const float* delta, void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                           const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                           const int64_t* do_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                           float softmax_scale, int causal, int q_offset, int k_offset, int accumulate_fp32,
+                           void* stream) {
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !dO || !lse || !delta || !dk || !dv) return FA_ERR_BAD_SHAPE;
+  if (!q_strides || !k_strides || !v_strides || !do_strides || !dk_strides || !dv_strides) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const int eb = accumulate_fp32 ? 4 : 2;
+  if (!out_strides_ok(dk, dk_strides, eb) || !out_strides_ok(dv, dv_strides, eb)) return FA_ERR_MISALIGNED;
+  BwdArgs a;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dkdv_cfg::BQ))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dkdv_cfg::BQ))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
+  a.lse = lse;
+  a.delta = delta;
+  a.dq = nullptr;
+  a.dq_sb = a.dq_sh = a.dq_sn = 0;
+  a.dk = dk;
+  a.dv = dv;
+  a.dk_sb = dk_strides[0];
+  a.dk_sh = dk_strides[1];
+  a.dk_sn = dk_strides[2];
+  a.dv_sb = dv_strides[0];
+  a.dv_sh = dv_strides[1];
+  a.dv_sn = dv_strides[2];
+  a.accumulate_fp32 = accumulate_fp32 ? 1 : 0;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_bwd_dkdv(a, D);
+}
+
+extern "C" int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B,
+                                int H, int N, int D, void* stream) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
+  if (!o_acc || !lse_acc || !o_part || !lse_part) return FA_ERR_BAD_SHAPE;
+  if (!aligned16(o_acc) || !aligned16(o_part)) return FA_ERR_MISALIGNED;
+  return launch_merge_partial(o_acc, lse_acc, static_cast<const __half*>(o_part), lse_part,
+                              (long long)B * H * N, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_device_status(int reset) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return FA_ERR_LAUNCH;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return FA_ERR_LAUNCH;
+  }
+  return v;
+}
+
+extern "C" const char* fa_status_string(int code) {
+  switch (code & 0xff) {
+    case FA_OK: return "ok";
+    case FA_ERR_UNSUPPORTED_HEAD_DIM: return "head_dim must be one of (32, 64, 128)";
+    case FA_ERR_BAD_SHAPE: return "invalid shape, pointer or scale";
+    case FA_ERR_MISALIGNED: return "pointer or stride is not 16-byte aligned (TMA requirement)";
+    case FA_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case FA_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled rejected a tensor map";
+    case FA_ERR_DRIVER: return "CUDA driver entry point cuTensorMapEncodeTiled unavailable";
+    case FA_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out on the device";
+    case FA_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    default: return "unknown error";
+  }
+}
+
+extern "C" int fa_version(void) { return 100; }

@@ -1,0 +1,64 @@
+// fa_common.cuh -- shared geometry and parameter blocks of the attention
+// kernels.
+#pragma once
+
+#include "sm100_ptx.cuh"
+
+namespace fa {
+
+// Geometry of an (R x D) fp16 tile as a TMA load with swizzle leaves it in
+// shared memory: D is cut into boxes of BOX elements (one swizzle row of SW
+// bytes each); box b holds rows 0..R-1 of columns [b*BOX, (b+1)*BOX) and sits
+// R*SW bytes after box b-1.
+template <int D>
+struct TileGeom {
+  static constexpr int SW = D >= 64 ? 128 : 64;  // swizzle width in bytes
+  static constexpr int BOX = SW / 2;             // fp16 elements per box row
+  static constexpr int NBOX = D / BOX;
+  static_assert(D == 32 || D == 64 || D == 128, "head dim");
+};
+
+// Descriptor of the 16-wide K slice `ks` of a K-major operand tile (rows are
+// the M or N index, D is the reduction index).
+template <int D, int R>
+__device__ __forceinline__ uint64_t desc_k_major(uint32_t tile_saddr, int ks) {
+  using G = TileGeom<D>;
+  const uint32_t e = uint32_t(ks) * 16u;
+  const uint32_t addr = tile_saddr + (e / G::BOX) * uint32_t(R * G::SW) + (e % G::BOX) * 2u;
+  return smem_desc<G::SW>(addr, 16u, 8u * G::SW);
+}
+
+// Descriptor of rows [16*ks, 16*ks+16) of an MN-major operand tile: the tile's
+// rows are the reduction index and its D columns the N index.
+template <int D, int R>
+__device__ __forceinline__ uint64_t desc_mn_major(uint32_t tile_saddr, int ks) {
+  using G = TileGeom<D>;
+  const uint32_t addr = tile_saddr + uint32_t(ks) * 16u * G::SW;
+  return smem_desc<G::SW>(addr, uint32_t(R * G::SW), 8u * G::SW);
+}
+
+// Problem description shared by the attention kernels (element strides).
+struct AttnShape {
+  int B, Hq, Hkv, Nq, Nk;
+  int q_off, k_off;  // global positions of query row 0 and key row 0
+  int causal;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  int* status;       // device status word (see CtaCtl)
+};
+
+// Number of K/V tiles of width BN a block of query rows [r0, r0 + rows)
+// touches; 0 when every key is masked for all of them.
+__device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, int r0, int rows, int BN) {
+  if (r0 >= s.Nq) return 0;
+  int last = s.Nk - 1;
+  if (s.causal) {
+    const int last_row = (r0 + rows < s.Nq ? r0 + rows : s.Nq) - 1;
+    const long long lim = (long long)last_row + s.q_off - s.k_off;
+    if (lim < 0) return 0;
+    if (lim < last) last = int(lim);
+  }
+  return last / BN + 1;
+}
+
+}  // namespace fa

@@ -1,0 +1,381 @@
+// fa_fwd.cu -- FlashAttention-2 forward for B200 (sm_100a).
+//
+// Same result as the reference's _attn_fwd (triton_flash_attention/
+// attention.py:90-234): O = softmax(scale * Q K^T [+ causal]) V and the base-2
+// log-sum-exp lse2 = m + log2(l) per query row (attention.py:230).  The
+// design is Blackwell-native rather than a translation:
+//
+//  * one CTA owns 2 query tiles of 128 rows (256 rows) of one (batch, head);
+//  * warp 0 streams K/V tiles of 128 keys through a ring of shared-memory
+//    stages with TMA (128- or 64-byte swizzle);
+//  * warp 1 (one thread) issues tcgen05.mma: S_t = Q_t K^T into TMEM, then
+//    O_t += P_t V with P_t read straight from TMEM (fp16, aliasing S_t);
+//  * warps 4-7 and 8-11 are the softmax warpgroups of tile 0 and tile 1, one
+//    thread per query row: they read S from TMEM, run the online softmax in
+//    the base-2 domain (exp2 with scale * log2(e) folded in, as
+//    attention.py:68-74), write P back to TMEM and rescale O in TMEM when the
+//    running maximum grows by more than 2^8 (lazy rescaling);
+//  * the two tiles ping-pong: while one warpgroup turns S into P, the tensor
+//    core runs the other tile's GEMMs.
+// TMEM: S_0 cols [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [256+D,256+2D).
+#include "fa_common.cuh"
+#include "fa_kernels.h"
+
+namespace fa {
+
+namespace fwd {
+
+constexpr int BM = 128;  // query rows per tile
+constexpr int BN = 128;  // keys per K/V tile
+constexpr int QT = 2;    // query tiles per CTA
+constexpr int NUM_THREADS = 384;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
+
+template <int D>
+struct Cfg {
+  using G = TileGeom<D>;
+  static constexpr int NST = D == 128 ? 2 : 3;
+  static constexpr int Q_TILE_BYTES = BM * D * 2;
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + QT * Q_TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
+  // barriers: q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
+  //           s_full[QT], p_ready[QT], o_full[QT], mma_done
+  static constexpr int NUM_BARS = 1 + 4 * NST + 3 * QT + 1;
+  static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_MISC = OFF_CTL + 16;
+  // + alignment slack; at least 116 KB so that one CTA (and its 512 TMEM
+  // columns) owns each SM
+  static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int S_COL0 = 0;
+  static constexpr int O_COL0 = QT * BN;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(O_COL0 + QT * D <= TMEM_COLS, "TMEM budget");
+};
+
+struct Smem {
+  uint64_t* q_full;
+  uint64_t* k_full;
+  uint64_t* k_empty;
+  uint64_t* v_full;
+  uint64_t* v_empty;
+  uint64_t* s_full;
+  uint64_t* p_ready;
+  uint64_t* o_full;
+  uint64_t* mma_done;
+  uint32_t* tmem_base;
+  CtaCtl* ctl;
+};
+
+}  // namespace fwd
+
+template <int D>
+__global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                  const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, __half* __restrict__ o_ptr,
+                  const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr) {
+  using namespace fwd;
+  using C = Cfg<D>;
+  using G = TileGeom<D>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled TMA destinations.
+  const uint32_t raw_saddr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
+  const uint32_t sbase = smem_u32(smem);
+
+  Smem sm;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  sm.q_full = bars;
+  sm.k_full = bars + 1;
+  sm.k_empty = sm.k_full + C::NST;
+  sm.v_full = sm.k_empty + C::NST;
+  sm.v_empty = sm.v_full + C::NST;
+  sm.s_full = sm.v_empty + C::NST;
+  sm.p_ready = sm.s_full + QT;
+  sm.o_full = sm.p_ready + QT;
+  sm.mma_done = sm.o_full + QT;
+  sm.tmem_base = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  sm.ctl = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
+  volatile CtaCtl* ctl = sm.ctl;
+
+  const int warp = int(warp_id());
+  const int lane = int(lane_id());
+
+  // ---- work item: heavy (late, causal) query blocks first ----
+  const int BH = shp.B * shp.Hq;
+  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
+  const int qblk = n_qblk - 1 - int(blockIdx.x) / BH;
+  const int bh = int(blockIdx.x) % BH;
+  const int b = bh / shp.Hq;
+  const int h = bh % shp.Hq;
+  const int kvh = h / (shp.Hq / shp.Hkv);
+  const int row0 = qblk * QT * BM;
+  int n_kv[QT];
+#pragma unroll
+  for (int t = 0; t < QT; ++t) n_kv[t] = kv_tiles_for_rows(shp, row0 + t * BM, BM, BN);
+  const int n_max = n_kv[0] > n_kv[1] ? n_kv[0] : n_kv[1];
+
+  if (threadIdx.x == 0) {
+    mbar_init(sm.q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(sm.k_full + s, 1);
+      mbar_init(sm.k_empty + s, 1);
+      mbar_init(sm.v_full + s, 1);
+      mbar_init(sm.v_empty + s, 1);
+    }
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(sm.s_full + t, 1);
+      mbar_init(sm.p_ready + t, 128);
+      mbar_init(sm.o_full + t, 1);
+    }
+    mbar_init(sm.mma_done, 1);
+    sm.ctl->abort = 0;
+    sm.ctl->status = shp.status;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(sm.tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sm.tmem_base;
+
+  if (warp == 0) {
+    // =================== TMA producer ===================
+    if (lane == 0 && n_max > 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      int q_bytes = 0;
+      for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? C::Q_TILE_BYTES : 0;
+      mbar_arrive_expect_tx(sm.q_full, q_bytes);
+      for (int t = 0; t < QT; ++t) {
+        if (n_kv[t] == 0) continue;
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q, sm.q_full, bx * G::BOX,
+                      row0 + t * BM, h, b);
+      }
+      int nk_iss = 0, nv_iss = 0;
+      for (int j = 0; j < n_max; ++j) {
+        const int s = j % C::NST;
+        const uint32_t u = uint32_t(j / C::NST);
+        if (u > 0 && !mbar_wait(sm.k_empty + s, (u - 1) & 1, ctl, 1)) break;
+        mbar_arrive_expect_tx(sm.k_full + s, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + C::OFF_K + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_k, sm.k_full + s,
+                      bx * G::BOX, j * BN, kvh, b);
+        ++nk_iss;
+        if (u > 0 && !mbar_wait(sm.v_empty + s, (u - 1) & 1, ctl, 2)) break;
+        mbar_arrive_expect_tx(sm.v_full + s, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + C::OFF_V + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_v, sm.v_full + s,
+                      bx * G::BOX, j * BN, kvh, b);
+        ++nv_iss;
+      }
+      // Drain: every load this thread issued must land before the CTA exits.
+      // On the normal path these phases have completed already.
+      mbar_wait_drain(sm.q_full, 0, ctl, 3);
+      for (int j = (nk_iss > C::NST ? nk_iss - C::NST : 0); j < nk_iss; ++j)
+        mbar_wait_drain(sm.k_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 4);
+      for (int j = (nv_iss > C::NST ? nv_iss - C::NST : 0); j < nv_iss; ++j)
+        mbar_wait_drain(sm.v_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 5);
+    }
+  } else if (warp == 1) {
+    // =================== tcgen05 MMA issuer ===================
+    if (lane == 0 && n_max > 0) {
+      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, D, 0, 1);
+      const uint32_t q_s = sbase + C::OFF_Q;
+      const uint32_t k_s = sbase + C::OFF_K;
+      const uint32_t v_s = sbase + C::OFF_V;
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qa = q_s + t * C::Q_TILE_BYTES;
+        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + C::S_COL0 + t * BN, desc_k_major<D, BM>(qa, ks), desc_k_major<D, BN>(kb, ks), IDESC_S,
+                  ks > 0);
+        umma_commit(sm.s_full + t);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = v_s + (j % C::NST) * C::KV_TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_ts(tmem + C::O_COL0 + t * D, tmem + C::S_COL0 + t * BN + ks * 8, desc_mn_major<D, BN>(vb, ks),
+                  IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(sm.q_full, 0, ctl, 10) && mbar_wait(sm.k_full, 0, ctl, 11);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < QT; ++t)
+          if (n_kv[t] > 0) issue_s(t, 0);
+        umma_commit(sm.k_empty);
+      }
+      for (int j = 0; j < n_max && ok; ++j) {
+        const int s = j % C::NST;
+        if (!mbar_wait(sm.v_full + s, uint32_t(j / C::NST) & 1, ctl, 12)) { ok = false; break; }
+        const bool more = j + 1 < n_max;
+        if (more && !mbar_wait(sm.k_full + (j + 1) % C::NST, uint32_t((j + 1) / C::NST) & 1, ctl, 13)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int t = 0; t < QT && ok; ++t) {
+          if (j >= n_kv[t]) continue;
+          if (!mbar_wait(sm.p_ready + t, uint32_t(j) & 1, ctl, 14)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < n_kv[t]) issue_s(t, j + 1);
+        }
+        if (!ok) break;
+        umma_commit(sm.v_empty + s);
+        if (more) umma_commit(sm.k_empty + (j + 1) % C::NST);
+      }
+      if (ok) {
+        for (int t = 0; t < QT; ++t)
+          if (n_kv[t] > 0) umma_commit(sm.o_full + t);
+      }
+      // Drain every MMA this thread issued before the CTA tears down TMEM.
+      umma_commit(sm.mma_done);
+      mbar_wait_drain(sm.mma_done, 0, ctl, 15);
+    }
+  } else if (warp >= 4) {
+    // =================== softmax warpgroups ===================
+    const int t = (warp - 4) / 4;       // query tile of this warpgroup
+    const int wq = warp & 3;            // TMEM lane quadrant this warp may access
+    const int row_local = wq * 32 + lane;
+    const int r = row0 + t * BM + row_local;  // query row
+    const int nt = n_kv[t];
+    // last visible key column of this row (local key index)
+    int lim = shp.Nk - 1;
+    if (shp.causal) {
+      const long long c = (long long)r + shp.q_off - shp.k_off;
+      lim = c < lim ? int(c) : lim;  // may be negative: no visible key
+    }
+    const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::S_COL0 + t * BN));
+    const uint32_t tO = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::O_COL0 + t * D));
+    const float c2 = shp.scale_log2;
+    float m = -INFINITY;  // running exponent base (scaled log2 units)
+    float l = 0.f;        // running row sum of exp2(s * c2 - m)
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!mbar_wait_warp(sm.s_full + t, uint32_t(j) & 1, ctl, 20 + t)) { ok = false; break; }
+      tc_fence_after();
+      float s[BN];
+      tmem_ld64(tS, *reinterpret_cast<float(*)[64]>(&s[0]));
+      tmem_ld64(tS + 64, *reinterpret_cast<float(*)[64]>(&s[64]));
+      const int lim_j = lim - j * BN;  // last visible local column in this tile
+      if (lim_j < BN - 1) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      const float m_tile = mx * c2;
+      bool rescale = false;
+      float m_new = m;
+      if (m_tile > m + RESCALE_THRESHOLD) {  // false while m_tile == -inf
+        m_new = m_tile;
+        rescale = true;
+      }
+      const float alpha = rescale ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 on the first tile
+      const float base = m_new == -INFINITY ? 0.f : m_new;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(s[cc * 32 + 2 * i], c2, -base));
+          const float p1 = ex2(fmaf(s[cc * 32 + 2 * i + 1], c2, -base));
+          rowsum += p0 + p1;
+          packed[i] = pack_half2(p0, p1);
+        }
+        tmem_st16(tS + cc * 16, packed);
+      }
+      l = l * alpha + rowsum;
+      m = m_new;
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float o[32];
+          tmem_ld32(tO + cc * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + cc * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(sm.p_ready + t);
+    }
+    // ---- epilogue: O / l -> fp16, lse2 = m + log2(l) ----
+    if (ok && nt > 0) ok = mbar_wait_warp(sm.o_full + t, 0, ctl, 22 + t);
+    if (ok) {
+      const bool row_ok = r < shp.Nq;
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      __half* orow = o_ptr + (long long)b * o_sb + (long long)h * o_sh + (long long)r * o_sn;
+      if (nt > 0) tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float o[32];
+        if (nt > 0) {
+          tmem_ld32(tO + cc * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_half2(o[v8 * 8 + 0] * inv_l, o[v8 * 8 + 1] * inv_l);
+            pk.y = pack_half2(o[v8 * 8 + 2] * inv_l, o[v8 * 8 + 3] * inv_l);
+            pk.z = pack_half2(o[v8 * 8 + 4] * inv_l, o[v8 * 8 + 5] * inv_l);
+            pk.w = pack_half2(o[v8 * 8 + 6] * inv_l, o[v8 * 8 + 7] * inv_l);
+            *reinterpret_cast<uint4*>(orow + cc * 32 + v8 * 8) = pk;
+          }
+        }
+      }
+      if (row_ok) lse_ptr[(long long)bh * shp.Nq + r] = l > 0.f ? m + lg2(l) : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch_fwd_t(const FwdArgs& a) {
+  using C = fwd::Cfg<D>;
+  const int smem = C::SMEM_BYTES;
+  auto kern = fa_fwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return FA_ERR_LAUNCH;
+  const int n_qblk = (a.shape.Nq + fwd::QT * fwd::BM - 1) / (fwd::QT * fwd::BM);
+  dim3 grid(unsigned(n_qblk * a.shape.B * a.shape.Hq));
+  kern<<<grid, fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, a.o, a.o_sb, a.o_sh,
+                                                   a.o_sn, a.lse);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int launch_fwd(const FwdArgs& a, int D) {
+  switch (D) {
+    case 32: return launch_fwd_t<32>(a);
+    case 64: return launch_fwd_t<64>(a);
+    case 128: return launch_fwd_t<128>(a);
+    default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+}
+
+}  // namespace fa

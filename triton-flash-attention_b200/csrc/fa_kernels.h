@@ -1,0 +1,57 @@
+// fa_kernels.h -- internal launch interface between the C ABI (fa_capi.cu)
+// and the kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include "../../include/fa_b200.h"
+#include "fa_common.cuh"
+
+namespace fa {
+
+struct FwdArgs {
+  CUtensorMap tmap_q, tmap_k, tmap_v;  // 4-D {D, N, H, B} fp16, box {<=64, 128, 1, 1}
+  AttnShape shape;
+  __half* o;
+  long long o_sb, o_sh, o_sn;
+  float* lse;
+  cudaStream_t stream;
+};
+
+struct BwdArgs {
+  CUtensorMap tmap_q, tmap_k, tmap_v, tmap_do;  // 4-D fp16 maps
+  AttnShape shape;
+  const float* lse;
+  const float* delta;
+  void* dq;  // fa_bwd_dq output (fp16, or fp32 when accumulate_fp32)
+  long long dq_sb, dq_sh, dq_sn;
+  void* dk;
+  void* dv;
+  long long dk_sb, dk_sh, dk_sn;
+  long long dv_sb, dv_sh, dv_sn;
+  int accumulate_fp32;
+  cudaStream_t stream;
+};
+
+int launch_fwd(const FwdArgs& a, int D);
+int launch_bwd_dq(const BwdArgs& a, int D);
+int launch_bwd_dkdv(const BwdArgs& a, int D);
+int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long o_sn, const __half* dO,
+                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
+                     cudaStream_t stream);
+int launch_merge_partial(float* o_acc, float* lse_acc, const __half* o_part, const float* lse_part, long long rows,
+                         int D, cudaStream_t stream);
+
+// Query-tile / key-tile sizes the host needs for TMA box shapes.
+namespace dq_cfg {
+constexpr int BM = 128;  // query rows per tile
+constexpr int BN = 64;   // keys per tile
+}  // namespace dq_cfg
+namespace dkdv_cfg {
+constexpr int BM = 128;  // key rows per tile (the MMA M dimension)
+constexpr int BQ = 64;   // query rows per tile
+}  // namespace dkdv_cfg
+
+}  // namespace fa
