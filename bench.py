@@ -1,0 +1,381 @@
+"""Benchmark of the attention hot path (driver contract: one JSON line).
+
+Metric: causal fp16 forward+backward algorithmic TFLOP/s at
+B=4, H=16, N=4096, D=64 (config C2), the FLOP convention of the reference's
+benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
+4*B*H*N(N+1)/2*D = 4.8115e11 FLOP per step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+* ``value``: one step = forward + Delta + dQ + dK/dV on device-resident
+  synthetic inputs (seeded N(0,1) fp16), K steps timed with CUDA events,
+  max over ranks.  The per-step working set (q, k, v, o, dO, dq, dk, dv =
+  256 MiB) exceeds the 126 MB L2, so no flush is inserted.
+* ``e2e``: the same metric through the public API
+  (``scaled_dot_product_attention`` + autograd backward) with pinned host
+  buffers: each step copies q, k, v, dO host->device and O, dQ, dK, dV
+  device->host inside the timed region.
+* ``roofline``: the dominant kernel (dK/dV) -- its GEMM FLOPs per launch over
+  its CUDA-event duration against the measured dense bf16/fp16 peak.
+* ``cpu_baseline``: the oracle's float32 restatement of the reference's CPU
+  path timed on the host cores on a bounded sample (whole heads of C2).
+* Multi-GPU (torchrun): weak scaling -- every rank runs its own C2-sized
+  batch shard; no collective touches the data path.
+* ``--impl reference``: the reference's CPU implementation of the path (the
+  oracle port of its SDPA fallback) on the host cores; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+B, H, N, D = 4, 16, 4096, 64
+CAUSAL = True
+WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
+DKDV_TRAFFIC_BYTES = 207_236_608 + 41_714_432
+
+
+def flops_step() -> int:
+    from triton_flash_attention_b200.flops import attention_flops
+    return attention_flops(batch=B, query_heads=H, sequence=N, head_dim=D, causal=CAUSAL, mode="forward-backward")
+
+
+def read_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_baseline(max_seconds: float = 12.0) -> dict:
+    """Oracle (float32 numpy/BLAS) forward+backward on whole C2 heads, timed
+    on the host cores until ``max_seconds`` of work; TFLOP/s of the sample."""
+    import numpy as np
+
+    from oracle import fa2_oracle as orc
+    from triton_flash_attention_b200.flops import attention_flops
+
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads") or 1) for i in threadpool_info()) if threadpool_info() else 1
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    heads = 0
+    t_total = 0.0
+    while heads < B * H and (t_total < max_seconds or heads == 0):
+        q, k, v, do = (rng.standard_normal((N, D)).astype(np.float16) for _ in range(4))
+        t0 = time.perf_counter()
+        orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
+        t_total += time.perf_counter() - t0
+        heads += 1
+    fl = attention_flops(batch=1, query_heads=heads, sequence=N, head_dim=D, causal=CAUSAL,
+                         mode="forward-backward")
+    return {"value": fl / t_total / 1e12, "unit": "TFLOP/s", "cores": int(cores), "kind": "port",
+            "sample": f"{heads} of {B * H} (batch, head) pairs of C2, fwd+bwd, float32 numpy+BLAS, "
+                      f"{t_total:.1f} s"}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier_max(world: int, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args) -> None:
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks = read_peaks()
+    scale = D ** -0.5
+    fl = flops_step()
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q, k, v, do = (torch.randn(B, H, N, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4))
+    stream = torch.cuda.current_stream(dev)
+
+    ev_kv = []
+
+    def step(record: bool):
+        o, lse = fa.attention_forward(q, k, v, CAUSAL, scale)
+        delta = fa.attention_delta(o, do)
+        fa.attention_backward_dq(q, k, v, do, lse, delta, CAUSAL, scale)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        fa.attention_backward_dkdv(q, k, v, do, lse, delta, CAUSAL, scale)
+        if record:
+            e1.record(stream)
+            ev_kv.append((e0, e1))
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = barrier_max(world, ms_local)
+    kv_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_kv)
+    value = world * fl / (ms * 1e-3) / 1e12
+    status = fa._abi.device_status()
+
+    # ---------------- end to end through the public API, host buffers
+    hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+    outs = [torch.empty(B, H, N, D, dtype=torch.float16).pin_memory() for _ in range(4)]
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+
+    def e2e_step():
+        qd = hq.to(dev, non_blocking=True).requires_grad_()
+        kd = hk.to(dev, non_blocking=True).requires_grad_()
+        vd = hv.to(dev, non_blocking=True).requires_grad_()
+        dod = hdo.to(dev, non_blocking=True)
+        o = fa.scaled_dot_product_attention(qd, kd, vd, is_causal=CAUSAL)
+        gq, gk, gv = torch.autograd.grad(o, (qd, kd, vd), dod)
+        for dst, src in zip(outs, (o, gq, gk, gv)):
+            dst.copy_(src.detach(), non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s2 = torch.cuda.Event(enable_timing=True)
+    e2 = torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = barrier_max(world, s2.elapsed_time(e2) / e2e_steps)
+    e2e_value = world * fl / (e2e_ms * 1e-3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    # dK/dV kernel: 4 GEMMs of 2*pairs*D FLOPs per (b, h) = 2x the forward
+    kv_flops = 2 * fa.attention_flops(batch=B, query_heads=H, sequence=N, head_dim=D, causal=CAUSAL,
+                                      mode="forward")
+    achieved = kv_flops / (kv_ms * 1e-3) / 1e12
+    # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch of
+    # the dK/dV kernel (profiles/c2_kernels_v1.md)
+    traffic = DKDV_TRAFFIC_BYTES
+    if rank == 0:
+        line = {
+            "metric": "causal fp16 fwd+bwd TFLOP/s, B4 H16 N4096 D64; % of B200 FP16 tensor peak",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp16",
+            "data": "synthetic: seeded N(0,1) q, k, v, dO (no dataset involved)",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "heads": H, "seq_len": N,
+                       "head_dim": D, "causal": CAUSAL, "parallelism": f"batch-shard x{world} (no collective)",
+                       "l2": "per-step working set 256 MiB > 126 MB L2; no flush"},
+            "pct_of_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+            "roofline": {"kernel": "fa_bwd_dkdv_kernel<64>", "bound": "tensor", "achieved": round(achieved, 2),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                         "peak_source": peaks["source"], "launch_ms": round(kv_ms, 4)},
+            "cpu_baseline": cpu,
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk.summary(),
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import fa2_oracle as orc
+    from triton_flash_attention_b200.flops import attention_flops
+
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads") or 1) for i in threadpool_info()) if threadpool_info() else 1
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    heads_per_step = 1
+    q, k, v, do = (rng.standard_normal((N, D)).astype(np.float16) for _ in range(4))
+    for _ in range(args.warmup):
+        orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for _h in range(heads_per_step):
+            orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    fl = attention_flops(batch=1, query_heads=heads_per_step, sequence=N, head_dim=D, causal=CAUSAL,
+                         mode="forward-backward")
+    value = fl / sec / 1e12
+    line = {
+        "impl": "reference",
+        "metric": "causal fp16 fwd+bwd TFLOP/s, B4 H16 N4096 D64; % of B200 FP16 tensor peak",
+        "value": round(value, 5),
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 inputs, fp32 CPU math",
+        "data": "synthetic: seeded N(0,1) q, k, v, dO",
+        "config": {"workload": WORKLOAD, "global_batch": B, "heads": H, "seq_len": N, "head_dim": D,
+                   "causal": CAUSAL, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": int(cores), "kind": "port",
+                         "sample": f"each step = fwd+bwd of {heads_per_step} of the {B * H} (batch, head) "
+                                   "pairs of C2 (the reference's CPU path: PyTorch SDPA math, restated in "
+                                   "float32 numpy/BLAS)"},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

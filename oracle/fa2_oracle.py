@@ -303,3 +303,29 @@ def attention_block(q, k, v, *, causal: bool, scale: float, q_offset: int = 0, k
     produces before merging."""
     r = sdpa_reference(q, k, v, causal=causal, scale=scale, q_offset=q_offset, k_offset=k_offset)
     return r["o"], r["lse2"]
+
+
+def sdpa_head_fwd_bwd_fp32(q, k, v, do, *, causal: bool, scale: float):
+    """One (batch, head) of dense attention forward + backward in float32
+    with BLAS matmuls: the reference's CPU path (attention.py:774-786 ->
+    PyTorch SDPA math) restated for timing the CPU baseline.  Inputs are
+    (N, D) arrays; returns (o, dq, dk, dv)."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    do = np.asarray(do, np.float32)
+    n = q.shape[0]
+    s = (q @ k.T) * np.float32(scale)
+    if causal:
+        s[np.triu_indices(n, 1, k.shape[0])] = -np.inf
+    s -= s.max(axis=1, keepdims=True)
+    p = np.exp(s, out=s)
+    p /= p.sum(axis=1, keepdims=True)
+    o = p @ v
+    dp = do @ v.T
+    delta = (o * do).sum(axis=1, keepdims=True)
+    ds = p * (dp - delta)
+    dq = (ds @ k) * np.float32(scale)
+    dk = (ds.T @ q) * np.float32(scale)
+    dv = p.T @ do
+    return o, dq, dk, dv

@@ -1,0 +1,69 @@
+"""The C-ABI library loads and exports every symbol include/fa_b200.h
+declares; argument validation answers without touching a GPU (CPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from triton_flash_attention_b200 import _abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    text = open(os.path.join(ROOT, "include", "fa_b200.h")).read()
+    return re.findall(r"FA_API\s+(?:const\s+)?\w+\**\s+\**(fa_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert {"fa_fwd", "fa_bwd_delta", "fa_bwd_dq", "fa_bwd_dkdv", "fa_merge_partial",
+            "fa_device_status", "fa_status_string", "fa_version"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _abi.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_declared()) == set(_abi.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    lib = _abi.lib()
+    assert lib.fa_version() >= 100
+    assert "head_dim" in _abi.status_string(_abi.FA_ERR_UNSUPPORTED_HEAD_DIM)
+    assert "16-byte" in _abi.status_string(_abi.FA_ERR_MISALIGNED)
+    assert "timed out" in _abi.status_string(_abi.FA_ERR_DEVICE_TIMEOUT)
+
+
+def _strides():
+    return (ctypes.c_int64 * 3)(4096, 1024, 64)
+
+
+@pytest.mark.parametrize("d,expect", [(48, _abi.FA_ERR_UNSUPPORTED_HEAD_DIM), (256, _abi.FA_ERR_UNSUPPORTED_HEAD_DIM)])
+def test_rejects_head_dim_before_any_cuda_call(d, expect):
+    s = _strides()
+    rc = _abi.lib().fa_fwd(16, 16, 16, 16, 16, 1, 1, 1, 8, 8, d, s, s, s, s, 0.1, 1, 0, 0, None)
+    assert rc == expect
+
+
+@pytest.mark.parametrize("shape", [(0, 1, 1, 8, 8), (1, 3, 2, 8, 8), (1, 1, 1, 0, 8), (1, 1, 1, 8, -1)])
+def test_rejects_bad_shapes(shape):
+    b, hq, hkv, nq, nk = shape
+    s = _strides()
+    rc = _abi.lib().fa_fwd(16, 16, 16, 16, 16, b, hq, hkv, nq, nk, 64, s, s, s, s, 0.1, 1, 0, 0, None)
+    assert rc == _abi.FA_ERR_BAD_SHAPE
+
+
+def test_rejects_misaligned_output_and_nonfinite_scale():
+    s = _strides()
+    lib = _abi.lib()
+    assert lib.fa_fwd(16, 16, 16, 18, 16, 1, 1, 1, 8, 8, 64, s, s, s, s, 0.1, 1, 0, 0, None) == _abi.FA_ERR_MISALIGNED
+    assert lib.fa_fwd(16, 16, 16, 16, 16, 1, 1, 1, 8, 8, 64, s, s, s, s, float("inf"), 1, 0, 0, None) \
+        == _abi.FA_ERR_BAD_SHAPE
+    odd = (ctypes.c_int64 * 3)(4096, 1024, 63)
+    assert lib.fa_bwd_delta(16, 16, 16, 1, 1, 8, 64, odd, s, None) == _abi.FA_ERR_MISALIGNED
