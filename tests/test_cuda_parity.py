@@ -142,9 +142,11 @@ def test_golden_vectors():
             ref_err = _maxabs(g[f"{name}/{key}"], ref[key])
             my_err = _maxabs(mine, ref[key])
             assert my_err <= max(1.5 * ref_err, 2e-4), (name, key, my_err, ref_err)
-        # the saved LSE agrees with the reference kernel's own saved LSE
+        # the saved LSE agrees with the reference kernel's own saved LSE; the
+        # bound covers the exp2 approximations (MUFU ex2.approx and the
+        # 1e-4-relative polynomial), i.e. ~1.4e-4 in log2 units
         _, lse = fa.attention_forward(q.cuda(), k.cuda(), v.cuda(), bool(causal), d ** -0.5)
-        assert _maxabs(lse.cpu(), g[f"{name}/lse2"]) <= 1e-4, name
+        assert _maxabs(lse.cpu(), g[f"{name}/lse2"]) <= 3e-4, name
 
 
 @pytest.mark.parametrize("hq,hkv", [(4, 4), (8, 2)])

@@ -166,8 +166,9 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
                         bx * G::BOX, q0, h, b);
           }
         }
-        // lse2 / Delta of the item's 64 query rows; rows past Nq, or rows
-        // that see no key at all, get lse2 = +inf so that their P is 0.
+        // -lse2 / -Delta of the item's 64 query rows (negated for the FMA);
+        // rows past Nq, or rows that see no key at all, get lse2 = +inf so
+        // that their P is 0.
         const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -178,8 +179,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
             if (lv == -INFINITY) lv = INFINITY;
             dv = delta[rowbase + qi];
           }
-          s_lse[s * BQ + lane * 2 + e] = lv;
-          s_delta[s * BQ + lane * 2 + e] = dv;
+          s_lse[s * BQ + lane * 2 + e] = -lv;
+          s_delta[s * BQ + lane * 2 + e] = -dv;
         }
         mbar_arrive(full + s);
         ++n_iss;
@@ -259,6 +260,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     const int rl = wq * 32 + lane;  // key row within the tile
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(w * 128));
     const float c2 = shp.scale_log2;
+    const uint64_t c2x2 = f2pack(c2, c2);
     // causal: key row rl sees query column c of an item at rows q0.. iff
     // c >= cmin_base - q0
     const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off;
@@ -278,28 +280,27 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         const long long x = cmin_base - q0;
         cmin = x <= 0 ? 0 : (x > BQ ? BQ : int(x));
       }
+      if (cmin > 0) {  // causal diagonal: queries before this key are invisible
+#pragma unroll
+        for (int c = 0; c < BQ; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+      }
+      // stage values are stored negated: -lse2 and -Delta
       const float4* l4 = reinterpret_cast<const float4*>(s_lse + s * BQ);
       const float4* d4 = reinterpret_cast<const float4*>(s_delta + s * BQ);
       uint32_t pk_p[BQ / 2], pk_ds[BQ / 2];
 #pragma unroll
       for (int c4 = 0; c4 < BQ / 4; ++c4) {
-        const float4 lv = l4[c4];
-        const float4 dv = d4[c4];
-        const float la[4] = {lv.x, lv.y, lv.z, lv.w};
-        const float da[4] = {dv.x, dv.y, dv.z, dv.w};
-        float p[4], ds[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = c4 * 4 + e;
-          float pv = ex2(fmaf(st[c], c2, -la[e]));
-          pv = c >= cmin ? pv : 0.f;
-          p[e] = pv;
-          ds[e] = pv * (dpt[c] - da[e]);
-        }
-        pk_p[c4 * 2] = pack_half2(p[0], p[1]);
-        pk_p[c4 * 2 + 1] = pack_half2(p[2], p[3]);
-        pk_ds[c4 * 2] = pack_half2(ds[0], ds[1]);
-        pk_ds[c4 * 2 + 1] = pack_half2(ds[2], ds[3]);
+        const float4 nl = l4[c4];
+        const float4 nd = d4[c4];
+        const int c = c4 * 4;
+        const uint32_t p01 = ex2_h2(h2_from_f2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
+        const uint32_t p23 = ex2_h2(h2_from_f2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
+        const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+        const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+        pk_p[c4 * 2] = p01;
+        pk_p[c4 * 2 + 1] = p23;
+        pk_ds[c4 * 2] = hmul2(p01, d01);
+        pk_ds[c4 * 2 + 1] = hmul2(p23, d23);
       }
       tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
       tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
@@ -365,6 +366,398 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D <= 64: 128-query items.  At D <= 64 an N = 64 MMA runs at ~70% of the
+// tensor rate (measured: M128 x N x K16 takes max(N/2, ~45) cycles), so the
+// items here are 128 query rows wide (S^T, dP^T are N = 128 MMAs at full
+// rate).  Both elementwise warpgroups work on every item, warpgroup w on
+// query columns [64w, 64w+64), and S^T is double-buffered in TMEM so that the
+// tensor core computes S^T of item i+2 and dP^T of item i+1 while the
+// warpgroups exponentiate item i+1.  P^T is published (for dV) before dS^T
+// (for dK), so the dV GEMM starts as soon as the exponentials are done.
+// TMEM: S^T buffers at [0,128) and [128,256), dP^T at [256,384),
+//       dV at [384, 384+D), dK at [384+D, 384+2D).
+// Warpgroup w writes P^T into its S^T buffer's columns [64w, 64w+32) and
+// dS^T into dP^T's columns [256+64w, 256+64w+32): inside the range it read,
+// so the two warpgroups never race.
+namespace bkvw {
+constexpr int BM = 128;   // keys per CTA
+constexpr int BQ = 128;   // query rows per item
+constexpr int NUM_THREADS = 384;
+constexpr int POLY_MASK = 4;  // pairs (i & 7) < 4 use the FMA-pipe exp2: half off MUFU
+
+template <int D>
+struct Cfg {
+  using G = TileGeom<D>;
+  static constexpr int NST = 4;
+  static constexpr int KV_TILE_BYTES = BM * D * 2;
+  static constexpr int Q_TILE_BYTES = BQ * D * 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_TILE_BYTES;
+  static constexpr int OFF_Q = OFF_V + KV_TILE_BYTES;
+  static constexpr int OFF_DO = OFF_Q + NST * Q_TILE_BYTES;
+  static constexpr int OFF_LSE = OFF_DO + NST * Q_TILE_BYTES;
+  static constexpr int OFF_DELTA = OFF_LSE + NST * BQ * 4;
+  static constexpr int OFF_BAR = OFF_DELTA + NST * BQ * 4;
+  // kv_full, full[NST], empty[NST], s_full[2], dp_full, p_ready[2], ds_ready, acc_full, mma_done
+  static constexpr int NUM_BARS = 1 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 1;
+  static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_MISC = OFF_CTL + 16;
+  static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DP_COL = 256;
+  static constexpr int DV_COL = 384;
+  static constexpr int DK_COL = 384 + D;
+  static_assert(D <= 64, "wide dK/dV path is for D <= 64");
+  static_assert(DK_COL + D <= TMEM_COLS, "TMEM budget");
+};
+}  // namespace bkvw
+
+template <int D>
+__global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
+    fa_bwd_dkdv_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                            const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                            const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
+                            void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh,
+                            const long long dk_sn, void* __restrict__ dv_out, const long long dv_sb,
+                            const long long dv_sh, const long long dv_sn, const int accumulate_fp32) {
+  using namespace bkvw;
+  using C = Cfg<D>;
+  using G = TileGeom<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_saddr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
+  const uint32_t sbase = smem_u32(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* full = bars + 1;
+  uint64_t* empty = full + C::NST;
+  uint64_t* s_full = empty + C::NST;
+  uint64_t* dp_full = s_full + 2;
+  // p_ready is per S^T buffer: phase k of p_ready[b] belongs to item 2k+b, so
+  // it cannot run two phases ahead of the MMA thread (item it+2's S^T is
+  // issued only after the MMA thread consumed item it's P^T).
+  uint64_t* p_ready = dp_full + 1;
+  uint64_t* ds_ready = p_ready + 2;
+  uint64_t* acc_full = ds_ready + 1;
+  uint64_t* mma_done = acc_full + 1;
+  CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
+  volatile CtaCtl* ctl = ctl_w;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  float* s_nlse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* s_ndelta = reinterpret_cast<float*>(smem + C::OFF_DELTA);
+
+  const int warp = int(warp_id());
+  const int lane = int(lane_id());
+
+  const int BHkv = shp.B * shp.Hkv;
+  const int kv_tile = int(blockIdx.x) / BHkv;
+  const int bhk = int(blockIdx.x) % BHkv;
+  const int b = bhk / shp.Hkv;
+  const int kvh = bhk % shp.Hkv;
+  const int group = shp.Hq / shp.Hkv;
+  const int kv0 = kv_tile * BM;
+  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  int i_start = 0;
+  if (shp.causal) {
+    const long long first_row = (long long)kv0 + shp.k_off - shp.q_off;
+    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
+    if (i_start > n_qt) i_start = n_qt;
+  }
+  const int per_head = n_qt - i_start;
+  const int n_items = per_head * group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(full + s, 1 + 32);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_full + 1, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_ready, 256);
+    mbar_init(p_ready + 1, 256);
+    mbar_init(ds_ready, 256);
+    mbar_init(acc_full, 1);
+    mbar_init(mma_done, 1);
+    ctl_w->abort = 0;
+    ctl_w->status = shp.status;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =================== producer warp ===================
+    if (n_items > 0) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tmap_q);
+        tma_prefetch_desc(&tmap_do);
+        tma_prefetch_desc(&tmap_k);
+        tma_prefetch_desc(&tmap_v);
+        mbar_arrive_expect_tx(kv_full, 2 * C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_K + bx * BM * G::SW, &tmap_k, kv_full, bx * G::BOX, kv0, kvh, b);
+          tma_load_4d(smem + C::OFF_V + bx * BM * G::SW, &tmap_v, kv_full, bx * G::BOX, kv0, kvh, b);
+        }
+      }
+      int n_iss = 0;
+      for (int it = 0; it < n_items; ++it) {
+        const int s = it % C::NST;
+        const uint32_t u = uint32_t(it / C::NST);
+        if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 161)) break;
+        const int h = kvh * group + it / per_head;
+        const int q0 = (i_start + it % per_head) * BQ;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full + s, 2 * C::Q_TILE_BYTES);
+          for (int bx = 0; bx < G::NBOX; ++bx) {
+            tma_load_4d(smem + C::OFF_Q + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_q, full + s, bx * G::BOX,
+                        q0, h, b);
+            tma_load_4d(smem + C::OFF_DO + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_do, full + s,
+                        bx * G::BOX, q0, h, b);
+          }
+        }
+        // -lse2 / -Delta of the item's 128 query rows; rows past Nq, or rows
+        // that see no key, get lse2 = +inf so that their P is 0.
+        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int qi = q0 + e * 32 + lane;
+          float lv = INFINITY, dv = 0.f;
+          if (qi < shp.Nq) {
+            lv = lse[rowbase + qi];
+            if (lv == -INFINITY) lv = INFINITY;
+            dv = delta[rowbase + qi];
+          }
+          s_nlse[s * BQ + e * 32 + lane] = -lv;
+          s_ndelta[s * BQ + e * 32 + lane] = -dv;
+        }
+        mbar_arrive(full + s);
+        ++n_iss;
+      }
+      if (lane == 0) {
+        mbar_wait_drain(kv_full, 0, ctl, 162);
+        for (int it = (n_iss > C::NST ? n_iss - C::NST : 0); it < n_iss; ++it)
+          mbar_wait_drain(full + it % C::NST, uint32_t(it / C::NST) & 1, ctl, 163);
+      }
+    }
+  } else if (warp == 1) {
+    // =================== tcgen05 MMA issuer ===================
+    if (lane == 0 && n_items > 0) {
+      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0);
+      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1);
+      const uint32_t k_s = sbase + C::OFF_K;
+      const uint32_t v_s = sbase + C::OFF_V;
+      auto q_tile = [&](int it) { return sbase + C::OFF_Q + (it % C::NST) * C::Q_TILE_BYTES; };
+      auto do_tile = [&](int it) { return sbase + C::OFF_DO + (it % C::NST) * C::Q_TILE_BYTES; };
+      auto issue_s = [&](int it) {  // S^T -> buffer it & 1
+        const uint32_t qb = q_tile(it);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + (it & 1) * 128, desc_k_major<D, BM>(k_s, ks), desc_k_major<D, BQ>(qb, ks), IDESC_ST,
+                  ks > 0);
+        umma_commit(s_full + (it & 1));
+      };
+      auto issue_dp = [&](int it) {
+        const uint32_t db = do_tile(it);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + C::DP_COL, desc_k_major<D, BM>(v_s, ks), desc_k_major<D, BQ>(db, ks), IDESC_ST, ks > 0);
+        umma_commit(dp_full);
+      };
+      // A operand (fp16 in TMEM) for query rows [16ks, 16ks+16) of a region
+      // whose halves sit 64 columns apart
+      auto a_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
+      bool ok = mbar_wait(kv_full, 0, ctl, 170) && mbar_wait(full, 0, ctl, 171);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
+        if (n_items > 1) {
+          ok = mbar_wait(full + 1 % C::NST, uint32_t(1 / C::NST) & 1, ctl, 172);
+          if (ok) {
+            tc_fence_after();
+            issue_s(1);
+          }
+        }
+      }
+      for (int it = 0; it < n_items && ok; ++it) {
+        const uint32_t db = do_tile(it);
+        const uint32_t qb = q_tile(it);
+        if (!mbar_wait(p_ready + (it & 1), uint32_t(it >> 1) & 1, ctl, 173)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < BQ / 16; ++ks)
+          umma_ts(tmem + C::DV_COL, tmem + (it & 1) * 128 + a_col(ks), desc_mn_major<D, BQ>(db, ks), IDESC_G,
+                  (it > 0 || ks > 0) ? 1u : 0u);
+        // S^T(it+2) reuses buffer it&1 (after dV(it) read P^T from it) and is
+        // queued before the dS^T wait so the tensor core stays busy meanwhile
+        if (it + 2 < n_items) {
+          const int n2 = it + 2;
+          if (!mbar_wait(full + n2 % C::NST, uint32_t(n2 / C::NST) & 1, ctl, 175)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(n2);
+        }
+        if (!mbar_wait(ds_ready, uint32_t(it) & 1, ctl, 174)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < BQ / 16; ++ks)
+          umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + a_col(ks), desc_mn_major<D, BQ>(qb, ks), IDESC_G,
+                  (it > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(empty + it % C::NST);
+        if (it + 1 < n_items) issue_dp(it + 1);  // its stage was waited for before S^T(it+1)
+      }
+      if (ok) umma_commit(acc_full);
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, ctl, 176);
+    }
+  } else if (warp >= 4) {
+    // =================== P^T / dS^T warpgroups ===================
+    const int w = (warp - 4) / 4;  // query-column half of every item
+    const int wq = warp & 3;
+    const int rl = wq * 32 + lane;  // key row within the tile
+    const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
+    const uint64_t c2x2 = f2pack(shp.scale_log2, shp.scale_log2);
+    const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off - 64 * w;
+    bool ok = true;
+    for (int it = 0; it < n_items; ++it) {
+      const int s = it % C::NST;
+      if (!mbar_wait_warp(s_full + (it & 1), uint32_t(it >> 1) & 1, ctl, 180 + w)) { ok = false; break; }
+      // the stage's -lse2/-Delta: its phase completed before S^T was issued
+      if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 182 + w)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tS = lane_base + uint32_t((it & 1) * 128 + 64 * w);
+      float st[64];
+      tmem_ld64(tS, st);
+      const int q0 = (i_start + it % per_head) * BQ;
+      if (shp.causal) {
+        const long long x = cmin_base - q0;
+        const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+        if (cmin > 0) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+        }
+      }
+      const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * w);
+      uint32_t pk_p[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 nl = l4[c4];
+        const int c = c4 * 4;
+        const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
+        const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
+        const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
+        const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
+        pk_p[c4 * 2] = h2_from_f2(e01);
+        pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+      }
+      tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
+      tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_ready + (it & 1));
+      // ---- dS^T = P^T (dP^T - Delta) ----
+      if (!mbar_wait_warp(dp_full, uint32_t(it) & 1, ctl, 184 + w)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * w);
+      float dpt[64];
+      tmem_ld64(tD, dpt);
+      const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * w);
+      uint32_t pk_ds[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 nd = d4[c4];
+        const int c = c4 * 4;
+        const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+        const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+        pk_ds[c4 * 2] = hmul2(pk_p[c4 * 2], d01);
+        pk_ds[c4 * 2 + 1] = hmul2(pk_p[c4 * 2 + 1], d23);
+      }
+      tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+      tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+    }
+    // ---- epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK ----
+    if (ok && n_items > 0) ok = mbar_wait_warp(acc_full, 0, ctl, 186 + w);
+    if (ok) {
+      const int kr = kv0 + rl;
+      const bool row_ok = kr < shp.Nk;
+      const float sc = w == 0 ? 1.f : shp.scale;
+      const uint32_t tAcc = lane_base + uint32_t(w == 0 ? C::DV_COL : C::DK_COL);
+      void* out = w == 0 ? dv_out : dk_out;
+      const long long off0 = w == 0 ? ((long long)b * dv_sb + (long long)kvh * dv_sh + (long long)kr * dv_sn)
+                                    : ((long long)b * dk_sb + (long long)kvh * dk_sh + (long long)kr * dk_sn);
+      if (n_items > 0) tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float g[32];
+        if (n_items > 0) {
+          tmem_ld32(tAcc + cc * 32, g);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g[i] = 0.f;
+        }
+        if (!row_ok) continue;
+        if (accumulate_fp32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + off0 + cc * 32);
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 x = dst[v4];
+            x.x += g[v4 * 4 + 0] * sc;
+            x.y += g[v4 * 4 + 1] * sc;
+            x.z += g[v4 * 4 + 2] * sc;
+            x.w += g[v4 * 4 + 3] * sc;
+            dst[v4] = x;
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out) + off0 + cc * 32);
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 pk;
+            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
+            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
+            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
+            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            dst[v8] = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
+  using C = bkvw::Cfg<D>;
+  auto kern = fa_bwd_dkdv_wide_kernel<D>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  const int n_kt = (a.shape.Nk + bkvw::BM - 1) / bkvw::BM;
+  dim3 grid(unsigned(n_kt * a.shape.B * a.shape.Hkv));
+  kern<<<grid, bkvw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape,
+                                                             a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv,
+                                                             a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 template <int D>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
@@ -381,8 +774,8 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
 
 int launch_bwd_dkdv(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return launch_bwd_dkdv_t<32>(a);
-    case 64: return launch_bwd_dkdv_t<64>(a);
+    case 32: return launch_bwd_dkdv_wide_t<32>(a);
+    case 64: return launch_bwd_dkdv_wide_t<64>(a);
     case 128: return launch_bwd_dkdv_t<128>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }

@@ -250,6 +250,9 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(t * 128));
     const uint32_t tQ = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::DQ_COL0 + t * D));
     const float c2 = shp.scale_log2;
+    const uint64_t c2x2 = f2pack(c2, c2);
+    const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
+    const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       if (!mbar_wait_warp(s_full + t, uint32_t(j) & 1, ctl, 50 + t)) { ok = false; break; }
@@ -258,17 +261,20 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
       tmem_ld64(tS, s);
       tmem_ld64(tS + 64, dp);
       const int lim_j = lim - j * BN;
+      if (lim_j < BN - 1) {  // diagonal / boundary tile: hide invisible keys
+#pragma unroll
+        for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
+      }
 #pragma unroll
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c0 = cc * 32 + 2 * i;
-          float p0 = ex2(fmaf(s[c0], c2, -lse_r));
-          float p1 = ex2(fmaf(s[c0 + 1], c2, -lse_r));
-          p0 = c0 <= lim_j ? p0 : 0.f;
-          p1 = c0 + 1 <= lim_j ? p1 : 0.f;
-          packed[i] = pack_half2(p0 * (dp[c0] - delta_r), p1 * (dp[c0 + 1] - delta_r));
+          // P = 2^(s*scale*log2e - lse2) in fp16x2, dS = P * (dP - Delta)
+          const uint32_t p = ex2_h2(h2_from_f2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
+          const uint32_t d = h2_from_f2(fadd2(f2pack(dp[c0], dp[c0 + 1]), ndelta2));
+          packed[i] = hmul2(p, d);
         }
         tmem_st16(tS + cc * 16, packed);
       }
@@ -328,6 +334,322 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D <= 64: 128-key tiles.  S = Q K^T and dP = dO V^T become N = 128 MMAs (full
+// tensor rate; N = 64 runs at ~70%).  One CTA owns one 128-row query tile;
+// both warpgroups work on every key tile, warpgroup w on key columns
+// [64w, 64w+64), and S is double-buffered in TMEM so the tensor core computes
+// S of tile j+2 and dP of tile j+1 while the warpgroups exponentiate tile j+1.
+// TMEM: S buffers [0,128) and [128,256), dP [256,384), dQ [384, 384+D).
+// Warpgroup w writes dS into its S buffer's columns [64w, 64w+32), inside the
+// range it read.
+namespace bdqw {
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per tile
+constexpr int NUM_THREADS = 384;
+constexpr int POLY_MASK = 4;  // pairs (i & 7) < 4 use the FMA-pipe exp2: half off MUFU
+
+template <int D>
+struct Cfg {
+  using G = TileGeom<D>;
+  static constexpr int NST = 4;
+  static constexpr int Q_TILE_BYTES = BM * D * 2;
+  static constexpr int KV_TILE_BYTES = BN * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + Q_TILE_BYTES;
+  static constexpr int OFF_K = OFF_DO + Q_TILE_BYTES;      // NST stages
+  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;  // NST stages
+  static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
+  // q_full, kv_full[NST], kv_empty[NST], s_full[2], dp_full, ds_ready[2], dq_full, mma_done
+  static constexpr int NUM_BARS = 1 + 2 * NST + 2 + 1 + 2 + 1 + 1;
+  static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
+  static constexpr int OFF_MISC = OFF_CTL + 16;
+  static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DP_COL = 256;
+  static constexpr int DQ_COL = 384;
+  static_assert(D <= 64, "wide dQ path is for D <= 64");
+};
+}  // namespace bdqw
+
+template <int D>
+__global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
+    fa_bwd_dq_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                          const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                          const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
+                          void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh,
+                          const long long dq_sn, const int accumulate_fp32) {
+  using namespace bdqw;
+  using C = Cfg<D>;
+  using G = TileGeom<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_saddr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
+  const uint32_t sbase = smem_u32(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::NST;
+  uint64_t* s_full = kv_empty + C::NST;
+  uint64_t* dp_full = s_full + 2;
+  uint64_t* ds_ready = dp_full + 1;  // per S buffer
+  uint64_t* dq_full = ds_ready + 2;
+  uint64_t* mma_done = dq_full + 1;
+  CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
+  volatile CtaCtl* ctl = ctl_w;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+
+  const int warp = int(warp_id());
+  const int lane = int(lane_id());
+
+  const int BH = shp.B * shp.Hq;
+  const int n_qt = (shp.Nq + BM - 1) / BM;
+  const int qt = n_qt - 1 - int(blockIdx.x) / BH;  // heavy (late) query tiles first
+  const int bh = int(blockIdx.x) % BH;
+  const int b = bh / shp.Hq;
+  const int h = bh % shp.Hq;
+  const int kvh = h / (shp.Hq / shp.Hkv);
+  const int row0 = qt * BM;
+  const int n_kv = kv_tiles_for_rows(shp, row0, BM, BN);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_full + 1, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_ready, 256);
+    mbar_init(ds_ready + 1, 256);
+    mbar_init(dq_full, 1);
+    mbar_init(mma_done, 1);
+    ctl_w->abort = 0;
+    ctl_w->status = shp.status;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =================== TMA producer ===================
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_do);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_TILE_BYTES);
+      for (int bx = 0; bx < G::NBOX; ++bx) {
+        tma_load_4d(smem + C::OFF_Q + bx * BM * G::SW, &tmap_q, q_full, bx * G::BOX, row0, h, b);
+        tma_load_4d(smem + C::OFF_DO + bx * BM * G::SW, &tmap_do, q_full, bx * G::BOX, row0, h, b);
+      }
+      int n_iss = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % C::NST;
+        const uint32_t u = uint32_t(j / C::NST);
+        if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, 131)) break;
+        mbar_arrive_expect_tx(kv_full + s, 2 * C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx) {
+          tma_load_4d(smem + C::OFF_K + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_k, kv_full + s,
+                      bx * G::BOX, j * BN, kvh, b);
+          tma_load_4d(smem + C::OFF_V + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_v, kv_full + s,
+                      bx * G::BOX, j * BN, kvh, b);
+        }
+        ++n_iss;
+      }
+      mbar_wait_drain(q_full, 0, ctl, 132);
+      for (int j = (n_iss > C::NST ? n_iss - C::NST : 0); j < n_iss; ++j)
+        mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 133);
+    }
+  } else if (warp == 1) {
+    // =================== tcgen05 MMA issuer ===================
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
+      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1);
+      const uint32_t q_s = sbase + C::OFF_Q;
+      const uint32_t do_s = sbase + C::OFF_DO;
+      auto k_tile = [&](int j) { return sbase + C::OFF_K + (j % C::NST) * C::KV_TILE_BYTES; };
+      auto v_tile = [&](int j) { return sbase + C::OFF_V + (j % C::NST) * C::KV_TILE_BYTES; };
+      auto wait_kv = [&](int j, int site) {
+        return mbar_wait(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, site);
+      };
+      auto issue_s = [&](int j) {
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + (j & 1) * 128, desc_k_major<D, BM>(q_s, ks), desc_k_major<D, BN>(k_tile(j), ks), IDESC_S,
+                  ks > 0);
+        umma_commit(s_full + (j & 1));
+      };
+      auto issue_dp = [&](int j) {
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + C::DP_COL, desc_k_major<D, BM>(do_s, ks), desc_k_major<D, BN>(v_tile(j), ks), IDESC_S,
+                  ks > 0);
+        umma_commit(dp_full);
+      };
+      auto a_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
+      bool ok = mbar_wait(q_full, 0, ctl, 140) && wait_kv(0, 141);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
+        if (n_kv > 1) {
+          ok = wait_kv(1, 142);
+          if (ok) {
+            tc_fence_after();
+            issue_s(1);
+          }
+        }
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (!mbar_wait(ds_ready + (j & 1), uint32_t(j >> 1) & 1, ctl, 143)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_ts(tmem + C::DQ_COL, tmem + (j & 1) * 128 + a_col(ks), desc_mn_major<D, BN>(k_tile(j), ks),
+                  IDESC_DQ, (j > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(kv_empty + j % C::NST);
+        if (j + 1 < n_kv) issue_dp(j + 1);  // its stage was waited for before S(j+1)
+        if (j + 2 < n_kv) {
+          if (!wait_kv(j + 2, 144)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(j + 2);
+        }
+      }
+      if (ok) umma_commit(dq_full);
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, ctl, 145);
+    }
+  } else if (warp >= 4) {
+    // =================== dS warpgroups ===================
+    const int w = (warp - 4) / 4;  // key-column half of every tile
+    const int wq = warp & 3;
+    const int r = row0 + wq * 32 + lane;
+    int lim = shp.Nk - 1;
+    if (shp.causal) {
+      const long long c = (long long)r + shp.q_off - shp.k_off;
+      lim = c < lim ? int(c) : lim;
+    }
+    const bool row_ok = r < shp.Nq;
+    float lse_r = INFINITY, delta_r = 0.f;
+    if (row_ok) {
+      const float x = lse[(long long)bh * shp.Nq + r];
+      lse_r = x == -INFINITY ? INFINITY : x;
+      delta_r = delta[(long long)bh * shp.Nq + r];
+    }
+    const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
+    const uint64_t c2x2 = f2pack(shp.scale_log2, shp.scale_log2);
+    const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
+    const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait_warp(s_full + (j & 1), uint32_t(j >> 1) & 1, ctl, 150 + w)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tS = lane_base + uint32_t((j & 1) * 128 + 64 * w);
+      float sv[64];
+      tmem_ld64(tS, sv);
+      const int lim_j = lim - j * BN - 64 * w;  // last visible column of this half
+      if (lim_j < 63) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) sv[c] = c <= lim_j ? sv[c] : -INFINITY;
+      }
+      uint32_t pk_p[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t x = ffma2(f2pack(sv[2 * i], sv[2 * i + 1]), c2x2, nlse2);
+        pk_p[i] = h2_from_f2((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
+      }
+      if (!mbar_wait_warp(dp_full, uint32_t(j) & 1, ctl, 152 + w)) { ok = false; break; }
+      tc_fence_after();
+      float dp[64];
+      tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
+      uint32_t pk_ds[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        pk_ds[i] = hmul2(pk_p[i], h2_from_f2(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+      tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+      tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(ds_ready + (j & 1));
+    }
+    // ---- epilogue: warpgroup w stores dQ columns [w*D/2, (w+1)*D/2) ----
+    if (ok && n_kv > 0) ok = mbar_wait_warp(dq_full, 0, ctl, 154 + w);
+    if (ok) {
+      if (n_kv > 0) tc_fence_after();
+      const float sc = shp.scale;
+      constexpr int HALF = D / 2;
+      float g[HALF];
+      if (n_kv > 0) {
+        if constexpr (HALF == 32) {
+          tmem_ld32(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[32]>(&g[0]));
+        } else {
+          tmem_ld16(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[16]>(&g[0]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < HALF; ++i) g[i] = 0.f;
+      }
+      if (row_ok) {
+        const long long off = (long long)b * dq_sb + (long long)h * dq_sh + (long long)r * dq_sn + w * HALF;
+        if (accumulate_fp32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
+#pragma unroll
+          for (int v4 = 0; v4 < HALF / 4; ++v4) {
+            float4 x = dst[v4];
+            x.x += g[v4 * 4 + 0] * sc;
+            x.y += g[v4 * 4 + 1] * sc;
+            x.z += g[v4 * 4 + 2] * sc;
+            x.w += g[v4 * 4 + 3] * sc;
+            dst[v4] = x;
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(dq_out) + off);
+#pragma unroll
+          for (int v8 = 0; v8 < HALF / 8; ++v8) {
+            uint4 pk;
+            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
+            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
+            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
+            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            dst[v8] = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch_bwd_dq_wide_t(const BwdArgs& a) {
+  using C = bdqw::Cfg<D>;
+  auto kern = fa_bwd_dq_wide_kernel<D>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
+  dim3 grid(unsigned(n_qt * a.shape.B * a.shape.Hq));
+  kern<<<grid, bdqw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape,
+                                                             a.lse, a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
+                                                             a.accumulate_fp32);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 template <int D>
 int launch_bwd_dq_t(const BwdArgs& a) {
   using C = bdq::Cfg<D>;
@@ -344,8 +666,8 @@ int launch_bwd_dq_t(const BwdArgs& a) {
 
 int launch_bwd_dq(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return launch_bwd_dq_t<32>(a);
-    case 64: return launch_bwd_dq_t<64>(a);
+    case 32: return launch_bwd_dq_wide_t<32>(a);
+    case 64: return launch_bwd_dq_wide_t<64>(a);
     case 128: return launch_bwd_dq_t<128>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }

@@ -154,8 +154,9 @@ extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void
   BwdArgs a;
   if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dq_cfg::BM))) return rc;
   if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dq_cfg::BM))) return rc;
-  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dq_cfg::BN))) return rc;
-  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dq_cfg::BN))) return rc;
+  const int bn = D <= 64 ? dq_cfg::BN_WIDE : dq_cfg::BN;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, bn))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, bn))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
   a.lse = lse;
   a.delta = delta;
@@ -184,8 +185,9 @@ extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const vo
   const int eb = accumulate_fp32 ? 4 : 2;
   if (!out_strides_ok(dk, dk_strides, eb) || !out_strides_ok(dv, dv_strides, eb)) return FA_ERR_MISALIGNED;
   BwdArgs a;
-  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dkdv_cfg::BQ))) return rc;
-  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dkdv_cfg::BQ))) return rc;
+  const int bq = D <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, bq))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);

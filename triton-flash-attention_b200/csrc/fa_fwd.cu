@@ -15,6 +15,10 @@
 //    the base-2 domain (exp2 with scale * log2(e) folded in, as
 //    attention.py:68-74), write P back to TMEM and rescale O in TMEM when the
 //    running maximum grows by more than 2^8 (lazy rescaling);
+//  * the softmax arithmetic is packed: a 3-input max tree and fma.rn.f32x2
+//    for s * scale*log2(e) - m; the exponentials are split between the MUFU
+//    unit (ex2.approx, 16 per clock per SM) and a polynomial on the FMA pipe
+//    (3 of every 8 pairs), which together beat the MUFU rate alone;
 //  * the two tiles ping-pong: while one warpgroup turns S into P, the tensor
 //    core runs the other tile's GEMMs.
 // TMEM: S_0 cols [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [256+D,256+2D).
@@ -30,6 +34,7 @@ constexpr int BN = 128;  // keys per K/V tile
 constexpr int QT = 2;    // query tiles per CTA
 constexpr int NUM_THREADS = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
+constexpr int POLY_MASK = 3;               // pairs (i & 7) < 3 use the FMA-pipe exp2
 
 template <int D>
 struct Cfg {
@@ -40,6 +45,7 @@ struct Cfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QT * Q_TILE_BYTES;
   static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;
+  static constexpr int OW = D;  // O columns in TMEM
   static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
   // barriers: q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
   //           s_full[QT], p_ready[QT], o_full[QT], mma_done
@@ -53,7 +59,7 @@ struct Cfg {
   static constexpr int S_COL0 = 0;
   static constexpr int O_COL0 = QT * BN;
   static constexpr int TMEM_COLS = 512;
-  static_assert(O_COL0 + QT * D <= TMEM_COLS, "TMEM budget");
+  static_assert(O_COL0 + QT * OW <= TMEM_COLS, "TMEM budget");
 };
 
 struct Smem {
@@ -189,7 +195,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     // =================== tcgen05 MMA issuer ===================
     if (lane == 0 && n_max > 0) {
       constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
-      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, D, 0, 1);
+      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, C::OW, 0, 1);
       const uint32_t q_s = sbase + C::OFF_Q;
       const uint32_t k_s = sbase + C::OFF_K;
       const uint32_t v_s = sbase + C::OFF_V;
@@ -204,10 +210,13 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t vb = v_s + (j % C::NST) * C::KV_TILE_BYTES;
+        // the D columns of V span NBOX boxes BN*SW bytes apart (LBO)
+        const uint32_t lbo = uint32_t(BN * G::SW);
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
-          umma_ts(tmem + C::O_COL0 + t * D, tmem + C::S_COL0 + t * BN + ks * 8, desc_mn_major<D, BN>(vb, ks),
-                  IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_ts(tmem + C::O_COL0 + t * C::OW, tmem + C::S_COL0 + t * BN + ks * 8,
+                  smem_desc<G::SW>(vb + uint32_t(ks) * 16u * G::SW, lbo, 8u * G::SW), IDESC_PV,
+                  (j > 0 || ks > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(sm.q_full, 0, ctl, 10) && mbar_wait(sm.k_full, 0, ctl, 11);
       if (ok) {
@@ -258,8 +267,9 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       lim = c < lim ? int(c) : lim;  // may be negative: no visible key
     }
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::S_COL0 + t * BN));
-    const uint32_t tO = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::O_COL0 + t * D));
+    const uint32_t tO = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::O_COL0 + t * C::OW));
     const float c2 = shp.scale_log2;
+    const uint64_t c2x2 = f2pack(c2, c2);
     float m = -INFINITY;  // running exponent base (scaled log2 units)
     float l = 0.f;        // running row sum of exp2(s * c2 - m)
     bool ok = true;
@@ -274,9 +284,16 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
       }
-      float mx = s[0];
+      // row max: 8 independent 3-input max chains, then a short tree
+      float a8[8];
 #pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      for (int k = 0; k < 8; ++k) {
+        float acc = fmax3(s[k * 16], s[k * 16 + 1], s[k * 16 + 2]);
+#pragma unroll
+        for (int i = 3; i < 15; i += 2) acc = fmax3(acc, s[k * 16 + i], s[k * 16 + i + 1]);
+        a8[k] = fmaxf(acc, s[k * 16 + 15]);
+      }
+      const float mx = fmax3(fmax3(a8[0], a8[1], a8[2]), fmax3(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
       const float m_tile = mx * c2;
       bool rescale = false;
       float m_new = m;
@@ -286,29 +303,43 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       const float alpha = rescale ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 on the first tile
       const float base = m_new == -INFINITY ? 0.f : m_new;
-      float rowsum = 0.f;
+      const uint64_t nb2 = f2pack(-base, -base);
+      uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(s[cc * 32 + 2 * i], c2, -base));
-          const float p1 = ex2(fmaf(s[cc * 32 + 2 * i + 1], c2, -base));
-          rowsum += p0 + p1;
-          packed[i] = pack_half2(p0, p1);
+          const int c0 = cc * 32 + 2 * i;
+          const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
+          // 3 of every 8 pairs on the FMA pipe, the rest on MUFU
+          const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
+          packed[i] = h2_from_f2(e);
+          sum2[i & 3] = fadd2(sum2[i & 3], e);
         }
         tmem_st16(tS + cc * 16, packed);
       }
-      l = l * alpha + rowsum;
+      {
+        float s0, s1, s2, s3, s4, s5, s6, s7;
+        f2unpack(sum2[0], s0, s1);
+        f2unpack(sum2[1], s2, s3);
+        f2unpack(sum2[2], s4, s5);
+        f2unpack(sum2[3], s6, s7);
+        l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)));
+      }
       m = m_new;
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        // O *= alpha
 #pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          float o[32];
-          tmem_ld32(tO + cc * 32, o);
+        for (int cc = 0; cc < C::OW / 16; ++cc) {
+          float o[16];
+          tmem_ld16(tO + cc * 16, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + cc * 32, o);
+          for (int i = 0; i < 16; ++i) o[i] *= alpha;
+          uint32_t u[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i]);
+          tmem_st16(tO + cc * 16, u);
         }
       }
       tmem_st_wait();
@@ -319,9 +350,9 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     if (ok && nt > 0) ok = mbar_wait_warp(sm.o_full + t, 0, ctl, 22 + t);
     if (ok) {
       const bool row_ok = r < shp.Nq;
+      if (nt > 0) tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       __half* orow = o_ptr + (long long)b * o_sb + (long long)h * o_sh + (long long)r * o_sn;
-      if (nt > 0) tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];

@@ -47,11 +47,13 @@ int launch_merge_partial(float* o_acc, float* lse_acc, const __half* o_part, con
 // Query-tile / key-tile sizes the host needs for TMA box shapes.
 namespace dq_cfg {
 constexpr int BM = 128;  // query rows per tile
-constexpr int BN = 64;   // keys per tile
+constexpr int BN = 64;   // keys per tile (D = 128)
+constexpr int BN_WIDE = 128;  // keys per tile (D <= 64)
 }  // namespace dq_cfg
 namespace dkdv_cfg {
 constexpr int BM = 128;  // key rows per tile (the MMA M dimension)
-constexpr int BQ = 64;   // query rows per tile
+constexpr int BQ = 64;   // query rows per tile (D = 128)
+constexpr int BQ_WIDE = 128;  // query rows per item (D <= 64)
 }  // namespace dkdv_cfg
 
 }  // namespace fa

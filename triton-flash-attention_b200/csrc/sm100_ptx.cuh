@@ -116,6 +116,12 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA / tcgen05.mma) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tensor maps built on the host with cuTensorMapEncodeTiled)
 // ---------------------------------------------------------------------------
@@ -232,16 +238,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
       : "memory");
 }
 
-// Two 32-column loads (64 columns) with a single wait.
+// 64 consecutive 32-bit columns in one load instruction, with the wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&r)[64]) {
   uint32_t* u = reinterpret_cast<uint32_t*>(r);
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
         "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]),
@@ -251,7 +256,7 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&r)[64]) {
         "=r"(u[40]), "=r"(u[41]), "=r"(u[42]), "=r"(u[43]), "=r"(u[44]), "=r"(u[45]), "=r"(u[46]), "=r"(u[47]),
         "=r"(u[48]), "=r"(u[49]), "=r"(u[50]), "=r"(u[51]), "=r"(u[52]), "=r"(u[53]), "=r"(u[54]), "=r"(u[55]),
         "=r"(u[56]), "=r"(u[57]), "=r"(u[58]), "=r"(u[59]), "=r"(u[60]), "=r"(u[61]), "=r"(u[62]), "=r"(u[63])
-      : "r"(taddr), "r"(taddr + 32u)
+      : "r"(taddr)
       : "memory");
 }
 
@@ -299,6 +304,109 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// ---- packed arithmetic (sm_100 f32x2 / f16x2) ----
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// fp32 pair -> fp16x2 (round to nearest), lo in bits 0-15
+__device__ __forceinline__ uint32_t h2_from_f2(uint64_t v) {
+  float lo, hi;
+  f2unpack(v, lo, hi);
+  return pack_half2(lo, hi);
+}
+// 2^x on both halves of an fp16x2 (one MUFU operation for two values)
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// fp16x2 -> fp32 pair
+__device__ __forceinline__ uint64_t f2_from_h2(uint32_t h) {
+  float lo, hi;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(h));
+  return f2pack(lo, hi);
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for both floats of a pair on the FMA/ALU pipes, offloading the MUFU
+// unit: x is clamped to >= -126, split as x = j + f with j = round(x) (the
+// float add of 1.5*2^23 leaves j in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f comes from a degree-3 polynomial fitted here for
+// minimum relative error (max 1.0e-4, below fp16's 4.9e-4 half-ulp), and
+// 2^j is applied by adding j to the exponent field.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC1 = 0.69328295f, kC2 = 0.24221102f, kC3 = 0.05500883f;
+  float xl, xh;
+  f2unpack(x, xl, xh);
+  xl = fmaxf(xl, -126.f);
+  xh = fmaxf(xh, -126.f);
+  const uint64_t xc = f2pack(xl, xh);
+  const uint64_t t = fadd2(xc, f2pack(kRound, kRound));
+  const uint64_t j = fadd2(t, f2pack(-kRound, -kRound));
+  const uint64_t f = ffma2(j, f2pack(-1.f, -1.f), xc);
+  uint64_t p = ffma2(f2pack(kC3, kC3), f, f2pack(kC2, kC2));
+  p = ffma2(p, f, f2pack(kC1, kC1));
+  p = ffma2(p, f, f2pack(1.f, 1.f));
+  float pl, ph, tl, th;
+  f2unpack(p, pl, ph);
+  f2unpack(t, tl, th);
+  const uint32_t rl = __float_as_uint(pl) + (__float_as_uint(tl) << 23);
+  const uint32_t rh = __float_as_uint(ph) + (__float_as_uint(th) << 23);
+  return f2pack(__uint_as_float(rl), __uint_as_float(rh));
+}
+
+// 2^x for a pair on the MUFU unit.
+__device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x) {
+  float a, b;
+  f2unpack(x, a, b);
+  return f2pack(ex2(a), ex2(b));
+}
+
+// 16 consecutive 32-bit columns -> 16 registers, with the wait.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(r);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+        "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15])
+      : "r"(taddr)
+      : "memory");
 }
 
 }  // namespace fa
