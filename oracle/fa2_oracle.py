@@ -329,3 +329,34 @@ def sdpa_head_fwd_bwd_fp32(q, k, v, do, *, causal: bool, scale: float):
     dk = (ds.T @ q) * np.float32(scale)
     dv = p.T @ do
     return o, dq, dk, dv
+
+
+def attention_block_grads(q, k, v, do, lse2, delta, *, causal: bool, scale: float,
+                          q_offset: int = 0, k_offset: int = 0):
+    """Gradient contributions of one key/value block given the GLOBAL
+    base-2 LSE and Delta of the queries (float64): P = 2^(scale*log2(e)*s -
+    lse2) on the block's visible keys, dS = P (dO V^T - Delta),
+    dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO (dK/dV summed over each
+    K/V head's query group).  Summing these over all blocks gives the full
+    gradient -- the decomposition a ring backward relies on."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    do = np.asarray(do, np.float64)
+    lse2 = np.asarray(lse2, np.float64)
+    delta = np.asarray(delta, np.float64)
+    b, hq, nq, d = q.shape
+    hkv, nk = k.shape[1], k.shape[2]
+    ke = _expand_kv(k, hq)
+    ve = _expand_kv(v, hq)
+    s2 = np.einsum("bhqd,bhkd->bhqk", q, ke) * scale * INV_LN2
+    with np.errstate(invalid="ignore"):
+        p = np.exp2(s2 - np.where(np.isfinite(lse2), lse2, np.inf)[..., None])
+    if causal:
+        p = np.where(causal_mask(nq, nk, q_offset, k_offset)[None, None], p, 0.0)
+    dp = np.einsum("bhqd,bhkd->bhqk", do, ve)
+    ds = p * (dp - delta[..., None])
+    dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
+    dke = np.einsum("bhqk,bhqd->bhkd", ds, q) * scale
+    dve = np.einsum("bhqk,bhqd->bhkd", p, do)
+    return dq, _reduce_kv(dke, hkv), _reduce_kv(dve, hkv)

@@ -105,7 +105,7 @@ def attention_forward(q, k, v, causal: bool, softmax_scale: float, *, q_offset: 
     log-sum-exp per query row in the scaled domain (attention.py:230)."""
     b, hq, nq, d = q.shape
     hkv, nk = k.shape[1], k.shape[2]
-    o = torch.empty_like(q)
+    o = torch.empty(q.shape, device=q.device, dtype=q.dtype)  # contiguous even for strided q
     lse = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
     lib = _abi.lib()
     rc = lib.fa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
@@ -138,7 +138,7 @@ def attention_backward_dq(q, k, v, do, lse, delta, causal: bool, softmax_scale: 
         if dq.dtype != torch.float32 or dq.shape != q.shape:
             raise ValueError("dq accumulator must be an fp32 tensor shaped like q")
     else:
-        dq = torch.empty_like(q)
+        dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     rc = _abi.lib().fa_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
                               lse.data_ptr(), delta.data_ptr(), dq.data_ptr(),
                               b, hq, hkv, nq, nk, d,
@@ -163,8 +163,8 @@ def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale
             if t.dtype != torch.float32 or t.shape != k.shape:
                 raise ValueError(f"{name} accumulator must be an fp32 tensor shaped like k")
     else:
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
+        dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+        dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
     rc = _abi.lib().fa_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
                                 lse.data_ptr(), delta.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                 b, hq, hkv, nq, nk, d,
