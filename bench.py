@@ -306,6 +306,71 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ ring workload (C5)
+RING_B, RING_HQ, RING_HKV, RING_N, RING_D = 1, 32, 8, 131072, 128
+
+
+def run_ring(args) -> None:
+    """C5: long-context GQA causal fwd+bwd with ring context parallelism over
+    the ranks (strong scaling: the global sequence is fixed and split zig-zag
+    into 2P chunks).  Each rank generates its own chunks from per-chunk seeds,
+    so no rank materialises the whole sequence."""
+    import torch
+    import torch.distributed as dist
+
+    import triton_flash_attention_b200 as fa
+    import triton_flash_attention_b200.ring as ring
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = args.ring_seq or RING_N
+    c = n // (2 * world)
+
+    def chunked(heads, tag):
+        parts = []
+        for cid in (rank, 2 * world - 1 - rank):
+            g = torch.Generator(device=dev).manual_seed(100003 * tag + cid)
+            parts.append(torch.randn(RING_B, heads, c, RING_D, device=dev, dtype=torch.float16, generator=g))
+        return torch.cat(parts, dim=2)
+
+    q, k, v, do = chunked(RING_HQ, 1), chunked(RING_HKV, 2), chunked(RING_HKV, 3), chunked(RING_HQ, 4)
+    scale = RING_D ** -0.5
+    group = dist.group.WORLD if world > 1 else None
+
+    def step():
+        o, lse = ring.ring_forward(q, k, v, causal=True, scale=scale, group=group)
+        ring.ring_backward(q, k, v, o, lse, do, causal=True, scale=scale, group=group)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = barrier_max(world, start.elapsed_time(end) / args.steps)
+    fl = fa.attention_flops(batch=RING_B, query_heads=RING_HQ, sequence=n, head_dim=RING_D, causal=True,
+                            mode="forward-backward")
+    if rank == 0:
+        print(json.dumps({
+            "metric": "causal fp16 fwd+bwd TFLOP/s, ring context parallel (C5)", "value": round(fl / ms / 1e9, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16", "data": "synthetic: seeded N(0,1) per zig-zag chunk",
+            "config": {"workload": "C5: GQA causal B1 Hq32 Hkv8 D128 ring context parallel", "seq_len": n,
+                       "chunk": c, "parallelism": f"ring-cp x{world} (NCCL P2P)"},
+            "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
@@ -368,11 +433,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c2", "ring"], default="c2",
+                    help="c2: the metric's configuration (default); ring: C5 ring context parallelism")
+    ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "ring":
+        run_ring(args)
     else:
         run_ours(args)
 

@@ -293,8 +293,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         const float4 nl = l4[c4];
         const float4 nd = d4[c4];
         const int c = c4 * 4;
-        const uint32_t p01 = ex2_h2(h2_from_f2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
-        const uint32_t p23 = ex2_h2(h2_from_f2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
+        const uint32_t p01 = h2_from_f2(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
+        const uint32_t p23 = h2_from_f2(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
         const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
         const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
         pk_p[c4 * 2] = p01;

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
         for (int i = 0; i < 16; ++i) {
           const int c0 = cc * 32 + 2 * i;
           // P = 2^(s*scale*log2e - lse2) in fp16x2, dS = P * (dP - Delta)
-          const uint32_t p = ex2_h2(h2_from_f2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
+          const uint32_t p = h2_from_f2(exp2_mufu2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
           const uint32_t d = h2_from_f2(fadd2(f2pack(dp[c0], dp[c0 + 1]), ndelta2));
           packed[i] = hmul2(p, d);
         }
