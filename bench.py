@@ -42,7 +42,7 @@ if ROOT not in sys.path:
 B, H, N, D = 4, 16, 4096, 64
 CAUSAL = True
 WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
-DKDV_TRAFFIC_BYTES = 207_236_608 + 41_714_432
+DKDV_TRAFFIC_BYTES = 190_924_032 + 39_982_336
 
 
 def flops_step() -> int:
@@ -269,7 +269,7 @@ def run_ours(args) -> None:
                                       mode="forward")
     achieved = kv_flops / (kv_ms * 1e-3) / 1e12
     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch of
-    # the dK/dV kernel (profiles/c2_kernels_v1.md)
+    # the dK/dV kernel (profiles/c2_kernels.md)
     traffic = DKDV_TRAFFIC_BYTES
     if rank == 0:
         line = {
@@ -291,7 +291,7 @@ def run_ours(args) -> None:
             "pct_of_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
-            "roofline": {"kernel": "fa_bwd_dkdv_kernel<64>", "bound": "tensor", "achieved": round(achieved, 2),
+            "roofline": {"kernel": "fa_bwd_dkdv_wide_kernel<64>", "bound": "tensor", "achieved": round(achieved, 2),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                          "peak_source": peaks["source"], "launch_ms": round(kv_ms, 4)},
