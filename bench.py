@@ -426,12 +426,68 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args) -> None:
+    """Informational: the reference's own Triton kernel (backend="triton"),
+    unmodified, from its pip install in baseline/_ref, timed on this GPU at C2
+    beside this build's kernels, with both implementations' max-abs errors
+    against fp32 math on two heads.  Not the driver's reference arm (that is
+    the CPU path, --impl reference)."""
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "triton_flash_attention")):
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "baseline/_ref is not installed"}))
+        return
+    sys.path.insert(0, ref_dir)
+    import triton_flash_attention as ref
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    q, k, v, do = (torch.randn(B, H, N, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4))
+    fl = flops_step()
+    out = {}
+    for name, sdpa, kw in (("reference_triton", ref.scaled_dot_product_attention, {"backend": "triton"}),
+                           ("b200", fa.scaled_dot_product_attention, {})):
+        qc, kc, vc = (t.clone().requires_grad_() for t in (q, k, v))
+
+        def step():
+            o = sdpa(qc, kc, vc, is_causal=CAUSAL, **kw)
+            o.backward(do)
+
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1) / args.steps
+        qs, ks, vs = (t[:1, :2].detach().clone().requires_grad_() for t in (q, k, v))
+        o = sdpa(qs, ks, vs, is_causal=CAUSAL, **kw)
+        grads = torch.autograd.grad(o, (qs, ks, vs), do[:1, :2])
+        q32, k32, v32 = (t[:1, :2].detach().float().requires_grad_() for t in (q, k, v))
+        o32 = torch.nn.functional.scaled_dot_product_attention(q32, k32, v32, is_causal=CAUSAL)
+        g32 = torch.autograd.grad(o32, (q32, k32, v32), do[:1, :2].float())
+        errs = [float((o.float() - o32).abs().max())] + [float((a.float() - b).abs().max()) for a, b in zip(grads, g32)]
+        out[name] = {"ms_per_step": round(ms, 4), "tflops": round(fl / ms / 1e9, 2),
+                     "max_abs_err_vs_fp32": dict(zip(("o", "dq", "dk", "dv"), (round(e, 6) for e in errs)))}
+    print(json.dumps({"impl": "reference-gpu", "metric": "causal fp16 fwd+bwd TFLOP/s, B4 H16 N4096 D64",
+                      "unit": "TFLOP/s", "steps": args.steps, "results": out,
+                      "speedup_b200_over_reference_triton": round(out["reference_triton"]["ms_per_step"]
+                                                                  / out["b200"]["ms_per_step"], 3)}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["c2", "ring"], default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism")
@@ -441,6 +497,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args)
     elif args.workload == "ring":
         run_ring(args)
     else:

@@ -198,31 +198,35 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1);
       const uint32_t k_s = sbase + C::OFF_K;
       const uint32_t v_s = sbase + C::OFF_V;
+      const SDesc kd = desc_k_base<D>(k_s);
+      const SDesc vd = desc_k_base<D>(v_s);
       auto issue_st = [&](int w, int it) {
         const int s = it % C::NST;
-        const uint32_t qb = sbase + C::OFF_Q + s * C::Q_TILE_BYTES;
-        const uint32_t db = sbase + C::OFF_DO + s * C::Q_TILE_BYTES;
+        const SDesc qd = desc_k_base<D>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
+        const SDesc dd = desc_k_base<D>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + w * 128, desc_k_major<D, BM>(k_s, ks), desc_k_major<D, BQ>(qb, ks), IDESC_ST, ks > 0);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + w * 128 + 64, desc_k_major<D, BM>(v_s, ks), desc_k_major<D, BQ>(db, ks), IDESC_ST,
+          umma_ss(tmem + w * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)), IDESC_ST,
                   ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + w * 128 + 64, sdesc_at(vd, k_major_off<D, BM>(ks)), sdesc_at(dd, k_major_off<D, BQ>(ks)),
+                  IDESC_ST, ks > 0);
         umma_commit(st_full + w);
       };
       auto issue_grad = [&](int w, int it) {
         const int s = it % C::NST;
-        const uint32_t qb = sbase + C::OFF_Q + s * C::Q_TILE_BYTES;
-        const uint32_t db = sbase + C::OFF_DO + s * C::Q_TILE_BYTES;
+        const SDesc qd = desc_mn_base<D, BQ>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
+        const SDesc dd = desc_mn_base<D, BQ>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
+        const uint32_t acc0 = it > 0 ? 1u : 0u;
+        umma_ts(tmem + C::DV_COL, tmem + w * 128, sdesc_at(dd, 0), IDESC_G, acc0);
 #pragma unroll
-        for (int ks = 0; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DV_COL, tmem + w * 128 + ks * 8, desc_mn_major<D, BQ>(db, ks), IDESC_G,
-                  (it > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 1; ks < BQ / 16; ++ks)
+          umma_ts(tmem + C::DV_COL, tmem + w * 128 + ks * 8, sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
+        umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64, sdesc_at(qd, 0), IDESC_G, acc0);
 #pragma unroll
-        for (int ks = 0; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64 + ks * 8, desc_mn_major<D, BQ>(qb, ks), IDESC_G,
-                  (it > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 1; ks < BQ / 16; ++ks)
+          umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64 + ks * 8, sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G, 1u);
       };
       bool ok = mbar_wait(kv_full, 0, ctl, 70) && mbar_wait(full, 0, ctl, 71);
       if (ok) {
@@ -370,16 +374,16 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 // D <= 64: 128-query items.  At D <= 64 an N = 64 MMA runs at ~70% of the
 // tensor rate (measured: M128 x N x K16 takes max(N/2, ~45) cycles), so the
 // items here are 128 query rows wide (S^T, dP^T are N = 128 MMAs at full
-// rate).  Both elementwise warpgroups work on every item, warpgroup w on
-// query columns [64w, 64w+64), and S^T is double-buffered in TMEM so that the
-// tensor core computes S^T of item i+2 and dP^T of item i+1 while the
-// warpgroups exponentiate item i+1.  P^T is published (for dV) before dS^T
-// (for dK), so the dV GEMM starts as soon as the exponentials are done.
+// rate).  The two elementwise warpgroups are specialised by phase so that
+// consecutive items overlap: warpgroup 0 turns S^T into P^T (the exponentials)
+// for whole items, warpgroup 1 turns dP^T and P^T into dS^T, one item behind.
+// S^T is double-buffered in TMEM; the MMA thread issues dV(i) as soon as P^T(i)
+// is published and dK(i), dP^T(i+1), S^T(i+2) once dS^T(i) is.
 // TMEM: S^T buffers at [0,128) and [128,256), dP^T at [256,384),
 //       dV at [384, 384+D), dK at [384+D, 384+2D).
-// Warpgroup w writes P^T into its S^T buffer's columns [64w, 64w+32) and
-// dS^T into dP^T's columns [256+64w, 256+64w+32): inside the range it read,
-// so the two warpgroups never race.
+// P^T of query columns [64h, 64h+64) is packed into its S^T buffer's columns
+// [64h, 64h+32), dS^T likewise into dP^T's columns [256+64h, 256+64h+32):
+// each half is written after it was read.
 namespace bkvw {
 constexpr int BM = 128;   // keys per CTA
 constexpr int BQ = 128;   // query rows per item
@@ -437,8 +441,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   uint64_t* s_full = empty + C::NST;
   uint64_t* dp_full = s_full + 2;
   // p_ready is per S^T buffer: phase k of p_ready[b] belongs to item 2k+b, so
-  // it cannot run two phases ahead of the MMA thread (item it+2's S^T is
-  // issued only after the MMA thread consumed item it's P^T).
+  // it cannot run two phases ahead of its waiters (item it+2's S^T is issued
+  // only after dS^T(it) -- and so P^T(it) -- was consumed).
   uint64_t* p_ready = dp_full + 1;
   uint64_t* ds_ready = p_ready + 2;
   uint64_t* acc_full = ds_ready + 1;
@@ -478,9 +482,9 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     mbar_init(s_full, 1);
     mbar_init(s_full + 1, 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_ready, 256);
-    mbar_init(p_ready + 1, 256);
-    mbar_init(ds_ready, 256);
+    mbar_init(p_ready, 128);
+    mbar_init(p_ready + 1, 128);
+    mbar_init(ds_ready, 128);
     mbar_init(acc_full, 1);
     mbar_init(mma_done, 1);
     ctl_w->abort = 0;
@@ -559,19 +563,22 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
       const uint32_t v_s = sbase + C::OFF_V;
       auto q_tile = [&](int it) { return sbase + C::OFF_Q + (it % C::NST) * C::Q_TILE_BYTES; };
       auto do_tile = [&](int it) { return sbase + C::OFF_DO + (it % C::NST) * C::Q_TILE_BYTES; };
+      const SDesc kd = desc_k_base<D>(k_s);
+      const SDesc vd = desc_k_base<D>(v_s);
       auto issue_s = [&](int it) {  // S^T -> buffer it & 1
-        const uint32_t qb = q_tile(it);
+        const SDesc qd = desc_k_base<D>(q_tile(it));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + (it & 1) * 128, desc_k_major<D, BM>(k_s, ks), desc_k_major<D, BQ>(qb, ks), IDESC_ST,
-                  ks > 0);
+          umma_ss(tmem + (it & 1) * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)),
+                  IDESC_ST, ks > 0);
         umma_commit(s_full + (it & 1));
       };
       auto issue_dp = [&](int it) {
-        const uint32_t db = do_tile(it);
+        const SDesc dd = desc_k_base<D>(do_tile(it));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + C::DP_COL, desc_k_major<D, BM>(v_s, ks), desc_k_major<D, BQ>(db, ks), IDESC_ST, ks > 0);
+          umma_ss(tmem + C::DP_COL, sdesc_at(vd, k_major_off<D, BM>(ks)), sdesc_at(dd, k_major_off<D, BQ>(ks)),
+                  IDESC_ST, ks > 0);
         umma_commit(dp_full);
       };
       // A operand (fp16 in TMEM) for query rows [16ks, 16ks+16) of a region
@@ -595,98 +602,120 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         const uint32_t qb = q_tile(it);
         if (!mbar_wait(p_ready + (it & 1), uint32_t(it >> 1) & 1, ctl, 173)) { ok = false; break; }
         tc_fence_after();
+        {
+          const SDesc dd = desc_mn_base<D, BQ>(db);
+          const uint32_t pa = tmem + (it & 1) * 128;
+          umma_ts(tmem + C::DV_COL, pa, sdesc_at(dd, 0), IDESC_G, it > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DV_COL, tmem + (it & 1) * 128 + a_col(ks), desc_mn_major<D, BQ>(db, ks), IDESC_G,
-                  (it > 0 || ks > 0) ? 1u : 0u);
-        // S^T(it+2) reuses buffer it&1 (after dV(it) read P^T from it) and is
-        // queued before the dS^T wait so the tensor core stays busy meanwhile
+          for (int ks = 1; ks < BQ / 16; ++ks)
+            umma_ts(tmem + C::DV_COL, pa + a_col(ks), sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
+        }
+        if (!mbar_wait(ds_ready, uint32_t(it) & 1, ctl, 174)) { ok = false; break; }
+        tc_fence_after();
+        {
+          const SDesc qd = desc_mn_base<D, BQ>(qb);
+          umma_ts(tmem + C::DK_COL, tmem + C::DP_COL, sdesc_at(qd, 0), IDESC_G, it > 0 ? 1u : 0u);
+#pragma unroll
+          for (int ks = 1; ks < BQ / 16; ++ks)
+            umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + a_col(ks), sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G, 1u);
+        }
+        umma_commit(empty + it % C::NST);
+        if (it + 1 < n_items) issue_dp(it + 1);  // its stage was waited for before S^T(it+1)
+        // buffer it&1 is free: dV(it) (issued above) and warpgroup 1 (before
+        // ds_ready) have read P^T(it)
         if (it + 2 < n_items) {
           const int n2 = it + 2;
           if (!mbar_wait(full + n2 % C::NST, uint32_t(n2 / C::NST) & 1, ctl, 175)) { ok = false; break; }
           tc_fence_after();
           issue_s(n2);
         }
-        if (!mbar_wait(ds_ready, uint32_t(it) & 1, ctl, 174)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + a_col(ks), desc_mn_major<D, BQ>(qb, ks), IDESC_G,
-                  (it > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(empty + it % C::NST);
-        if (it + 1 < n_items) issue_dp(it + 1);  // its stage was waited for before S^T(it+1)
       }
       if (ok) umma_commit(acc_full);
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0, ctl, 176);
     }
   } else if (warp >= 4) {
-    // =================== P^T / dS^T warpgroups ===================
-    const int w = (warp - 4) / 4;  // query-column half of every item
+    // =================== P^T (warpgroup 0) / dS^T (warpgroup 1) ===================
+    const int w = (warp - 4) / 4;  // 0: exponentials, 1: dS^T
     const int wq = warp & 3;
     const int rl = wq * 32 + lane;  // key row within the tile
     const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
     const uint64_t c2x2 = f2pack(shp.scale_log2, shp.scale_log2);
-    const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off - 64 * w;
+    const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off;
     bool ok = true;
-    for (int it = 0; it < n_items; ++it) {
-      const int s = it % C::NST;
-      if (!mbar_wait_warp(s_full + (it & 1), uint32_t(it >> 1) & 1, ctl, 180 + w)) { ok = false; break; }
-      // the stage's -lse2/-Delta: its phase completed before S^T was issued
-      if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 182 + w)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tS = lane_base + uint32_t((it & 1) * 128 + 64 * w);
-      float st[64];
-      tmem_ld64(tS, st);
-      const int q0 = (i_start + it % per_head) * BQ;
-      if (shp.causal) {
-        const long long x = cmin_base - q0;
-        const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
-        if (cmin > 0) {
+    if (w == 0) {
+      for (int it = 0; it < n_items; ++it) {
+        const int s = it % C::NST;
+        if (!mbar_wait_warp(s_full + (it & 1), uint32_t(it >> 1) & 1, ctl, 180)) { ok = false; break; }
+        // the stage's -lse2/-Delta: its phase completed before S^T was issued
+        if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 182)) { ok = false; break; }
+        tc_fence_after();
+        const int q0 = (i_start + it % per_head) * BQ;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t tS = lane_base + uint32_t((it & 1) * 128 + 64 * hh);
+          float st[64];
+          tmem_ld64(tS, st);
+          if (shp.causal) {
+            const long long x = cmin_base - q0 - 64 * hh;
+            const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+            if (cmin > 0) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+              for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+            }
+          }
+          const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
+          uint32_t pk_p[32];
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 nl = l4[c4];
+            const int c = c4 * 4;
+            const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
+            const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
+            const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
+            const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
+            pk_p[c4 * 2] = h2_from_f2(e01);
+            pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+          }
+          tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
+          tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
         }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_ready + (it & 1));
       }
-      const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * w);
-      uint32_t pk_p[32];
+    } else {
+      for (int it = 0; it < n_items; ++it) {
+        const int s = it % C::NST;
+        if (!mbar_wait_warp(p_ready + (it & 1), uint32_t(it >> 1) & 1, ctl, 184)) { ok = false; break; }
+        if (!mbar_wait_warp(dp_full, uint32_t(it) & 1, ctl, 185)) { ok = false; break; }
+        if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 183)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * hh);
+          float dpt[64];
+          tmem_ld64(tD, dpt);
+          float pf[32];
+          tmem_ld32(lane_base + uint32_t((it & 1) * 128 + 64 * hh), pf);
+          const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * hh);
+          uint32_t pk_ds[32];
 #pragma unroll
-      for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 nl = l4[c4];
-        const int c = c4 * 4;
-        const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
-        const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
-        const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
-        const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
-        pk_p[c4 * 2] = h2_from_f2(e01);
-        pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 nd = d4[c4];
+            const int c = c4 * 4;
+            const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+            const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+            pk_ds[c4 * 2] = hmul2(__float_as_uint(pf[c4 * 2]), d01);
+            pk_ds[c4 * 2 + 1] = hmul2(__float_as_uint(pf[c4 * 2 + 1]), d23);
+          }
+          tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+          tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(ds_ready);
       }
-      tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
-      tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_ready + (it & 1));
-      // ---- dS^T = P^T (dP^T - Delta) ----
-      if (!mbar_wait_warp(dp_full, uint32_t(it) & 1, ctl, 184 + w)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * w);
-      float dpt[64];
-      tmem_ld64(tD, dpt);
-      const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * w);
-      uint32_t pk_ds[32];
-#pragma unroll
-      for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 nd = d4[c4];
-        const int c = c4 * 4;
-        const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-        const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-        pk_ds[c4 * 2] = hmul2(pk_p[c4 * 2], d01);
-        pk_ds[c4 * 2 + 1] = hmul2(pk_p[c4 * 2 + 1], d23);
-      }
-      tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
-      tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(ds_ready);
     }
     // ---- epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK ----
     if (ok && n_items > 0) ok = mbar_wait_warp(acc_full, 0, ctl, 186 + w);

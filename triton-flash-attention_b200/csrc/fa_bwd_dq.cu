@@ -176,25 +176,32 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
       const uint32_t do_s = sbase + C::OFF_DO;
       const uint32_t k_s = sbase + C::OFF_K;
       const uint32_t v_s = sbase + C::OFF_V;
+      SDesc qd[QT], dd[QT];
+#pragma unroll
+      for (int t = 0; t < QT; ++t) {
+        qd[t] = desc_k_base<D>(q_s + t * C::Q_TILE_BYTES);
+        dd[t] = desc_k_base<D>(do_s + t * C::Q_TILE_BYTES);
+      }
       auto issue_sdp = [&](int t, int j) {
-        const uint32_t qa = q_s + t * C::Q_TILE_BYTES;
-        const uint32_t da = do_s + t * C::Q_TILE_BYTES;
-        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
-        const uint32_t vb = v_s + (j % C::NST) * C::KV_TILE_BYTES;
+        const SDesc kd = desc_k_base<D>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
+        const SDesc vd = desc_k_base<D>(v_s + (j % C::NST) * C::KV_TILE_BYTES);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + t * 128, desc_k_major<D, BM>(qa, ks), desc_k_major<D, BN>(kb, ks), IDESC_S, ks > 0);
+          umma_ss(tmem + t * 128, sdesc_at(qd[t], k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)),
+                  IDESC_S, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + t * 128 + 64, desc_k_major<D, BM>(da, ks), desc_k_major<D, BN>(vb, ks), IDESC_S, ks > 0);
+          umma_ss(tmem + t * 128 + 64, sdesc_at(dd[t], k_major_off<D, BM>(ks)), sdesc_at(vd, k_major_off<D, BN>(ks)),
+                  IDESC_S, ks > 0);
         umma_commit(s_full + t);
       };
       auto issue_dq = [&](int t, int j) {
-        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
+        const SDesc kd = desc_mn_base<D, BN>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
+        const uint32_t dst = tmem + C::DQ_COL0 + t * D;
+        umma_ts(dst, tmem + t * 128, sdesc_at(kd, 0), IDESC_DQ, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          umma_ts(tmem + C::DQ_COL0 + t * D, tmem + t * 128 + ks * 8, desc_mn_major<D, BN>(kb, ks), IDESC_DQ,
-                  (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 1; ks < BN / 16; ++ks)
+          umma_ts(dst, tmem + t * 128 + ks * 8, sdesc_at(kd, mn_major_off<D>(ks)), IDESC_DQ, 1u);
       };
       bool ok = mbar_wait(q_full, 0, ctl, 40) && mbar_wait(k_full, 0, ctl, 41) && mbar_wait(v_full, 0, ctl, 42);
       if (ok) {
@@ -482,18 +489,22 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       auto wait_kv = [&](int j, int site) {
         return mbar_wait(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, site);
       };
+      const SDesc qd = desc_k_base<D>(q_s);
+      const SDesc dd = desc_k_base<D>(do_s);
       auto issue_s = [&](int j) {
+        const SDesc kd = desc_k_base<D>(k_tile(j));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + (j & 1) * 128, desc_k_major<D, BM>(q_s, ks), desc_k_major<D, BN>(k_tile(j), ks), IDESC_S,
-                  ks > 0);
+          umma_ss(tmem + (j & 1) * 128, sdesc_at(qd, k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)),
+                  IDESC_S, ks > 0);
         umma_commit(s_full + (j & 1));
       };
       auto issue_dp = [&](int j) {
+        const SDesc vd = desc_k_base<D>(v_tile(j));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + C::DP_COL, desc_k_major<D, BM>(do_s, ks), desc_k_major<D, BN>(v_tile(j), ks), IDESC_S,
-                  ks > 0);
+          umma_ss(tmem + C::DP_COL, sdesc_at(dd, k_major_off<D, BM>(ks)), sdesc_at(vd, k_major_off<D, BN>(ks)),
+                  IDESC_S, ks > 0);
         umma_commit(dp_full);
       };
       auto a_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
@@ -513,10 +524,14 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       for (int j = 0; j < n_kv && ok; ++j) {
         if (!mbar_wait(ds_ready + (j & 1), uint32_t(j >> 1) & 1, ctl, 143)) { ok = false; break; }
         tc_fence_after();
+        {
+          const SDesc kd = desc_mn_base<D, BN>(k_tile(j));
+          const uint32_t pa = tmem + (j & 1) * 128;
+          umma_ts(tmem + C::DQ_COL, pa, sdesc_at(kd, 0), IDESC_DQ, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          umma_ts(tmem + C::DQ_COL, tmem + (j & 1) * 128 + a_col(ks), desc_mn_major<D, BN>(k_tile(j), ks),
-                  IDESC_DQ, (j > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 1; ks < BN / 16; ++ks)
+            umma_ts(tmem + C::DQ_COL, pa + a_col(ks), sdesc_at(kd, mn_major_off<D>(ks)), IDESC_DQ, 1u);
+        }
         umma_commit(kv_empty + j % C::NST);
         if (j + 1 < n_kv) issue_dp(j + 1);  // its stage was waited for before S(j+1)
         if (j + 2 < n_kv) {

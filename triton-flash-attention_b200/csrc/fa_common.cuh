@@ -18,23 +18,27 @@ struct TileGeom {
   static_assert(D == 32 || D == 64 || D == 128, "head dim");
 };
 
-// Descriptor of the 16-wide K slice `ks` of a K-major operand tile (rows are
-// the M or N index, D is the reduction index).
+// Byte offset of the 16-wide K slice `ks` inside a K-major (R x D) tile, and
+// of rows [16 ks, 16 ks + 16) inside an MN-major tile (compile-time).
 template <int D, int R>
-__device__ __forceinline__ uint64_t desc_k_major(uint32_t tile_saddr, int ks) {
+__host__ __device__ constexpr uint32_t k_major_off(int ks) {
   using G = TileGeom<D>;
-  const uint32_t e = uint32_t(ks) * 16u;
-  const uint32_t addr = tile_saddr + (e / G::BOX) * uint32_t(R * G::SW) + (e % G::BOX) * 2u;
-  return smem_desc<G::SW>(addr, 16u, 8u * G::SW);
+  return uint32_t((ks * 16) / G::BOX) * uint32_t(R * G::SW) + uint32_t((ks * 16) % G::BOX) * 2u;
 }
-
-// Descriptor of rows [16*ks, 16*ks+16) of an MN-major operand tile: the tile's
-// rows are the reduction index and its D columns the N index.
-template <int D, int R>
-__device__ __forceinline__ uint64_t desc_mn_major(uint32_t tile_saddr, int ks) {
+template <int D>
+__host__ __device__ constexpr uint32_t mn_major_off(int ks) {
+  return uint32_t(ks) * 16u * uint32_t(TileGeom<D>::SW);
+}
+// Descriptor bases: advance with sdesc_at(base, k_major_off / mn_major_off).
+template <int D>
+__device__ __forceinline__ SDesc desc_k_base(uint32_t tile_saddr) {
   using G = TileGeom<D>;
-  const uint32_t addr = tile_saddr + uint32_t(ks) * 16u * G::SW;
-  return smem_desc<G::SW>(addr, uint32_t(R * G::SW), 8u * G::SW);
+  return sdesc<G::SW>(tile_saddr, 16u, 8u * G::SW);
+}
+template <int D, int R>
+__device__ __forceinline__ SDesc desc_mn_base(uint32_t tile_saddr) {
+  using G = TileGeom<D>;
+  return sdesc<G::SW>(tile_saddr, uint32_t(R * G::SW), 8u * G::SW);
 }
 
 // Problem description shared by the attention kernels (element strides).

@@ -199,24 +199,27 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       const uint32_t q_s = sbase + C::OFF_Q;
       const uint32_t k_s = sbase + C::OFF_K;
       const uint32_t v_s = sbase + C::OFF_V;
+      // descriptor bases (the issue loops below only add constants)
+      SDesc qd[QT];
+#pragma unroll
+      for (int t = 0; t < QT; ++t) qd[t] = desc_k_base<D>(q_s + t * C::Q_TILE_BYTES);
       auto issue_s = [&](int t, int j) {
-        const uint32_t qa = q_s + t * C::Q_TILE_BYTES;
-        const uint32_t kb = k_s + (j % C::NST) * C::KV_TILE_BYTES;
+        const SDesc kd = desc_k_base<D>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
+        const uint32_t dst = tmem + C::S_COL0 + t * BN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + C::S_COL0 + t * BN, desc_k_major<D, BM>(qa, ks), desc_k_major<D, BN>(kb, ks), IDESC_S,
+          umma_ss(dst, sdesc_at(qd[t], k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)), IDESC_S,
                   ks > 0);
         umma_commit(sm.s_full + t);
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t vb = v_s + (j % C::NST) * C::KV_TILE_BYTES;
         // the D columns of V span NBOX boxes BN*SW bytes apart (LBO)
-        const uint32_t lbo = uint32_t(BN * G::SW);
+        const SDesc vd = desc_mn_base<D, BN>(v_s + (j % C::NST) * C::KV_TILE_BYTES);
+        const uint32_t dst = tmem + C::O_COL0 + t * C::OW;
+        const uint32_t pa = tmem + C::S_COL0 + t * BN;
+        umma_ts(dst, pa, sdesc_at(vd, 0), IDESC_PV, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          umma_ts(tmem + C::O_COL0 + t * C::OW, tmem + C::S_COL0 + t * BN + ks * 8,
-                  smem_desc<G::SW>(vb + uint32_t(ks) * 16u * G::SW, lbo, 8u * G::SW), IDESC_PV,
-                  (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 1; ks < BN / 16; ++ks) umma_ts(dst, pa + ks * 8, sdesc_at(vd, mn_major_off<D>(ks)), IDESC_PV, 1u);
       };
       bool ok = mbar_wait(sm.q_full, 0, ctl, 10) && mbar_wait(sm.k_full, 0, ctl, 11);
       if (ok) {

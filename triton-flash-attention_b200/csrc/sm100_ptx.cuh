@@ -215,6 +215,25 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
          (uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
 }
 
+// A descriptor split in its two 32-bit words.  The start-address field
+// (bits 0-13, address >> 4) lives in the low word and never carries out of it
+// for shared-memory addresses below 256 KB, so advancing a descriptor inside a
+// tile is one 32-bit add of a compile-time constant -- which keeps the
+// MMA-issuing thread's instruction stream short.
+struct SDesc {
+  uint32_t lo, hi;
+};
+template <int SW>
+__device__ __forceinline__ SDesc sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  const uint64_t d = smem_desc<SW>(saddr, lbo_bytes, sbo_bytes);
+  return SDesc{uint32_t(d), uint32_t(d >> 32)};
+}
+__device__ __forceinline__ uint64_t sdesc_at(SDesc d, uint32_t byte_off) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(d.lo + (byte_off >> 4)), "r"(d.hi));
+  return r;
+}
+
 // TMEM address: lane in bits 31-16, column in bits 15-0.
 __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
   return base + (lane << 16) + col;
