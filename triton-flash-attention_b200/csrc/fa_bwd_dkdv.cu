@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
   volatile CtaCtl* ctl = ctl_w;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
-  float* s_lse = reinterpret_cast<float*>(smem + C::OFF_LSE);
-  float* s_delta = reinterpret_cast<float*>(smem + C::OFF_DELTA);
+  float* s_nlse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* s_ndelta = reinterpret_cast<float*>(smem + C::OFF_DELTA);
 
   const int warp = int(warp_id());
   const int lane = int(lane_id());
@@ -112,9 +112,9 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   const int n_items = per_head * group;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    mbar_init(kv_full, 2);
     for (int s = 0; s < C::NST; ++s) {
-      mbar_init(full + s, 1 + 32);  // TMA expect_tx arrive + one arrive per producer lane
+      mbar_init(full + s, 2 + 32);  // two TMA expect_tx arrives + one arrive per lane of warp 0
       mbar_init(empty + s, 1);
     }
     for (int w = 0; w < 2; ++w) {
@@ -136,53 +136,77 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // =================== producer warp ===================
+  if (warp == 0 || warp == 3) {
+    // =================== producer warps ===================
+    // Warp 0 loads K and the Q tiles and writes lse2 / Delta; warp 3 loads V
+    // and the dO tiles.  One thread's TMA loads are processed one after
+    // another, so the two streams come from two threads.
+    const bool is_q = warp == 0;
     if (n_items > 0) {
+      const CUtensorMap* tmap_kv = is_q ? &tmap_k : &tmap_v;
+      const CUtensorMap* tmap_qd = is_q ? &tmap_q : &tmap_do;
+      const int qd_off = is_q ? C::OFF_Q : C::OFF_DO;
       if (lane == 0) {
-        tma_prefetch_desc(&tmap_q);
-        tma_prefetch_desc(&tmap_do);
-        tma_prefetch_desc(&tmap_k);
-        tma_prefetch_desc(&tmap_v);
-        mbar_arrive_expect_tx(kv_full, 2 * C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_K + bx * BM * G::SW, &tmap_k, kv_full, bx * G::BOX, kv0, kvh, b);
-          tma_load_4d(smem + C::OFF_V + bx * BM * G::SW, &tmap_v, kv_full, bx * G::BOX, kv0, kvh, b);
-        }
+        tma_prefetch_desc(tmap_qd);
+        tma_prefetch_desc(tmap_kv);
+        mbar_arrive_expect_tx(kv_full, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + (is_q ? C::OFF_K : C::OFF_V) + bx * BM * G::SW, tmap_kv, kv_full, bx * G::BOX, kv0, kvh, b);
       }
+      // lse2 / Delta of the item's 64 query rows are read with plain
+      // loads issued two items ahead: under the TMA stream one L2 round trip
+      // (~1-2k cycles) would otherwise pace the whole loop.  Rows past Nq, or
+      // rows that see no key, get lse2 = +inf so that their P is 0.
+      constexpr int PF = 2;
+      float lv[PF + 1][2], dv[PF + 1][2];
+      auto fetch = [&](int it, float (&l)[2], float (&d)[2]) {
+        const int h = kvh * group + it / per_head;
+        const int q0 = (i_start + it % per_head) * BQ;
+        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int qi = q0 + lane * 2 + e;
+          l[e] = INFINITY;
+          d[e] = 0.f;
+          if (is_q && it < n_items && qi < shp.Nq) {
+            l[e] = lse[rowbase + qi];
+            d[e] = delta[rowbase + qi];
+          }
+        }
+      };
+#pragma unroll
+      for (int p = 0; p < PF; ++p) fetch(p, lv[p], dv[p]);
       int n_iss = 0;
       for (int it = 0; it < n_items; ++it) {
+        if (is_q) fetch(it + PF, lv[PF], dv[PF]);
         const int s = it % C::NST;
         const uint32_t u = uint32_t(it / C::NST);
         if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 61)) break;
         const int h = kvh * group + it / per_head;
         const int q0 = (i_start + it % per_head) * BQ;
         if (lane == 0) {
-          mbar_arrive_expect_tx(full + s, 2 * C::Q_TILE_BYTES);
-          for (int bx = 0; bx < G::NBOX; ++bx) {
-            tma_load_4d(smem + C::OFF_Q + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_q, full + s, bx * G::BOX,
-                        q0, h, b);
-            tma_load_4d(smem + C::OFF_DO + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_do, full + s,
-                        bx * G::BOX, q0, h, b);
-          }
+          mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
+          for (int bx = 0; bx < G::NBOX; ++bx)
+            tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
+                        b);
         }
-        // -lse2 / -Delta of the item's 64 query rows (negated for the FMA);
-        // rows past Nq, or rows that see no key at all, get lse2 = +inf so
-        // that their P is 0.
-        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+        if (is_q) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int qi = q0 + lane * 2 + e;
-          float lv = INFINITY, dv = 0.f;
-          if (qi < shp.Nq) {
-            lv = lse[rowbase + qi];
-            if (lv == -INFINITY) lv = INFINITY;
-            dv = delta[rowbase + qi];
+          for (int e = 0; e < 2; ++e) {
+            const float l = lv[0][e] == -INFINITY ? INFINITY : lv[0][e];
+            s_nlse[s * BQ + lane * 2 + e] = -l;
+            s_ndelta[s * BQ + lane * 2 + e] = -dv[0][e];
           }
-          s_lse[s * BQ + lane * 2 + e] = -lv;
-          s_delta[s * BQ + lane * 2 + e] = -dv;
+          mbar_arrive(full + s);
+#pragma unroll
+          for (int p = 0; p < PF; ++p) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              lv[p][e] = lv[p + 1][e];
+              dv[p][e] = dv[p + 1][e];
+            }
+          }
         }
-        mbar_arrive(full + s);
         ++n_iss;
       }
       if (lane == 0) {
@@ -289,8 +313,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         for (int c = 0; c < BQ; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
       }
       // stage values are stored negated: -lse2 and -Delta
-      const float4* l4 = reinterpret_cast<const float4*>(s_lse + s * BQ);
-      const float4* d4 = reinterpret_cast<const float4*>(s_delta + s * BQ);
+      const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ);
+      const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ);
       uint32_t pk_p[BQ / 2], pk_ds[BQ / 2];
 #pragma unroll
       for (int c4 = 0; c4 < BQ / 4; ++c4) {
@@ -474,9 +498,9 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   const int n_items = per_head * group;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    mbar_init(kv_full, 2);
     for (int s = 0; s < C::NST; ++s) {
-      mbar_init(full + s, 1 + 32);
+      mbar_init(full + s, 2 + 32);  // two TMA expect_tx arrives + one arrive per lane of warp 0
       mbar_init(empty + s, 1);
     }
     mbar_init(s_full, 1);
@@ -500,52 +524,77 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // =================== producer warp ===================
+  if (warp == 0 || warp == 3) {
+    // =================== producer warps ===================
+    // Warp 0 loads K and the Q tiles and writes lse2 / Delta; warp 3 loads V
+    // and the dO tiles.  One thread's TMA loads are processed one after
+    // another, so the two streams come from two threads.
+    const bool is_q = warp == 0;
     if (n_items > 0) {
+      const CUtensorMap* tmap_kv = is_q ? &tmap_k : &tmap_v;
+      const CUtensorMap* tmap_qd = is_q ? &tmap_q : &tmap_do;
+      const int qd_off = is_q ? C::OFF_Q : C::OFF_DO;
       if (lane == 0) {
-        tma_prefetch_desc(&tmap_q);
-        tma_prefetch_desc(&tmap_do);
-        tma_prefetch_desc(&tmap_k);
-        tma_prefetch_desc(&tmap_v);
-        mbar_arrive_expect_tx(kv_full, 2 * C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_K + bx * BM * G::SW, &tmap_k, kv_full, bx * G::BOX, kv0, kvh, b);
-          tma_load_4d(smem + C::OFF_V + bx * BM * G::SW, &tmap_v, kv_full, bx * G::BOX, kv0, kvh, b);
-        }
+        tma_prefetch_desc(tmap_qd);
+        tma_prefetch_desc(tmap_kv);
+        mbar_arrive_expect_tx(kv_full, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + (is_q ? C::OFF_K : C::OFF_V) + bx * BM * G::SW, tmap_kv, kv_full, bx * G::BOX, kv0, kvh, b);
       }
+      // lse2 / Delta of the item's 128 query rows are read with plain
+      // loads issued two items ahead: under the TMA stream one L2 round trip
+      // (~1-2k cycles) would otherwise pace the whole loop.  Rows past Nq, or
+      // rows that see no key, get lse2 = +inf so that their P is 0.
+      constexpr int PF = 2;
+      float lv[PF + 1][4], dv[PF + 1][4];
+      auto fetch = [&](int it, float (&l)[4], float (&d)[4]) {
+        const int h = kvh * group + it / per_head;
+        const int q0 = (i_start + it % per_head) * BQ;
+        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int qi = q0 + e * 32 + lane;
+          l[e] = INFINITY;
+          d[e] = 0.f;
+          if (is_q && it < n_items && qi < shp.Nq) {
+            l[e] = lse[rowbase + qi];
+            d[e] = delta[rowbase + qi];
+          }
+        }
+      };
+#pragma unroll
+      for (int p = 0; p < PF; ++p) fetch(p, lv[p], dv[p]);
       int n_iss = 0;
       for (int it = 0; it < n_items; ++it) {
+        if (is_q) fetch(it + PF, lv[PF], dv[PF]);
         const int s = it % C::NST;
         const uint32_t u = uint32_t(it / C::NST);
         if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 161)) break;
         const int h = kvh * group + it / per_head;
         const int q0 = (i_start + it % per_head) * BQ;
         if (lane == 0) {
-          mbar_arrive_expect_tx(full + s, 2 * C::Q_TILE_BYTES);
-          for (int bx = 0; bx < G::NBOX; ++bx) {
-            tma_load_4d(smem + C::OFF_Q + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_q, full + s, bx * G::BOX,
-                        q0, h, b);
-            tma_load_4d(smem + C::OFF_DO + s * C::Q_TILE_BYTES + bx * BQ * G::SW, &tmap_do, full + s,
-                        bx * G::BOX, q0, h, b);
-          }
+          mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
+          for (int bx = 0; bx < G::NBOX; ++bx)
+            tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
+                        b);
         }
-        // -lse2 / -Delta of the item's 128 query rows; rows past Nq, or rows
-        // that see no key, get lse2 = +inf so that their P is 0.
-        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+        if (is_q) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = q0 + e * 32 + lane;
-          float lv = INFINITY, dv = 0.f;
-          if (qi < shp.Nq) {
-            lv = lse[rowbase + qi];
-            if (lv == -INFINITY) lv = INFINITY;
-            dv = delta[rowbase + qi];
+          for (int e = 0; e < 4; ++e) {
+            const float l = lv[0][e] == -INFINITY ? INFINITY : lv[0][e];
+            s_nlse[s * BQ + e * 32 + lane] = -l;
+            s_ndelta[s * BQ + e * 32 + lane] = -dv[0][e];
           }
-          s_nlse[s * BQ + e * 32 + lane] = -lv;
-          s_ndelta[s * BQ + e * 32 + lane] = -dv;
+          mbar_arrive(full + s);
+#pragma unroll
+          for (int p = 0; p < PF; ++p) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              lv[p][e] = lv[p + 1][e];
+              dv[p][e] = dv[p + 1][e];
+            }
+          }
         }
-        mbar_arrive(full + s);
         ++n_iss;
       }
       if (lane == 0) {

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
   const int n_max = n_kv[0] > n_kv[1] ? n_kv[0] : n_kv[1];
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, 2);
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
@@ -125,47 +125,44 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // =================== TMA producer ===================
+  if (warp == 0 || warp == 3) {
+    // =================== TMA producers ===================
+    // Warp 0 loads Q and the K tiles, warp 3 dO and the V tiles: one
+    // thread's TMA loads are processed one after another, so two threads
+    // double the stream rate.  q_full expects one arrival from each.
+    const bool is_k = warp == 0;
     if (lane == 0 && n_max > 0) {
-      tma_prefetch_desc(&tmap_q);
-      tma_prefetch_desc(&tmap_do);
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
+      const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
+      const CUtensorMap* tmap_qd = is_k ? &tmap_q : &tmap_do;
+      uint64_t* kv_full = is_k ? k_full : v_full;
+      uint64_t* kv_empty = is_k ? k_empty : v_empty;
+      const int kv_off = is_k ? C::OFF_K : C::OFF_V;
+      const int qd_off = is_k ? C::OFF_Q : C::OFF_DO;
+      tma_prefetch_desc(tmap_qd);
+      tma_prefetch_desc(tmap_kv);
       int q_bytes = 0;
-      for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? 2 * C::Q_TILE_BYTES : 0;
+      for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? C::Q_TILE_BYTES : 0;
       mbar_arrive_expect_tx(q_full, q_bytes);
       for (int t = 0; t < QT; ++t) {
         if (n_kv[t] == 0) continue;
-        for (int bx = 0; bx < G::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q, q_full, bx * G::BOX,
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + qd_off + t * C::Q_TILE_BYTES + bx * BM * G::SW, tmap_qd, q_full, bx * G::BOX,
                       row0 + t * BM, h, b);
-          tma_load_4d(smem + C::OFF_DO + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_do, q_full, bx * G::BOX,
-                      row0 + t * BM, h, b);
-        }
       }
-      int nk_iss = 0, nv_iss = 0;
+      int n_iss = 0;
       for (int j = 0; j < n_max; ++j) {
         const int s = j % C::NST;
         const uint32_t u = uint32_t(j / C::NST);
-        if (u > 0 && !mbar_wait(k_empty + s, (u - 1) & 1, ctl, 31)) break;
-        mbar_arrive_expect_tx(k_full + s, C::KV_TILE_BYTES);
+        if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, is_k ? 31 : 32)) break;
+        mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
         for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + C::OFF_K + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_k, k_full + s, bx * G::BOX,
+          tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
                       j * BN, kvh, b);
-        ++nk_iss;
-        if (u > 0 && !mbar_wait(v_empty + s, (u - 1) & 1, ctl, 32)) break;
-        mbar_arrive_expect_tx(v_full + s, C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + C::OFF_V + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_v, v_full + s, bx * G::BOX,
-                      j * BN, kvh, b);
-        ++nv_iss;
+        ++n_iss;
       }
       mbar_wait_drain(q_full, 0, ctl, 33);
-      for (int j = (nk_iss > C::NST ? nk_iss - C::NST : 0); j < nk_iss; ++j)
-        mbar_wait_drain(k_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 34);
-      for (int j = (nv_iss > C::NST ? nv_iss - C::NST : 0); j < nv_iss; ++j)
-        mbar_wait_drain(v_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 35);
+      for (int j = (n_iss > C::NST ? n_iss - C::NST : 0); j < n_iss; ++j)
+        mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, is_k ? 34 : 35);
     }
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
@@ -422,9 +419,9 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   const int n_kv = kv_tiles_for_rows(shp, row0, BM, BN);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, 2);
     for (int s = 0; s < C::NST; ++s) {
-      mbar_init(kv_full + s, 1);
+      mbar_init(kv_full + s, 2);
       mbar_init(kv_empty + s, 1);
     }
     mbar_init(s_full, 1);
@@ -447,30 +444,30 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // =================== TMA producer ===================
+  if (warp == 0 || warp == 3) {
+    // =================== TMA producers ===================
+    // Warp 0 loads Q and the K tiles, warp 3 dO and the V tiles (one thread's
+    // TMA loads are processed one after another); q_full and kv_full expect
+    // one arrival from each.
+    const bool is_k = warp == 0;
     if (lane == 0 && n_kv > 0) {
-      tma_prefetch_desc(&tmap_q);
-      tma_prefetch_desc(&tmap_do);
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
-      mbar_arrive_expect_tx(q_full, 2 * C::Q_TILE_BYTES);
-      for (int bx = 0; bx < G::NBOX; ++bx) {
-        tma_load_4d(smem + C::OFF_Q + bx * BM * G::SW, &tmap_q, q_full, bx * G::BOX, row0, h, b);
-        tma_load_4d(smem + C::OFF_DO + bx * BM * G::SW, &tmap_do, q_full, bx * G::BOX, row0, h, b);
-      }
+      const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
+      const CUtensorMap* tmap_qd = is_k ? &tmap_q : &tmap_do;
+      const int kv_off = is_k ? C::OFF_K : C::OFF_V;
+      tma_prefetch_desc(tmap_qd);
+      tma_prefetch_desc(tmap_kv);
+      mbar_arrive_expect_tx(q_full, C::Q_TILE_BYTES);
+      for (int bx = 0; bx < G::NBOX; ++bx)
+        tma_load_4d(smem + (is_k ? C::OFF_Q : C::OFF_DO) + bx * BM * G::SW, tmap_qd, q_full, bx * G::BOX, row0, h, b);
       int n_iss = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % C::NST;
         const uint32_t u = uint32_t(j / C::NST);
         if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, 131)) break;
-        mbar_arrive_expect_tx(kv_full + s, 2 * C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx) {
-          tma_load_4d(smem + C::OFF_K + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_k, kv_full + s,
-                      bx * G::BOX, j * BN, kvh, b);
-          tma_load_4d(smem + C::OFF_V + s * C::KV_TILE_BYTES + bx * BN * G::SW, &tmap_v, kv_full + s,
-                      bx * G::BOX, j * BN, kvh, b);
-        }
+        mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
+                      j * BN, kvh, b);
         ++n_iss;
       }
       mbar_wait_drain(q_full, 0, ctl, 132);
