@@ -395,21 +395,28 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// D <= 64: 128-query items.  At D <= 64 an N = 64 MMA runs at ~70% of the
-// tensor rate (measured: M128 x N x K16 takes max(N/2, ~45) cycles), so the
-// items here are 128 query rows wide (S^T, dP^T are N = 128 MMAs at full
-// rate).  The two elementwise warpgroups are specialised by phase so that
-// consecutive items overlap: warpgroup 0 turns S^T into P^T (the exponentials)
-// for whole items, warpgroup 1 turns dP^T and P^T into dS^T, one item behind.
-// S^T is double-buffered in TMEM; the MMA thread issues dV(i) as soon as P^T(i)
-// is published and dK(i), dP^T(i+1), S^T(i+2) once dS^T(i) is.
+// D <= 64: persistent kernel with 128-query items.  At D <= 64 an N = 64 MMA
+// runs at ~70% of the tensor rate (measured: M128 x N x K16 takes
+// max(N/2, ~45) cycles), so the items here are 128 query rows wide (S^T, dP^T
+// are N = 128 MMAs at full rate).
+// One CTA per SM walks its share of the work tiles (128 keys of one batch and
+// kv head each) back to back: K/V are double-buffered, so the next tile's K/V
+// load, its first S^T / dP^T MMAs and its first exponentials overlap the
+// current tile's last items and its dK/dV epilogue.  Measured before this
+// change, one CTA per tile spent ~7k of its ~60k cycles on the start-up and
+// the epilogue that nothing overlapped.
+// The two elementwise warpgroups are specialised by phase: warpgroup 0 turns
+// S^T into P^T (the exponentials) for whole items, warpgroup 1 turns dP^T and
+// P^T into dS^T, one item behind.  S^T is double-buffered in TMEM; the MMA
+// thread issues dV(i) as soon as P^T(i) is published and dK(i), dP^T(i+1),
+// S^T(i+2) once dS^T(i) is.
 // TMEM: S^T buffers at [0,128) and [128,256), dP^T at [256,384),
 //       dV at [384, 384+D), dK at [384+D, 384+2D).
 // P^T of query columns [64h, 64h+64) is packed into its S^T buffer's columns
 // [64h, 64h+32), dS^T likewise into dP^T's columns [256+64h, 256+64h+32):
 // each half is written after it was read.
 namespace bkvw {
-constexpr int BM = 128;   // keys per CTA
+constexpr int BM = 128;   // keys per tile
 constexpr int BQ = 128;   // query rows per item
 constexpr int NUM_THREADS = 384;
 constexpr int POLY_MASK = 4;  // pairs (i & 7) < 4 use the FMA-pipe exp2: half off MUFU
@@ -420,26 +427,61 @@ struct Cfg {
   static constexpr int NST = 4;
   static constexpr int KV_TILE_BYTES = BM * D * 2;
   static constexpr int Q_TILE_BYTES = BQ * D * 2;
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + KV_TILE_BYTES;
-  static constexpr int OFF_Q = OFF_V + KV_TILE_BYTES;
+  static constexpr int OFF_K = 0;                          // 2 buffers
+  static constexpr int OFF_V = OFF_K + 2 * KV_TILE_BYTES;  // 2 buffers
+  static constexpr int OFF_Q = OFF_V + 2 * KV_TILE_BYTES;
   static constexpr int OFF_DO = OFF_Q + NST * Q_TILE_BYTES;
   static constexpr int OFF_LSE = OFF_DO + NST * Q_TILE_BYTES;
   static constexpr int OFF_DELTA = OFF_LSE + NST * BQ * 4;
   static constexpr int OFF_BAR = OFF_DELTA + NST * BQ * 4;
-  // kv_full, full[NST], empty[NST], s_full[2], dp_full, p_ready[2], ds_ready, acc_full, mma_done
-  static constexpr int NUM_BARS = 1 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 1;
+  // kv_full[2], kv_empty[2], full[NST], empty[NST], s_full[2], dp_full, p_ready[2], ds_ready,
+  // acc_full, acc_empty, mma_done
+  static constexpr int NUM_BARS = 2 + 2 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 1 + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
-  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED;
   static constexpr int TMEM_COLS = 512;
   static constexpr int DP_COL = 256;
   static constexpr int DV_COL = 384;
   static constexpr int DK_COL = 384 + D;
   static_assert(D <= 64, "wide dK/dV path is for D <= 64");
   static_assert(DK_COL + D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
+
+// A work tile: 128 keys of one (batch, kv head) and the query items (query
+// head of the group x 128-row query tile) that see them.
+struct Tile {
+  int kv0, b, kvh, i_start, per_head, n_items;
+};
+__device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
+  const int BHkv = shp.B * shp.Hkv;
+  const int kv_tile = t / BHkv;
+  const int bhk = t % BHkv;
+  Tile w;
+  w.b = bhk / shp.Hkv;
+  w.kvh = bhk % shp.Hkv;
+  w.kv0 = kv_tile * BM;
+  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  int i_start = 0;
+  if (shp.causal) {
+    const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
+    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
+    if (i_start > n_qt) i_start = n_qt;
+  }
+  w.i_start = i_start;
+  w.per_head = n_qt - i_start;
+  w.n_items = w.per_head * (shp.Hq / shp.Hkv);
+  return w;
+}
+// The k-th tile of CTA c when G CTAs share n tiles: snake order over rounds
+// of G (tiles are numbered heaviest first for causal masks), which evens out
+// the items per CTA.  Returns n when the CTA has no k-th tile.
+__device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
+  const int t = k * G + ((k & 1) ? G - 1 - c : c);
+  return t < n ? t : n;
+}
 }  // namespace bkvw
 
 template <int D>
@@ -449,7 +491,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
                             const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                             void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh,
                             const long long dk_sn, void* __restrict__ dv_out, const long long dv_sb,
-                            const long long dv_sh, const long long dv_sn, const int accumulate_fp32) {
+                            const long long dv_sh, const long long dv_sn, const int accumulate_fp32,
+                            const int n_tiles) {
   using namespace bkvw;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -460,17 +503,20 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* full = bars + 1;
+  uint64_t* kv_empty = kv_full + 2;
+  uint64_t* full = kv_empty + 2;
   uint64_t* empty = full + C::NST;
   uint64_t* s_full = empty + C::NST;
   uint64_t* dp_full = s_full + 2;
   // p_ready is per S^T buffer: phase k of p_ready[b] belongs to item 2k+b, so
-  // it cannot run two phases ahead of its waiters (item it+2's S^T is issued
-  // only after dS^T(it) -- and so P^T(it) -- was consumed).
+  // it cannot run two phases ahead of its waiters (item i+2's S^T is issued
+  // only after dS^T(i) -- and so P^T(i) -- was consumed).  Items are counted
+  // across the CTA's tiles.
   uint64_t* p_ready = dp_full + 1;
   uint64_t* ds_ready = p_ready + 2;
-  uint64_t* acc_full = ds_ready + 1;
-  uint64_t* mma_done = acc_full + 1;
+  uint64_t* acc_full = ds_ready + 1;   // one phase per non-empty tile: dV, dK complete
+  uint64_t* acc_empty = acc_full + 1;  // one phase per non-empty tile: the epilogue read them
+  uint64_t* mma_done = acc_empty + 1;
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
   volatile CtaCtl* ctl = ctl_w;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -479,26 +525,15 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 
   const int warp = int(warp_id());
   const int lane = int(lane_id());
-
-  const int BHkv = shp.B * shp.Hkv;
-  const int kv_tile = int(blockIdx.x) / BHkv;
-  const int bhk = int(blockIdx.x) % BHkv;
-  const int b = bhk / shp.Hkv;
-  const int kvh = bhk % shp.Hkv;
   const int group = shp.Hq / shp.Hkv;
-  const int kv0 = kv_tile * BM;
-  const int n_qt = (shp.Nq + BQ - 1) / BQ;
-  int i_start = 0;
-  if (shp.causal) {
-    const long long first_row = (long long)kv0 + shp.k_off - shp.q_off;
-    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
-    if (i_start > n_qt) i_start = n_qt;
-  }
-  const int per_head = n_qt - i_start;
-  const int n_items = per_head * group;
+  const int cta = int(blockIdx.x);
+  const int n_cta = int(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 2);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + i, 2);  // K from warp 0, V from warp 3
+      mbar_init(kv_empty + i, 1);
+    }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(full + s, 2 + 32);  // two TMA expect_tx arrives + one arrive per lane of warp 0
       mbar_init(empty + s, 1);
@@ -510,6 +545,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     mbar_init(p_ready + 1, 128);
     mbar_init(ds_ready, 128);
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
     mbar_init(mma_done, 1);
     ctl_w->abort = 0;
     ctl_w->status = shp.status;
@@ -530,53 +566,83 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     // and the dO tiles.  One thread's TMA loads are processed one after
     // another, so the two streams come from two threads.
     const bool is_q = warp == 0;
-    if (n_items > 0) {
-      const CUtensorMap* tmap_kv = is_q ? &tmap_k : &tmap_v;
-      const CUtensorMap* tmap_qd = is_q ? &tmap_q : &tmap_do;
-      const int qd_off = is_q ? C::OFF_Q : C::OFF_DO;
-      if (lane == 0) {
-        tma_prefetch_desc(tmap_qd);
-        tma_prefetch_desc(tmap_kv);
-        mbar_arrive_expect_tx(kv_full, C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + (is_q ? C::OFF_K : C::OFF_V) + bx * BM * G::SW, tmap_kv, kv_full, bx * G::BOX, kv0, kvh, b);
+    const CUtensorMap* tmap_kv = is_q ? &tmap_k : &tmap_v;
+    const CUtensorMap* tmap_qd = is_q ? &tmap_q : &tmap_do;
+    const int kv_off = is_q ? C::OFF_K : C::OFF_V;
+    const int qd_off = is_q ? C::OFF_Q : C::OFF_DO;
+    if (lane == 0) {
+      tma_prefetch_desc(tmap_qd);
+      tma_prefetch_desc(tmap_kv);
+    }
+    // lse2 / Delta of an item's 128 query rows are read with plain loads
+    // issued two items ahead (across tiles): under the TMA stream one L2
+    // round trip (~1-2k cycles) would otherwise pace the loop.  Rows past Nq,
+    // or rows that see no key, get lse2 = +inf so that their P is 0.
+    constexpr int PF = 2;
+    float lv[PF + 1][4], dv[PF + 1][4];
+    int pf_k = 0, pf_it = 0;  // prefetch cursor: tile round k, item it
+    Tile pf_w = tile_of(shp, tile_index(cta, 0, n_cta, n_tiles) < n_tiles ? tile_index(cta, 0, n_cta, n_tiles) : 0);
+    bool pf_live = tile_index(cta, 0, n_cta, n_tiles) < n_tiles;
+    auto pf_skip_empty = [&]() {
+      while (pf_live && pf_it >= pf_w.n_items) {
+        pf_it = 0;
+        ++pf_k;
+        const int t = tile_index(cta, pf_k, n_cta, n_tiles);
+        pf_live = t < n_tiles;
+        if (pf_live) pf_w = tile_of(shp, t);
       }
-      // lse2 / Delta of the item's 128 query rows are read with plain
-      // loads issued two items ahead: under the TMA stream one L2 round trip
-      // (~1-2k cycles) would otherwise pace the whole loop.  Rows past Nq, or
-      // rows that see no key, get lse2 = +inf so that their P is 0.
-      constexpr int PF = 2;
-      float lv[PF + 1][4], dv[PF + 1][4];
-      auto fetch = [&](int it, float (&l)[4], float (&d)[4]) {
-        const int h = kvh * group + it / per_head;
-        const int q0 = (i_start + it % per_head) * BQ;
-        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+    };
+    auto fetch = [&](float (&l)[4], float (&d)[4]) {
+      pf_skip_empty();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = q0 + e * 32 + lane;
-          l[e] = INFINITY;
-          d[e] = 0.f;
-          if (is_q && it < n_items && qi < shp.Nq) {
-            l[e] = lse[rowbase + qi];
-            d[e] = delta[rowbase + qi];
-          }
+      for (int e = 0; e < 4; ++e) {
+        l[e] = INFINITY;
+        d[e] = 0.f;
+      }
+      if (!pf_live || !is_q) return;
+      const int h = pf_w.kvh * group + pf_it / pf_w.per_head;
+      const int q0 = (pf_w.i_start + pf_it % pf_w.per_head) * BQ;
+      const long long rowbase = ((long long)pf_w.b * shp.Hq + h) * shp.Nq;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = q0 + e * 32 + lane;
+        if (qi < shp.Nq) {
+          l[e] = lse[rowbase + qi];
+          d[e] = delta[rowbase + qi];
         }
-      };
+      }
+      ++pf_it;
+    };
 #pragma unroll
-      for (int p = 0; p < PF; ++p) fetch(p, lv[p], dv[p]);
-      int n_iss = 0;
-      for (int it = 0; it < n_items; ++it) {
-        if (is_q) fetch(it + PF, lv[PF], dv[PF]);
-        const int s = it % C::NST;
-        const uint32_t u = uint32_t(it / C::NST);
-        if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 161)) break;
-        const int h = kvh * group + it / per_head;
-        const int q0 = (i_start + it % per_head) * BQ;
+    for (int p = 0; p < PF; ++p) fetch(lv[p], dv[p]);
+    int gi = 0, tcn = 0;  // items and non-empty tiles issued
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int t = tile_index(cta, k, n_cta, n_tiles);
+      if (t >= n_tiles) break;
+      const Tile w = tile_of(shp, t);
+      if (w.n_items == 0) continue;
+      const int kb = tcn & 1;
+      if (tcn >= 2 && !mbar_wait_warp(kv_empty + kb, uint32_t((tcn >> 1) - 1) & 1, ctl, 160)) { ok = false; break; }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full + kb, C::KV_TILE_BYTES);
+        for (int bx = 0; bx < G::NBOX; ++bx)
+          tma_load_4d(smem + kv_off + kb * C::KV_TILE_BYTES + bx * BM * G::SW, tmap_kv, kv_full + kb, bx * G::BOX,
+                      w.kv0, w.kvh, w.b);
+      }
+      ++tcn;
+      for (int it = 0; it < w.n_items; ++it) {
+        fetch(lv[PF], dv[PF]);
+        const int s = gi % C::NST;
+        const uint32_t u = uint32_t(gi / C::NST);
+        if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 161)) { ok = false; break; }
+        const int h = w.kvh * group + it / w.per_head;
+        const int q0 = (w.i_start + it % w.per_head) * BQ;
         if (lane == 0) {
           mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
             tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
-                        b);
+                        w.b);
         }
         if (is_q) {
 #pragma unroll
@@ -586,100 +652,117 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             s_ndelta[s * BQ + e * 32 + lane] = -dv[0][e];
           }
           mbar_arrive(full + s);
+        }
 #pragma unroll
-          for (int p = 0; p < PF; ++p) {
+        for (int p = 0; p < PF; ++p) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              lv[p][e] = lv[p + 1][e];
-              dv[p][e] = dv[p + 1][e];
-            }
+          for (int e = 0; e < 4; ++e) {
+            lv[p][e] = lv[p + 1][e];
+            dv[p][e] = dv[p + 1][e];
           }
         }
-        ++n_iss;
+        ++gi;
       }
-      if (lane == 0) {
-        mbar_wait_drain(kv_full, 0, ctl, 162);
-        for (int it = (n_iss > C::NST ? n_iss - C::NST : 0); it < n_iss; ++it)
-          mbar_wait_drain(full + it % C::NST, uint32_t(it / C::NST) & 1, ctl, 163);
-      }
+    }
+    if (lane == 0) {
+      for (int j = (tcn > 2 ? tcn - 2 : 0); j < tcn; ++j)
+        mbar_wait_drain(kv_full + (j & 1), uint32_t(j >> 1) & 1, ctl, 162);
+      for (int j = (gi > C::NST ? gi - C::NST : 0); j < gi; ++j)
+        mbar_wait_drain(full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 163);
     }
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
-    if (lane == 0 && n_items > 0) {
+    if (lane == 0) {
       constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0);
       constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1);
-      const uint32_t k_s = sbase + C::OFF_K;
-      const uint32_t v_s = sbase + C::OFF_V;
-      auto q_tile = [&](int it) { return sbase + C::OFF_Q + (it % C::NST) * C::Q_TILE_BYTES; };
-      auto do_tile = [&](int it) { return sbase + C::OFF_DO + (it % C::NST) * C::Q_TILE_BYTES; };
-      const SDesc kd = desc_k_base<D>(k_s);
-      const SDesc vd = desc_k_base<D>(v_s);
-      auto issue_s = [&](int it) {  // S^T -> buffer it & 1
-        const SDesc qd = desc_k_base<D>(q_tile(it));
+      auto q_tile = [&](int g) { return sbase + C::OFF_Q + (g % C::NST) * C::Q_TILE_BYTES; };
+      auto do_tile = [&](int g) { return sbase + C::OFF_DO + (g % C::NST) * C::Q_TILE_BYTES; };
+      SDesc kd = desc_k_base<D>(sbase + C::OFF_K);
+      SDesc vd = desc_k_base<D>(sbase + C::OFF_V);
+      auto issue_s = [&](int g) {  // S^T -> buffer g & 1
+        const SDesc qd = desc_k_base<D>(q_tile(g));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + (it & 1) * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)),
+          umma_ss(tmem + (g & 1) * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)),
                   IDESC_ST, ks > 0);
-        umma_commit(s_full + (it & 1));
+        umma_commit(s_full + (g & 1));
       };
-      auto issue_dp = [&](int it) {
-        const SDesc dd = desc_k_base<D>(do_tile(it));
+      auto issue_dp = [&](int g) {
+        const SDesc dd = desc_k_base<D>(do_tile(g));
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
           umma_ss(tmem + C::DP_COL, sdesc_at(vd, k_major_off<D, BM>(ks)), sdesc_at(dd, k_major_off<D, BQ>(ks)),
                   IDESC_ST, ks > 0);
         umma_commit(dp_full);
       };
+      auto wait_full = [&](int g, int site) {
+        const bool r = mbar_wait(full + g % C::NST, uint32_t(g / C::NST) & 1, ctl, site);
+        tc_fence_after();
+        return r;
+      };
       // A operand (fp16 in TMEM) for query rows [16ks, 16ks+16) of a region
       // whose halves sit 64 columns apart
       auto a_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
-      bool ok = mbar_wait(kv_full, 0, ctl, 170) && mbar_wait(full, 0, ctl, 171);
-      if (ok) {
+      int gi = 0, tcn = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = tile_index(cta, k, n_cta, n_tiles);
+        if (t >= n_tiles) break;
+        const int n = tile_of(shp, t).n_items;
+        if (n == 0) continue;
+        const int kb = tcn & 1;
+        if (!mbar_wait(kv_full + kb, uint32_t(tcn >> 1) & 1, ctl, 170)) { ok = false; break; }
         tc_fence_after();
-        issue_s(0);
-        issue_dp(0);
-        if (n_items > 1) {
-          ok = mbar_wait(full + 1 % C::NST, uint32_t(1 / C::NST) & 1, ctl, 172);
-          if (ok) {
-            tc_fence_after();
-            issue_s(1);
+        kd = desc_k_base<D>(sbase + C::OFF_K + kb * C::KV_TILE_BYTES);
+        vd = desc_k_base<D>(sbase + C::OFF_V + kb * C::KV_TILE_BYTES);
+        // the tile's first S^T and dP^T, and the second S^T, run while the
+        // warpgroups finish the previous tile
+        if (!wait_full(gi, 171)) { ok = false; break; }
+        issue_s(gi);
+        issue_dp(gi);
+        if (n > 1) {
+          if (!wait_full(gi + 1, 172)) { ok = false; break; }
+          issue_s(gi + 1);
+        }
+        for (int it = 0; it < n; ++it) {
+          const int g = gi + it;
+          if (!mbar_wait(p_ready + (g & 1), uint32_t(g >> 1) & 1, ctl, 173)) { ok = false; break; }
+          // dV / dK of the previous tile were read by the epilogue
+          if (it == 0 && tcn > 0 && !mbar_wait(acc_empty, uint32_t(tcn - 1) & 1, ctl, 177)) { ok = false; break; }
+          tc_fence_after();
+          {
+            const SDesc dd = desc_mn_base<D, BQ>(do_tile(g));
+            const uint32_t pa = tmem + (g & 1) * 128;
+            umma_ts(tmem + C::DV_COL, pa, sdesc_at(dd, 0), IDESC_G, it > 0 ? 1u : 0u);
+#pragma unroll
+            for (int ks = 1; ks < BQ / 16; ++ks)
+              umma_ts(tmem + C::DV_COL, pa + a_col(ks), sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
+          }
+          if (!mbar_wait(ds_ready, uint32_t(g) & 1, ctl, 174)) { ok = false; break; }
+          tc_fence_after();
+          {
+            const SDesc qd = desc_mn_base<D, BQ>(q_tile(g));
+            umma_ts(tmem + C::DK_COL, tmem + C::DP_COL, sdesc_at(qd, 0), IDESC_G, it > 0 ? 1u : 0u);
+#pragma unroll
+            for (int ks = 1; ks < BQ / 16; ++ks)
+              umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + a_col(ks), sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G,
+                      1u);
+          }
+          umma_commit(empty + g % C::NST);
+          if (it + 1 < n) issue_dp(g + 1);  // its stage was waited for before S^T(g+1)
+          // buffer g&1 is free: dV(g) (issued above) and warpgroup 1 (before
+          // ds_ready) have read P^T(g)
+          if (it + 2 < n) {
+            if (!wait_full(g + 2, 175)) { ok = false; break; }
+            issue_s(g + 2);
           }
         }
+        if (!ok) break;
+        umma_commit(acc_full);
+        umma_commit(kv_empty + kb);
+        gi += n;
+        ++tcn;
       }
-      for (int it = 0; it < n_items && ok; ++it) {
-        const uint32_t db = do_tile(it);
-        const uint32_t qb = q_tile(it);
-        if (!mbar_wait(p_ready + (it & 1), uint32_t(it >> 1) & 1, ctl, 173)) { ok = false; break; }
-        tc_fence_after();
-        {
-          const SDesc dd = desc_mn_base<D, BQ>(db);
-          const uint32_t pa = tmem + (it & 1) * 128;
-          umma_ts(tmem + C::DV_COL, pa, sdesc_at(dd, 0), IDESC_G, it > 0 ? 1u : 0u);
-#pragma unroll
-          for (int ks = 1; ks < BQ / 16; ++ks)
-            umma_ts(tmem + C::DV_COL, pa + a_col(ks), sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
-        }
-        if (!mbar_wait(ds_ready, uint32_t(it) & 1, ctl, 174)) { ok = false; break; }
-        tc_fence_after();
-        {
-          const SDesc qd = desc_mn_base<D, BQ>(qb);
-          umma_ts(tmem + C::DK_COL, tmem + C::DP_COL, sdesc_at(qd, 0), IDESC_G, it > 0 ? 1u : 0u);
-#pragma unroll
-          for (int ks = 1; ks < BQ / 16; ++ks)
-            umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + a_col(ks), sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G, 1u);
-        }
-        umma_commit(empty + it % C::NST);
-        if (it + 1 < n_items) issue_dp(it + 1);  // its stage was waited for before S^T(it+1)
-        // buffer it&1 is free: dV(it) (issued above) and warpgroup 1 (before
-        // ds_ready) have read P^T(it)
-        if (it + 2 < n_items) {
-          const int n2 = it + 2;
-          if (!mbar_wait(full + n2 % C::NST, uint32_t(n2 / C::NST) & 1, ctl, 175)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(n2);
-        }
-      }
-      if (ok) umma_commit(acc_full);
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0, ctl, 176);
     }
@@ -690,101 +773,106 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     const int rl = wq * 32 + lane;  // key row within the tile
     const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
     const uint64_t c2x2 = f2pack(shp.scale_log2, shp.scale_log2);
-    const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off;
+    int gi = 0, tcn = 0;
     bool ok = true;
-    if (w == 0) {
-      for (int it = 0; it < n_items; ++it) {
-        const int s = it % C::NST;
-        if (!mbar_wait_warp(s_full + (it & 1), uint32_t(it >> 1) & 1, ctl, 180)) { ok = false; break; }
-        // the stage's -lse2/-Delta: its phase completed before S^T was issued
-        if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 182)) { ok = false; break; }
-        tc_fence_after();
-        const int q0 = (i_start + it % per_head) * BQ;
+    for (int k = 0; ok; ++k) {
+      const int t = tile_index(cta, k, n_cta, n_tiles);
+      if (t >= n_tiles) break;
+      const Tile wt = tile_of(shp, t);
+      const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
+      for (int it = 0; it < wt.n_items && ok; ++it) {
+        const int g = gi + it;
+        const int s = g % C::NST;
+        const int q0 = (wt.i_start + it % wt.per_head) * BQ;
+        if (w == 0) {
+          if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 180)) { ok = false; break; }
+          // the stage's -lse2/-Delta: its phase completed before S^T was issued
+          if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 182)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t tS = lane_base + uint32_t((it & 1) * 128 + 64 * hh);
-          float st[64];
-          tmem_ld64(tS, st);
-          if (shp.causal) {
-            const long long x = cmin_base - q0 - 64 * hh;
-            const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
-            if (cmin > 0) {
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * hh);
+            float st[64];
+            tmem_ld64(tS, st);
+            if (shp.causal) {
+              const long long x = cmin_base - q0 - 64 * hh;
+              const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+              if (cmin > 0) {
 #pragma unroll
-              for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+                for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+              }
             }
-          }
-          const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
-          uint32_t pk_p[32];
+            const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
+            uint32_t pk_p[32];
 #pragma unroll
-          for (int c4 = 0; c4 < 16; ++c4) {
-            const float4 nl = l4[c4];
-            const int c = c4 * 4;
-            const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
-            const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
-            const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
-            const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
-            pk_p[c4 * 2] = h2_from_f2(e01);
-            pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+            for (int c4 = 0; c4 < 16; ++c4) {
+              const float4 nl = l4[c4];
+              const int c = c4 * 4;
+              const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
+              const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
+              const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
+              const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
+              pk_p[c4 * 2] = h2_from_f2(e01);
+              pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+            }
+            tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
+            tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
           }
-          tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
-          tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_ready + (it & 1));
-      }
-    } else {
-      for (int it = 0; it < n_items; ++it) {
-        const int s = it % C::NST;
-        if (!mbar_wait_warp(p_ready + (it & 1), uint32_t(it >> 1) & 1, ctl, 184)) { ok = false; break; }
-        if (!mbar_wait_warp(dp_full, uint32_t(it) & 1, ctl, 185)) { ok = false; break; }
-        if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 183)) { ok = false; break; }
-        tc_fence_after();
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(p_ready + (g & 1));
+        } else {
+          if (!mbar_wait_warp(p_ready + (g & 1), uint32_t(g >> 1) & 1, ctl, 184)) { ok = false; break; }
+          if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 185)) { ok = false; break; }
+          if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 183)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * hh);
-          float dpt[64];
-          tmem_ld64(tD, dpt);
-          float pf[32];
-          tmem_ld32(lane_base + uint32_t((it & 1) * 128 + 64 * hh), pf);
-          const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * hh);
-          uint32_t pk_ds[32];
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * hh);
+            float dpt[64];
+            tmem_ld64(tD, dpt);
+            float pf[32];
+            tmem_ld32(lane_base + uint32_t((g & 1) * 128 + 64 * hh), pf);
+            const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * hh);
+            uint32_t pk_ds[32];
 #pragma unroll
-          for (int c4 = 0; c4 < 16; ++c4) {
-            const float4 nd = d4[c4];
-            const int c = c4 * 4;
-            const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-            const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-            pk_ds[c4 * 2] = hmul2(__float_as_uint(pf[c4 * 2]), d01);
-            pk_ds[c4 * 2 + 1] = hmul2(__float_as_uint(pf[c4 * 2 + 1]), d23);
+            for (int c4 = 0; c4 < 16; ++c4) {
+              const float4 nd = d4[c4];
+              const int c = c4 * 4;
+              const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+              const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+              pk_ds[c4 * 2] = hmul2(__float_as_uint(pf[c4 * 2]), d01);
+              pk_ds[c4 * 2 + 1] = hmul2(__float_as_uint(pf[c4 * 2 + 1]), d23);
+            }
+            tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+            tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
           }
-          tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
-          tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(ds_ready);
         }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(ds_ready);
       }
-    }
-    // ---- epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK ----
-    if (ok && n_items > 0) ok = mbar_wait_warp(acc_full, 0, ctl, 186 + w);
-    if (ok) {
-      const int kr = kv0 + rl;
+      if (!ok) break;
+      // ---- epilogue of the tile: warpgroup 0 stores dV, warpgroup 1 stores dK ----
+      if (wt.n_items > 0) {
+        if (!mbar_wait_warp(acc_full, uint32_t(tcn) & 1, ctl, 186 + w)) { ok = false; break; }
+        tc_fence_after();
+      }
+      const int kr = wt.kv0 + rl;
       const bool row_ok = kr < shp.Nk;
       const float sc = w == 0 ? 1.f : shp.scale;
       const uint32_t tAcc = lane_base + uint32_t(w == 0 ? C::DV_COL : C::DK_COL);
       void* out = w == 0 ? dv_out : dk_out;
-      const long long off0 = w == 0 ? ((long long)b * dv_sb + (long long)kvh * dv_sh + (long long)kr * dv_sn)
-                                    : ((long long)b * dk_sb + (long long)kvh * dk_sh + (long long)kr * dk_sn);
-      if (n_items > 0) tc_fence_after();
+      const long long off0 = w == 0 ? ((long long)wt.b * dv_sb + (long long)wt.kvh * dv_sh + (long long)kr * dv_sn)
+                                    : ((long long)wt.b * dk_sb + (long long)wt.kvh * dk_sh + (long long)kr * dk_sn);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
-        float g[32];
-        if (n_items > 0) {
-          tmem_ld32(tAcc + cc * 32, g);
+        float gv[32];
+        if (wt.n_items > 0) {
+          tmem_ld32(tAcc + cc * 32, gv);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) g[i] = 0.f;
+          for (int i = 0; i < 32; ++i) gv[i] = 0.f;
         }
         if (!row_ok) continue;
         if (accumulate_fp32) {
@@ -792,10 +880,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
             float4 x = dst[v4];
-            x.x += g[v4 * 4 + 0] * sc;
-            x.y += g[v4 * 4 + 1] * sc;
-            x.z += g[v4 * 4 + 2] * sc;
-            x.w += g[v4 * 4 + 3] * sc;
+            x.x += gv[v4 * 4 + 0] * sc;
+            x.y += gv[v4 * 4 + 1] * sc;
+            x.z += gv[v4 * 4 + 2] * sc;
+            x.w += gv[v4 * 4 + 3] * sc;
             dst[v4] = x;
           }
         } else {
@@ -803,13 +891,19 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            pk.x = pack_half2(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
+            pk.y = pack_half2(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
+            pk.z = pack_half2(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
+            pk.w = pack_half2(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
+      }
+      if (wt.n_items > 0) {
+        tc_fence_before();
+        mbar_arrive(acc_empty);
+        gi += wt.n_items;
+        ++tcn;
       }
     }
   }
@@ -829,10 +923,12 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkvw::BM - 1) / bkvw::BM;
-  dim3 grid(unsigned(n_kt * a.shape.B * a.shape.Hkv));
-  kern<<<grid, bkvw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape,
-                                                             a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv,
-                                                             a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32);
+  const int n_tiles = n_kt * a.shape.B * a.shape.Hkv;
+  const int sms = device_sm_count();
+  const int n_cta = n_tiles < sms ? n_tiles : sms;
+  kern<<<dim3(unsigned(n_cta)), bkvw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
+      a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv, a.dv_sb,
+      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

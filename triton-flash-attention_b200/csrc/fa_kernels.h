@@ -35,6 +35,20 @@ struct BwdArgs {
   cudaStream_t stream;
 };
 
+// Number of SMs of the current device (cached per device); persistent
+// kernels launch at most one CTA per SM.
+inline int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 int launch_fwd(const FwdArgs& a, int D);
 int launch_bwd_dq(const BwdArgs& a, int D);
 int launch_bwd_dkdv(const BwdArgs& a, int D);
