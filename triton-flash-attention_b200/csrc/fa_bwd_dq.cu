@@ -351,7 +351,7 @@ namespace bdqw {
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per tile
 constexpr int NUM_THREADS = 384;
-constexpr int POLY_MASK = 4;  // pairs (i & 7) < 4 use the FMA-pipe exp2: half off MUFU
+constexpr int POLY_MASK = 2;  // pairs (i & 7) < 2 use the FMA-pipe exp2: a quarter off MUFU
 
 template <int D>
 struct Cfg {

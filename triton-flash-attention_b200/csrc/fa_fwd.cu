@@ -16,9 +16,11 @@
 //    attention.py:68-74), write P back to TMEM and rescale O in TMEM when the
 //    running maximum grows by more than 2^8 (lazy rescaling);
 //  * the softmax arithmetic is packed: a 3-input max tree and fma.rn.f32x2
-//    for s * scale*log2(e) - m; the exponentials are split between the MUFU
-//    unit (ex2.approx, 16 per clock per SM) and a polynomial on the FMA pipe
-//    (3 of every 8 pairs), which together beat the MUFU rate alone;
+//    for s * scale*log2(e) - m; the exponentials run on the MUFU unit
+//    (ex2.approx, 16 per clock per SM).  A share of them can go to a
+//    polynomial on the FMA pipe (POLY_MASK); measured, that no longer pays
+//    here: its extra ALU/FMA instructions slow the MMA issue on the same SM
+//    more than they relieve MUFU;
 //  * the two tiles ping-pong: while one warpgroup turns S into P, the tensor
 //    core runs the other tile's GEMMs.
 // TMEM: S_0 cols [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [256+D,256+2D).
@@ -34,7 +36,7 @@ constexpr int BN = 128;  // keys per K/V tile
 constexpr int QT = 2;    // query tiles per CTA
 constexpr int NUM_THREADS = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
-constexpr int POLY_MASK = 3;               // pairs (i & 7) < 3 use the FMA-pipe exp2
+constexpr int POLY_MASK = 0;               // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
 
 template <int D>
 struct Cfg {
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int i = 0; i < 16; ++i) {
           const int c0 = cc * 32 + 2 * i;
           const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
-          // 3 of every 8 pairs on the FMA pipe, the rest on MUFU
+          // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
           const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
           packed[i] = h2_from_f2(e);
           sum2[i & 3] = fadd2(sum2[i & 3], e);
