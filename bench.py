@@ -23,6 +23,12 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
   batch shard; no collective touches the data path.
 * ``--impl reference``: the reference's CPU implementation of the path (the
   oracle port of its SDPA fallback) on the host cores; rank 0 only.
+* ``--workload sweep``: the parity/measurement configurations C3 (non-causal,
+  B4 H16, D in {32,64,128} x N in {512,...,8192}) and C4 (GQA causal), forward
+  and forward+backward through the public API, one JSON line per
+  configuration, with the reference's Triton kernel (``backend="triton"``,
+  from baseline/_ref) timed beside it when installed.  Informational; the
+  metric line is the default workload.
 """
 
 from __future__ import annotations
@@ -482,6 +488,69 @@ def run_reference_gpu(args) -> None:
                                                                   / out["b200"]["ms_per_step"], 3)}), flush=True)
 
 
+SWEEP = ([("C3", 4, 16, 16, n, d, False) for d in (32, 64, 128) for n in (512, 1024, 2048, 2049, 4096, 8192)]
+         + [("C4", 2, 32, 8, 8191, 128, True)])
+
+
+def run_sweep(args) -> None:
+    """C3 / C4: forward-only and forward+backward TFLOP/s through the public
+    API (this build, and the reference's Triton kernel when baseline/_ref is
+    installed), CUDA events, one JSON line per configuration."""
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    impls = [("b200", fa.scaled_dot_product_attention, {})]
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if os.path.isdir(os.path.join(ref_dir, "triton_flash_attention")):
+        sys.path.insert(0, ref_dir)
+        import triton_flash_attention as ref
+
+        impls.append(("reference_triton", ref.scaled_dot_product_attention, {"backend": "triton"}))
+    dev = torch.device("cuda", 0)
+    steps = max(1, min(args.steps, 20))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    for name, b, hq, hkv, n, d, causal in SWEEP:
+        g = torch.Generator(device=dev).manual_seed(7 + n + d)
+        q = torch.randn(b, hq, n, d, device=dev, dtype=torch.float16, generator=g)
+        k, v = (torch.randn(b, hkv, n, d, device=dev, dtype=torch.float16, generator=g) for _ in range(2))
+        do = torch.randn(b, hq, n, d, device=dev, dtype=torch.float16, generator=g)
+        fl_f = fa.attention_flops(batch=b, query_heads=hq, sequence=n, head_dim=d, causal=causal, mode="forward")
+        fl_fb = fa.attention_flops(batch=b, query_heads=hq, sequence=n, head_dim=d, causal=causal, mode="forward-backward")
+        row = {"workload": "sweep", "config": name, "B": b, "Hq": hq, "Hkv": hkv, "N": n, "D": d, "causal": causal,
+               "unit": "TFLOP/s", "steps": steps}
+        for tag, sdpa, kw in impls:
+            qc, kc, vc = (t.clone().requires_grad_() for t in (q, k, v))
+            gqa = hq != hkv
+            with torch.no_grad():
+                ms_f = timed(lambda: sdpa(qc, kc, vc, is_causal=causal, enable_gqa=gqa, **kw))
+
+            def fwd_bwd():
+                o = sdpa(qc, kc, vc, is_causal=causal, enable_gqa=gqa, **kw)
+                o.backward(do)
+
+            ms_fb = timed(fwd_bwd)
+            row[tag] = {"fwd_ms": round(ms_f, 4), "fwd_tflops": round(fl_f / ms_f / 1e9, 1),
+                        "fwd_bwd_ms": round(ms_fb, 4), "fwd_bwd_tflops": round(fl_fb / ms_fb / 1e9, 1)}
+            del qc, kc, vc
+        print(json.dumps(row), flush=True)
+        del q, k, v, do
+        torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -489,8 +558,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c2", "ring"], default="c2",
-                    help="c2: the metric's configuration (default); ring: C5 ring context parallelism")
+    ap.add_argument("--workload", choices=["c2", "ring", "sweep"], default="c2",
+                    help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
+                         "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -501,6 +571,8 @@ def main() -> None:
         run_reference_gpu(args)
     elif args.workload == "ring":
         run_ring(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 
