@@ -48,7 +48,7 @@ if ROOT not in sys.path:
 B, H, N, D = 4, 16, 4096, 64
 CAUSAL = True
 WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
-DKDV_TRAFFIC_BYTES = 190_924_032 + 39_982_336
+DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472  # ncu dram__bytes_read.sum + dram__bytes_write.sum, one C2 launch (profiles/c2_kernels.md)
 
 
 def flops_step() -> int:
