@@ -48,7 +48,7 @@ if ROOT not in sys.path:
 B, H, N, D = 4, 16, 4096, 64
 CAUSAL = True
 WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
-DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472  # ncu dram__bytes_read.sum + dram__bytes_write.sum, one C2 launch (profiles/c2_kernels.md)
+DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472  # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch
 
 
 def flops_step() -> int:
@@ -275,7 +275,7 @@ def run_ours(args) -> None:
                                       mode="forward")
     achieved = kv_flops / (kv_ms * 1e-3) / 1e12
     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch of
-    # the dK/dV kernel (profiles/c2_kernels.md)
+    # the dK/dV kernel, from a --set full capture of this command
     traffic = DKDV_TRAFFIC_BYTES
     if rank == 0:
         line = {
