@@ -339,17 +339,20 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// D <= 64: 128-key tiles.  S = Q K^T and dP = dO V^T become N = 128 MMAs (full
-// tensor rate; N = 64 runs at ~70%).  One CTA owns one 128-row query tile;
-// both warpgroups work on every key tile, warpgroup w on key columns
+// D <= 64: persistent kernel with 128-key tiles.  S = Q K^T and dP = dO V^T
+// become N = 128 MMAs (full tensor rate; N = 64 runs at ~70%).  One CTA per SM
+// walks its share of the work tiles (128 query rows of one batch and head)
+// back to back, with Q and dO double-buffered so that the next tile's loads
+// and first MMAs overlap the current tile's last key tiles and its epilogue.
+// Both warpgroups work on every key tile, warpgroup w on key columns
 // [64w, 64w+64), and S is double-buffered in TMEM so the tensor core computes
 // S of tile j+2 and dP of tile j+1 while the warpgroups exponentiate tile j+1.
 // TMEM: S buffers [0,128) and [128,256), dP [256,384), dQ [384, 384+D).
 // Warpgroup w writes dS into its S buffer's columns [64w, 64w+32), inside the
 // range it read.
 namespace bdqw {
-constexpr int BM = 128;  // query rows per CTA
-constexpr int BN = 128;  // keys per tile
+constexpr int BM = 128;  // query rows per tile
+constexpr int BN = 128;  // keys per key tile
 constexpr int NUM_THREADS = 384;
 constexpr int POLY_MASK = 2;  // pairs (i & 7) < 2 use the FMA-pipe exp2: a quarter off MUFU
 
@@ -359,22 +362,48 @@ struct Cfg {
   static constexpr int NST = 4;
   static constexpr int Q_TILE_BYTES = BM * D * 2;
   static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = OFF_Q + Q_TILE_BYTES;
-  static constexpr int OFF_K = OFF_DO + Q_TILE_BYTES;      // NST stages
-  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;  // NST stages
+  static constexpr int OFF_Q = 0;                              // 2 buffers
+  static constexpr int OFF_DO = OFF_Q + 2 * Q_TILE_BYTES;      // 2 buffers
+  static constexpr int OFF_K = OFF_DO + 2 * Q_TILE_BYTES;      // NST stages
+  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;    // NST stages
   static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
-  // q_full, kv_full[NST], kv_empty[NST], s_full[2], dp_full, ds_ready[2], dq_full, mma_done
-  static constexpr int NUM_BARS = 1 + 2 * NST + 2 + 1 + 2 + 1 + 1;
+  // q_full[2], q_empty[2], kv_full[NST], kv_empty[NST], s_full[2], dp_full, ds_ready[2], dq_full, dq_empty, mma_done
+  static constexpr int NUM_BARS = 2 + 2 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
-  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED;
   static constexpr int TMEM_COLS = 512;
   static constexpr int DP_COL = 256;
   static constexpr int DQ_COL = 384;
   static_assert(D <= 64, "wide dQ path is for D <= 64");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
+
+// A work tile: 128 query rows of one (batch, query head) and the key tiles
+// they see.  Tiles are numbered late query tiles first (the heavy ones under
+// a causal mask).
+struct Tile {
+  int b, h, kvh, row0, n_kv;
+};
+__device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
+  const int BH = shp.B * shp.Hq;
+  const int n_qt = (shp.Nq + BM - 1) / BM;
+  Tile w;
+  const int bh = t % BH;
+  w.b = bh / shp.Hq;
+  w.h = bh % shp.Hq;
+  w.kvh = w.h / (shp.Hq / shp.Hkv);
+  w.row0 = (n_qt - 1 - t / BH) * BM;
+  w.n_kv = kv_tiles_for_rows(shp, w.row0, BM, BN);
+  return w;
+}
+// The k-th tile of CTA c when G CTAs share n tiles (snake order over rounds
+// of G); n when the CTA has no k-th tile.
+__device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
+  const int t = k * G + ((k & 1) ? G - 1 - c : c);
+  return t < n ? t : n;
+}
 }  // namespace bdqw
 
 template <int D>
@@ -383,7 +412,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                           const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                           void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh,
-                          const long long dq_sn, const int accumulate_fp32) {
+                          const long long dq_sn, const int accumulate_fp32, const int n_tiles) {
   using namespace bdqw;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -393,33 +422,30 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   const uint32_t sbase = smem_u32(smem);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
+  uint64_t* q_full = bars;          // per Q/dO buffer
+  uint64_t* q_empty = q_full + 2;   // per Q/dO buffer
+  uint64_t* kv_full = q_empty + 2;
   uint64_t* kv_empty = kv_full + C::NST;
   uint64_t* s_full = kv_empty + C::NST;
   uint64_t* dp_full = s_full + 2;
   uint64_t* ds_ready = dp_full + 1;  // per S buffer
-  uint64_t* dq_full = ds_ready + 2;
-  uint64_t* mma_done = dq_full + 1;
+  uint64_t* dq_full = ds_ready + 2;  // one phase per non-empty tile
+  uint64_t* dq_empty = dq_full + 1;  // one phase per non-empty tile: the epilogue read dQ
+  uint64_t* mma_done = dq_empty + 1;
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
   volatile CtaCtl* ctl = ctl_w;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
 
   const int warp = int(warp_id());
   const int lane = int(lane_id());
-
-  const int BH = shp.B * shp.Hq;
-  const int n_qt = (shp.Nq + BM - 1) / BM;
-  const int qt = n_qt - 1 - int(blockIdx.x) / BH;  // heavy (late) query tiles first
-  const int bh = int(blockIdx.x) % BH;
-  const int b = bh / shp.Hq;
-  const int h = bh % shp.Hq;
-  const int kvh = h / (shp.Hq / shp.Hkv);
-  const int row0 = qt * BM;
-  const int n_kv = kv_tiles_for_rows(shp, row0, BM, BN);
+  const int cta = int(blockIdx.x);
+  const int n_cta = int(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 2);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full + i, 2);
+      mbar_init(q_empty + i, 1);
+    }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(kv_full + s, 2);
       mbar_init(kv_empty + s, 1);
@@ -430,6 +456,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     mbar_init(ds_ready, 256);
     mbar_init(ds_ready + 1, 256);
     mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 256);
     mbar_init(mma_done, 1);
     ctl_w->abort = 0;
     ctl_w->status = shp.status;
@@ -450,94 +477,118 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     // TMA loads are processed one after another); q_full and kv_full expect
     // one arrival from each.
     const bool is_k = warp == 0;
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
       const CUtensorMap* tmap_qd = is_k ? &tmap_q : &tmap_do;
       const int kv_off = is_k ? C::OFF_K : C::OFF_V;
+      const int qd_off = is_k ? C::OFF_Q : C::OFF_DO;
       tma_prefetch_desc(tmap_qd);
       tma_prefetch_desc(tmap_kv);
-      mbar_arrive_expect_tx(q_full, C::Q_TILE_BYTES);
-      for (int bx = 0; bx < G::NBOX; ++bx)
-        tma_load_4d(smem + (is_k ? C::OFF_Q : C::OFF_DO) + bx * BM * G::SW, tmap_qd, q_full, bx * G::BOX, row0, h, b);
-      int n_iss = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % C::NST;
-        const uint32_t u = uint32_t(j / C::NST);
-        if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, 131)) break;
-        mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
+      int gj = 0, tcn = 0;  // key tiles and non-empty tiles issued
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = tile_index(cta, k, n_cta, n_tiles);
+        if (t >= n_tiles) break;
+        const Tile w = tile_of(shp, t);
+        if (w.n_kv == 0) continue;
+        const int tb = tcn & 1;
+        if (tcn >= 2 && !mbar_wait(q_empty + tb, uint32_t((tcn >> 1) - 1) & 1, ctl, 130)) break;
+        mbar_arrive_expect_tx(q_full + tb, C::Q_TILE_BYTES);
         for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                      j * BN, kvh, b);
-        ++n_iss;
+          tma_load_4d(smem + qd_off + tb * C::Q_TILE_BYTES + bx * BM * G::SW, tmap_qd, q_full + tb, bx * G::BOX,
+                      w.row0, w.h, w.b);
+        ++tcn;
+        for (int j = 0; j < w.n_kv; ++j, ++gj) {
+          const int s = gj % C::NST;
+          const uint32_t u = uint32_t(gj / C::NST);
+          if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, 131)) { ok = false; break; }
+          mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
+          for (int bx = 0; bx < G::NBOX; ++bx)
+            tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
+                        j * BN, w.kvh, w.b);
+        }
       }
-      mbar_wait_drain(q_full, 0, ctl, 132);
-      for (int j = (n_iss > C::NST ? n_iss - C::NST : 0); j < n_iss; ++j)
+      for (int i = (tcn > 2 ? tcn - 2 : 0); i < tcn; ++i)
+        mbar_wait_drain(q_full + (i & 1), uint32_t(i >> 1) & 1, ctl, 132);
+      for (int j = (gj > C::NST ? gj - C::NST : 0); j < gj; ++j)
         mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 133);
     }
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
       constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1);
-      const uint32_t q_s = sbase + C::OFF_Q;
-      const uint32_t do_s = sbase + C::OFF_DO;
       auto k_tile = [&](int j) { return sbase + C::OFF_K + (j % C::NST) * C::KV_TILE_BYTES; };
       auto v_tile = [&](int j) { return sbase + C::OFF_V + (j % C::NST) * C::KV_TILE_BYTES; };
       auto wait_kv = [&](int j, int site) {
-        return mbar_wait(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, site);
-      };
-      const SDesc qd = desc_k_base<D>(q_s);
-      const SDesc dd = desc_k_base<D>(do_s);
-      auto issue_s = [&](int j) {
-        const SDesc kd = desc_k_base<D>(k_tile(j));
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + (j & 1) * 128, sdesc_at(qd, k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)),
-                  IDESC_S, ks > 0);
-        umma_commit(s_full + (j & 1));
-      };
-      auto issue_dp = [&](int j) {
-        const SDesc vd = desc_k_base<D>(v_tile(j));
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + C::DP_COL, sdesc_at(dd, k_major_off<D, BM>(ks)), sdesc_at(vd, k_major_off<D, BN>(ks)),
-                  IDESC_S, ks > 0);
-        umma_commit(dp_full);
+        const bool r = mbar_wait(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, site);
+        tc_fence_after();
+        return r;
       };
       auto a_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
-      bool ok = mbar_wait(q_full, 0, ctl, 140) && wait_kv(0, 141);
-      if (ok) {
+      int gj = 0, tcn = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = tile_index(cta, k, n_cta, n_tiles);
+        if (t >= n_tiles) break;
+        const int n_kv = tile_of(shp, t).n_kv;
+        if (n_kv == 0) continue;
+        const int tb = tcn & 1;
+        if (!mbar_wait(q_full + tb, uint32_t(tcn >> 1) & 1, ctl, 140)) { ok = false; break; }
         tc_fence_after();
-        issue_s(0);
-        issue_dp(0);
+        const SDesc qd = desc_k_base<D>(sbase + C::OFF_Q + tb * C::Q_TILE_BYTES);
+        const SDesc dd = desc_k_base<D>(sbase + C::OFF_DO + tb * C::Q_TILE_BYTES);
+        // S buffer / barrier parities follow the CTA-wide key-tile count g
+        auto issue_s = [&](int g) {
+          const SDesc kd = desc_k_base<D>(k_tile(g));
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_ss(tmem + (g & 1) * 128, sdesc_at(qd, k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)),
+                    IDESC_S, ks > 0);
+          umma_commit(s_full + (g & 1));
+        };
+        auto issue_dp = [&](int g) {
+          const SDesc vd = desc_k_base<D>(v_tile(g));
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_ss(tmem + C::DP_COL, sdesc_at(dd, k_major_off<D, BM>(ks)), sdesc_at(vd, k_major_off<D, BN>(ks)),
+                    IDESC_S, ks > 0);
+          umma_commit(dp_full);
+        };
+        if (!wait_kv(gj, 141)) { ok = false; break; }
+        issue_s(gj);
+        issue_dp(gj);
         if (n_kv > 1) {
-          ok = wait_kv(1, 142);
-          if (ok) {
-            tc_fence_after();
-            issue_s(1);
+          if (!wait_kv(gj + 1, 142)) { ok = false; break; }
+          issue_s(gj + 1);
+        }
+        for (int j = 0; j < n_kv; ++j) {
+          const int g = gj + j;
+          if (!mbar_wait(ds_ready + (g & 1), uint32_t(g >> 1) & 1, ctl, 143)) { ok = false; break; }
+          // dQ of the previous tile was read by the epilogue
+          if (j == 0 && tcn > 0 && !mbar_wait(dq_empty, uint32_t(tcn - 1) & 1, ctl, 146)) { ok = false; break; }
+          tc_fence_after();
+          {
+            const SDesc kd = desc_mn_base<D, BN>(k_tile(g));
+            const uint32_t pa = tmem + (g & 1) * 128;
+            umma_ts(tmem + C::DQ_COL, pa, sdesc_at(kd, 0), IDESC_DQ, j > 0 ? 1u : 0u);
+#pragma unroll
+            for (int ks = 1; ks < BN / 16; ++ks)
+              umma_ts(tmem + C::DQ_COL, pa + a_col(ks), sdesc_at(kd, mn_major_off<D>(ks)), IDESC_DQ, 1u);
+          }
+          umma_commit(kv_empty + g % C::NST);
+          if (j + 1 < n_kv) issue_dp(g + 1);  // its stage was waited for before S(g+1)
+          if (j + 2 < n_kv) {
+            if (!wait_kv(g + 2, 144)) { ok = false; break; }
+            issue_s(g + 2);
           }
         }
+        if (!ok) break;
+        umma_commit(dq_full);
+        umma_commit(q_empty + tb);
+        gj += n_kv;
+        ++tcn;
       }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (!mbar_wait(ds_ready + (j & 1), uint32_t(j >> 1) & 1, ctl, 143)) { ok = false; break; }
-        tc_fence_after();
-        {
-          const SDesc kd = desc_mn_base<D, BN>(k_tile(j));
-          const uint32_t pa = tmem + (j & 1) * 128;
-          umma_ts(tmem + C::DQ_COL, pa, sdesc_at(kd, 0), IDESC_DQ, j > 0 ? 1u : 0u);
-#pragma unroll
-          for (int ks = 1; ks < BN / 16; ++ks)
-            umma_ts(tmem + C::DQ_COL, pa + a_col(ks), sdesc_at(kd, mn_major_off<D>(ks)), IDESC_DQ, 1u);
-        }
-        umma_commit(kv_empty + j % C::NST);
-        if (j + 1 < n_kv) issue_dp(j + 1);  // its stage was waited for before S(j+1)
-        if (j + 2 < n_kv) {
-          if (!wait_kv(j + 2, 144)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(j + 2);
-        }
-      }
-      if (ok) umma_commit(dq_full);
       umma_commit(mma_done);
       mbar_wait_drain(mma_done, 0, ctl, 145);
     }
@@ -545,83 +596,107 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     // =================== dS warpgroups ===================
     const int w = (warp - 4) / 4;  // key-column half of every tile
     const int wq = warp & 3;
-    const int r = row0 + wq * 32 + lane;
-    int lim = shp.Nk - 1;
-    if (shp.causal) {
-      const long long c = (long long)r + shp.q_off - shp.k_off;
-      lim = c < lim ? int(c) : lim;
-    }
-    const bool row_ok = r < shp.Nq;
-    float lse_r = INFINITY, delta_r = 0.f;
-    if (row_ok) {
-      const float x = lse[(long long)bh * shp.Nq + r];
-      lse_r = x == -INFINITY ? INFINITY : x;
-      delta_r = delta[(long long)bh * shp.Nq + r];
-    }
     const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
     const uint64_t c2x2 = f2pack(shp.scale_log2, shp.scale_log2);
-    const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
-    const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
+    // lse2 / Delta of this thread's row for the next tile are loaded one tile
+    // ahead, so their latency hides behind the current tile.
+    auto row_vals = [&](const Tile& wt, float& l, float& d) {
+      const int r = wt.row0 + wq * 32 + lane;
+      l = INFINITY;
+      d = 0.f;
+      if (r < shp.Nq && wt.n_kv > 0) {
+        const long long bh = (long long)wt.b * shp.Hq + wt.h;
+        const float x = lse[bh * shp.Nq + r];
+        l = x == -INFINITY ? INFINITY : x;
+        d = delta[bh * shp.Nq + r];
+      }
+    };
+    int t_cur = tile_index(cta, 0, n_cta, n_tiles);
+    Tile wt = tile_of(shp, t_cur < n_tiles ? t_cur : 0);
+    float lse_n = INFINITY, delta_n = 0.f;
+    if (t_cur < n_tiles) row_vals(wt, lse_n, delta_n);
+    int gj = 0, tcn = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait_warp(s_full + (j & 1), uint32_t(j >> 1) & 1, ctl, 150 + w)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tS = lane_base + uint32_t((j & 1) * 128 + 64 * w);
-      float sv[64];
-      tmem_ld64(tS, sv);
-      const int lim_j = lim - j * BN - 64 * w;  // last visible column of this half
-      if (lim_j < 63) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) sv[c] = c <= lim_j ? sv[c] : -INFINITY;
+    for (int k = 0; ok && t_cur < n_tiles; ++k) {
+      const Tile cur = wt;
+      const float lse_r = lse_n, delta_r = delta_n;
+      t_cur = tile_index(cta, k + 1, n_cta, n_tiles);
+      if (t_cur < n_tiles) {
+        wt = tile_of(shp, t_cur);
+        row_vals(wt, lse_n, delta_n);
       }
-      uint32_t pk_p[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint64_t x = ffma2(f2pack(sv[2 * i], sv[2 * i + 1]), c2x2, nlse2);
-        pk_p[i] = h2_from_f2((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
+      const int r = cur.row0 + wq * 32 + lane;
+      int lim = shp.Nk - 1;
+      if (shp.causal) {
+        const long long c = (long long)r + shp.q_off - shp.k_off;
+        lim = c < lim ? int(c) : lim;
       }
-      if (!mbar_wait_warp(dp_full, uint32_t(j) & 1, ctl, 152 + w)) { ok = false; break; }
-      tc_fence_after();
-      float dp[64];
-      tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
-      uint32_t pk_ds[32];
+      const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
+      const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
+      for (int j = 0; j < cur.n_kv; ++j) {
+        const int g = gj + j;
+        if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 150 + w)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * w);
+        float sv[64];
+        tmem_ld64(tS, sv);
+        const int lim_j = lim - j * BN - 64 * w;  // last visible column of this half
+        if (lim_j < 63) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        pk_ds[i] = hmul2(pk_p[i], h2_from_f2(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
-      tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
-      tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(ds_ready + (j & 1));
-    }
-    // ---- epilogue: warpgroup w stores dQ columns [w*D/2, (w+1)*D/2) ----
-    if (ok && n_kv > 0) ok = mbar_wait_warp(dq_full, 0, ctl, 154 + w);
-    if (ok) {
-      if (n_kv > 0) tc_fence_after();
+          for (int c = 0; c < 64; ++c) sv[c] = c <= lim_j ? sv[c] : -INFINITY;
+        }
+        uint32_t pk_p[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint64_t x = ffma2(f2pack(sv[2 * i], sv[2 * i + 1]), c2x2, nlse2);
+          pk_p[i] = h2_from_f2((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
+        }
+        if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 152 + w)) { ok = false; break; }
+        tc_fence_after();
+        float dp[64];
+        tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
+        uint32_t pk_ds[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          pk_ds[i] = hmul2(pk_p[i], h2_from_f2(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+        tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+        tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(ds_ready + (g & 1));
+      }
+      if (!ok) break;
+      // ---- epilogue of the tile: warpgroup w stores dQ columns [w*D/2, (w+1)*D/2) ----
+      if (cur.n_kv > 0) {
+        if (!mbar_wait_warp(dq_full, uint32_t(tcn) & 1, ctl, 154 + w)) { ok = false; break; }
+        tc_fence_after();
+      }
       const float sc = shp.scale;
       constexpr int HALF = D / 2;
-      float g[HALF];
-      if (n_kv > 0) {
+      float gv[HALF];
+      if (cur.n_kv > 0) {
         if constexpr (HALF == 32) {
-          tmem_ld32(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[32]>(&g[0]));
+          tmem_ld32(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[32]>(&gv[0]));
         } else {
-          tmem_ld16(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[16]>(&g[0]));
+          tmem_ld16(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[16]>(&gv[0]));
         }
+        tc_fence_before();
+        mbar_arrive(dq_empty);
       } else {
 #pragma unroll
-        for (int i = 0; i < HALF; ++i) g[i] = 0.f;
+        for (int i = 0; i < HALF; ++i) gv[i] = 0.f;
       }
-      if (row_ok) {
-        const long long off = (long long)b * dq_sb + (long long)h * dq_sh + (long long)r * dq_sn + w * HALF;
+      if (r < shp.Nq) {
+        const long long off = (long long)cur.b * dq_sb + (long long)cur.h * dq_sh + (long long)r * dq_sn + w * HALF;
         if (accumulate_fp32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
 #pragma unroll
           for (int v4 = 0; v4 < HALF / 4; ++v4) {
             float4 x = dst[v4];
-            x.x += g[v4 * 4 + 0] * sc;
-            x.y += g[v4 * 4 + 1] * sc;
-            x.z += g[v4 * 4 + 2] * sc;
-            x.w += g[v4 * 4 + 3] * sc;
+            x.x += gv[v4 * 4 + 0] * sc;
+            x.y += gv[v4 * 4 + 1] * sc;
+            x.z += gv[v4 * 4 + 2] * sc;
+            x.w += gv[v4 * 4 + 3] * sc;
             dst[v4] = x;
           }
         } else {
@@ -629,13 +704,17 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
 #pragma unroll
           for (int v8 = 0; v8 < HALF / 8; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            pk.x = pack_half2(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
+            pk.y = pack_half2(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
+            pk.z = pack_half2(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
+            pk.w = pack_half2(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
+      }
+      if (cur.n_kv > 0) {
+        gj += cur.n_kv;
+        ++tcn;
       }
     }
   }
@@ -655,10 +734,12 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
-  dim3 grid(unsigned(n_qt * a.shape.B * a.shape.Hq));
-  kern<<<grid, bdqw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape,
-                                                             a.lse, a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
-                                                             a.accumulate_fp32);
+  const int n_tiles = n_qt * a.shape.B * a.shape.Hq;
+  const int sms = device_sm_count();
+  const int n_cta = n_tiles < sms ? n_tiles : sms;
+  kern<<<dim3(unsigned(n_cta)), bdqw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
+      a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
+      a.accumulate_fp32, n_tiles);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
