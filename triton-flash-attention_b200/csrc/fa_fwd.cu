@@ -5,9 +5,13 @@
 // log-sum-exp lse2 = m + log2(l) per query row (attention.py:230).  The
 // design is Blackwell-native rather than a translation:
 //
-//  * one CTA owns 2 query tiles of 128 rows (256 rows) of one (batch, head);
-//  * warp 0 streams K/V tiles of 128 keys through a ring of shared-memory
-//    stages with TMA (128- or 64-byte swizzle);
+//  * a work unit is 2 query tiles of 128 rows (256 rows) of one (batch,
+//    head); the kernel is persistent: one CTA per SM walks its share of the
+//    units back to back, so the next unit's Q load and first S MMAs overlap
+//    the current unit's last key tiles and its epilogue (Q is
+//    double-buffered where shared memory allows, D <= 64);
+//  * warps 0 and 3 stream K and V tiles of 128 keys through a ring of
+//    shared-memory stages with TMA (128- or 64-byte swizzle);
 //  * warp 1 (one thread) issues tcgen05.mma: S_t = Q_t K^T into TMEM, then
 //    O_t += P_t V with P_t read straight from TMEM (fp16, aliasing S_t);
 //  * warps 4-7 and 8-11 are the softmax warpgroups of tile 0 and tile 1, one
@@ -33,25 +37,35 @@ namespace fwd {
 
 constexpr int BM = 128;  // query rows per tile
 constexpr int BN = 128;  // keys per K/V tile
-constexpr int QT = 2;    // query tiles per CTA
+constexpr int QT = 2;    // query tiles per work unit
 constexpr int NUM_THREADS = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int POLY_MASK = 0;               // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
+// Registers per thread: launched at 168 (384 threads); the control
+// warpgroup (warps 0-3) drops to CTRL_REGS and the two softmax warpgroups
+// rise to SOFT_REGS.  128 * CTRL_REGS + 256 * SOFT_REGS must not exceed
+// 384 * 168 = 64512.
+constexpr uint32_t LAUNCH_REGS = 168;
+constexpr uint32_t CTRL_REGS = 64;
+constexpr uint32_t SOFT_REGS = 216;
+static_assert(128 * CTRL_REGS + 256 * SOFT_REGS <= NUM_THREADS * LAUNCH_REGS, "register split");
 
 template <int D>
 struct Cfg {
   using G = TileGeom<D>;
   static constexpr int NST = D == 128 ? 2 : 3;
+  static constexpr int QB = D == 128 ? 1 : 2;  // Q buffers (units in flight)
   static constexpr int Q_TILE_BYTES = BM * D * 2;
+  static constexpr int Q_UNIT_BYTES = QT * Q_TILE_BYTES;
   static constexpr int KV_TILE_BYTES = BN * D * 2;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + QT * Q_TILE_BYTES;
+  static constexpr int OFF_K = OFF_Q + QB * Q_UNIT_BYTES;
   static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;
   static constexpr int OW = D;  // O columns in TMEM
   static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
-  // barriers: q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
-  //           s_full[QT], p_ready[QT], o_full[QT], mma_done
-  static constexpr int NUM_BARS = 1 + 4 * NST + 3 * QT + 1;
+  // barriers: q_full[QB], q_empty[QB], k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
+  //           s_full[QT], p_ready[QT], o_full[QT], o_empty[QT], mma_done
+  static constexpr int NUM_BARS = 2 * QB + 4 * NST + 4 * QT + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   // + alignment slack; at least 116 KB so that one CTA (and its 512 TMEM
@@ -62,21 +76,38 @@ struct Cfg {
   static constexpr int O_COL0 = QT * BN;
   static constexpr int TMEM_COLS = 512;
   static_assert(O_COL0 + QT * OW <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-struct Smem {
-  uint64_t* q_full;
-  uint64_t* k_full;
-  uint64_t* k_empty;
-  uint64_t* v_full;
-  uint64_t* v_empty;
-  uint64_t* s_full;
-  uint64_t* p_ready;
-  uint64_t* o_full;
-  uint64_t* mma_done;
-  uint32_t* tmem_base;
-  CtaCtl* ctl;
+// A work unit: QT query tiles of one (batch, head); n_kv[t] key tiles each.
+// Units are numbered late query blocks first (the heavy ones under a causal
+// mask).
+struct Unit {
+  int b, h, kvh, row0, n_kv[QT], n_max;
 };
+__device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
+  const int BH = shp.B * shp.Hq;
+  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
+  Unit w;
+  const int bh = u % BH;
+  w.b = bh / shp.Hq;
+  w.h = bh % shp.Hq;
+  w.kvh = w.h / (shp.Hq / shp.Hkv);
+  w.row0 = (n_qblk - 1 - u / BH) * QT * BM;
+  w.n_max = 0;
+#pragma unroll
+  for (int t = 0; t < QT; ++t) {
+    w.n_kv[t] = kv_tiles_for_rows(shp, w.row0 + t * BM, BM, BN);
+    w.n_max = w.n_kv[t] > w.n_max ? w.n_kv[t] : w.n_max;
+  }
+  return w;
+}
+// The k-th unit of CTA c when G CTAs share n units (snake order over rounds
+// of G); n when the CTA has no k-th unit.
+__device__ __forceinline__ int unit_index(int c, int k, int G, int n) {
+  const int t = k * G + ((k & 1) ? G - 1 - c : c);
+  return t < n ? t : n;
+}
 
 }  // namespace fwd
 
@@ -84,7 +115,8 @@ template <int D>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, __half* __restrict__ o_ptr,
-                  const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr) {
+                  const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr,
+                  const int n_units) {
   using namespace fwd;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -94,276 +126,318 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
   const uint32_t sbase = smem_u32(smem);
 
-  Smem sm;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  sm.q_full = bars;
-  sm.k_full = bars + 1;
-  sm.k_empty = sm.k_full + C::NST;
-  sm.v_full = sm.k_empty + C::NST;
-  sm.v_empty = sm.v_full + C::NST;
-  sm.s_full = sm.v_empty + C::NST;
-  sm.p_ready = sm.s_full + QT;
-  sm.o_full = sm.p_ready + QT;
-  sm.mma_done = sm.o_full + QT;
-  sm.tmem_base = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
-  sm.ctl = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
-  volatile CtaCtl* ctl = sm.ctl;
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = q_full + C::QB;
+  uint64_t* k_full = q_empty + C::QB;
+  uint64_t* k_empty = k_full + C::NST;
+  uint64_t* v_full = k_empty + C::NST;
+  uint64_t* v_empty = v_full + C::NST;
+  // per query tile t: s_full / p_ready complete once per key tile of t,
+  // o_full / o_empty once per unit in which t sees a key
+  uint64_t* s_full = v_empty + C::NST;
+  uint64_t* p_ready = s_full + QT;
+  uint64_t* o_full = p_ready + QT;
+  uint64_t* o_empty = o_full + QT;
+  uint64_t* mma_done = o_empty + QT;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
+  volatile CtaCtl* ctl = ctl_w;
 
   const int warp = int(warp_id());
   const int lane = int(lane_id());
-
-  // ---- work item: heavy (late, causal) query blocks first ----
-  const int BH = shp.B * shp.Hq;
-  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
-  const int qblk = n_qblk - 1 - int(blockIdx.x) / BH;
-  const int bh = int(blockIdx.x) % BH;
-  const int b = bh / shp.Hq;
-  const int h = bh % shp.Hq;
-  const int kvh = h / (shp.Hq / shp.Hkv);
-  const int row0 = qblk * QT * BM;
-  int n_kv[QT];
-#pragma unroll
-  for (int t = 0; t < QT; ++t) n_kv[t] = kv_tiles_for_rows(shp, row0 + t * BM, BM, BN);
-  const int n_max = n_kv[0] > n_kv[1] ? n_kv[0] : n_kv[1];
+  const int cta = int(blockIdx.x);
+  const int n_cta = int(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(sm.q_full, 1);
+    for (int i = 0; i < C::QB; ++i) {
+      mbar_init(q_full + i, 1);
+      mbar_init(q_empty + i, 1);
+    }
     for (int s = 0; s < C::NST; ++s) {
-      mbar_init(sm.k_full + s, 1);
-      mbar_init(sm.k_empty + s, 1);
-      mbar_init(sm.v_full + s, 1);
-      mbar_init(sm.v_empty + s, 1);
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
     }
     for (int t = 0; t < QT; ++t) {
-      mbar_init(sm.s_full + t, 1);
-      mbar_init(sm.p_ready + t, 128);
-      mbar_init(sm.o_full + t, 1);
+      mbar_init(s_full + t, 1);
+      mbar_init(p_ready + t, 128);
+      mbar_init(o_full + t, 1);
+      mbar_init(o_empty + t, 128);
     }
-    mbar_init(sm.mma_done, 1);
-    sm.ctl->abort = 0;
-    sm.ctl->status = shp.status;
+    mbar_init(mma_done, 1);
+    ctl_w->abort = 0;
+    ctl_w->status = shp.status;
     fence_mbar_init();
   }
   if (warp == 2) {
-    tmem_alloc(sm.tmem_base, C::TMEM_COLS);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *sm.tmem_base;
+  const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 3) {
-    // =================== TMA producers ===================
-    // Warp 0 loads Q and the K tiles, warp 3 the V tiles: one thread's TMA
-    // loads are processed one after another (~0.5 us per 16 KB box measured),
-    // so K and V come from two threads to double the stream rate.
-    const bool is_k = warp == 0;
-    if (lane == 0 && n_max > 0) {
-      const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
-      uint64_t* kv_full = is_k ? sm.k_full : sm.v_full;
-      uint64_t* kv_empty = is_k ? sm.k_empty : sm.v_empty;
-      const int kv_off = is_k ? C::OFF_K : C::OFF_V;
-      tma_prefetch_desc(tmap_kv);
-      if (is_k) {
-        tma_prefetch_desc(&tmap_q);
-        int q_bytes = 0;
-        for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? C::Q_TILE_BYTES : 0;
-        mbar_arrive_expect_tx(sm.q_full, q_bytes);
-        for (int t = 0; t < QT; ++t) {
-          if (n_kv[t] == 0) continue;
-          for (int bx = 0; bx < G::NBOX; ++bx)
-            tma_load_4d(smem + C::OFF_Q + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q, sm.q_full, bx * G::BOX,
-                        row0 + t * BM, h, b);
+  if (warp < 4) {
+    regs_release<CTRL_REGS>();
+    if (warp == 0 || warp == 3) {
+      // =================== TMA producers ===================
+      // Warp 0 loads Q and the K tiles, warp 3 the V tiles: one thread's TMA
+      // loads are processed one after another (~0.5 us per 16 KB box measured),
+      // so K and V come from two threads to double the stream rate.
+      const bool is_k = warp == 0;
+      if (lane == 0) {
+        const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
+        uint64_t* kv_full = is_k ? k_full : v_full;
+        uint64_t* kv_empty = is_k ? k_empty : v_empty;
+        const int kv_off = is_k ? C::OFF_K : C::OFF_V;
+        tma_prefetch_desc(tmap_kv);
+        if (is_k) tma_prefetch_desc(&tmap_q);
+        int gj = 0, uc = 0;  // key tiles and non-empty units issued
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          const int ui = unit_index(cta, k, n_cta, n_units);
+          if (ui >= n_units) break;
+          const Unit w = unit_of(shp, ui);
+          if (w.n_max == 0) continue;
+          if (is_k) {
+            const int qb = uc % C::QB;
+            if (uc >= C::QB && !mbar_wait(q_empty + qb, uint32_t(uc / C::QB - 1) & 1, ctl, 6)) break;
+            int q_bytes = 0;
+            for (int t = 0; t < QT; ++t) q_bytes += w.n_kv[t] > 0 ? C::Q_TILE_BYTES : 0;
+            mbar_arrive_expect_tx(q_full + qb, q_bytes);
+            for (int t = 0; t < QT; ++t) {
+              if (w.n_kv[t] == 0) continue;
+              for (int bx = 0; bx < G::NBOX; ++bx)
+                tma_load_4d(smem + C::OFF_Q + qb * C::Q_UNIT_BYTES + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q,
+                            q_full + qb, bx * G::BOX, w.row0 + t * BM, w.h, w.b);
+            }
+          }
+          ++uc;
+          for (int j = 0; j < w.n_max; ++j, ++gj) {
+            const int s = gj % C::NST;
+            const uint32_t u = uint32_t(gj / C::NST);
+            if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, is_k ? 1 : 2)) { ok = false; break; }
+            mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
+            for (int bx = 0; bx < G::NBOX; ++bx)
+              tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
+                          j * BN, w.kvh, w.b);
+          }
         }
+        // Drain: every load this thread issued must land before the CTA exits.
+        // On the normal path these phases have completed already.
+        if (is_k)
+          for (int i = (uc > C::QB ? uc - C::QB : 0); i < uc; ++i)
+            mbar_wait_drain(q_full + i % C::QB, uint32_t(i / C::QB) & 1, ctl, 3);
+        for (int j = (gj > C::NST ? gj - C::NST : 0); j < gj; ++j)
+          mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, is_k ? 4 : 5);
       }
-      int n_iss = 0;
-      for (int j = 0; j < n_max; ++j) {
-        const int s = j % C::NST;
-        const uint32_t u = uint32_t(j / C::NST);
-        if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, is_k ? 1 : 2)) break;
-        mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                      j * BN, kvh, b);
-        ++n_iss;
-      }
-      // Drain: every load this thread issued must land before the CTA exits.
-      // On the normal path these phases have completed already.
-      if (is_k) mbar_wait_drain(sm.q_full, 0, ctl, 3);
-      for (int j = (n_iss > C::NST ? n_iss - C::NST : 0); j < n_iss; ++j)
-        mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, is_k ? 4 : 5);
-    }
-  } else if (warp == 1) {
-    // =================== tcgen05 MMA issuer ===================
-    if (lane == 0 && n_max > 0) {
-      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
-      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, C::OW, 0, 1);
-      const uint32_t q_s = sbase + C::OFF_Q;
-      const uint32_t k_s = sbase + C::OFF_K;
-      const uint32_t v_s = sbase + C::OFF_V;
-      // descriptor bases (the issue loops below only add constants)
-      SDesc qd[QT];
-#pragma unroll
-      for (int t = 0; t < QT; ++t) qd[t] = desc_k_base<D>(q_s + t * C::Q_TILE_BYTES);
-      auto issue_s = [&](int t, int j) {
-        const SDesc kd = desc_k_base<D>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
-        const uint32_t dst = tmem + C::S_COL0 + t * BN;
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(dst, sdesc_at(qd[t], k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)), IDESC_S,
-                  ks > 0);
-        umma_commit(sm.s_full + t);
-      };
-      auto issue_pv = [&](int t, int j) {
-        // the D columns of V span NBOX boxes BN*SW bytes apart (LBO)
-        const SDesc vd = desc_mn_base<D, BN>(v_s + (j % C::NST) * C::KV_TILE_BYTES);
-        const uint32_t dst = tmem + C::O_COL0 + t * C::OW;
-        const uint32_t pa = tmem + C::S_COL0 + t * BN;
-        umma_ts(dst, pa, sdesc_at(vd, 0), IDESC_PV, j > 0 ? 1u : 0u);
-#pragma unroll
-        for (int ks = 1; ks < BN / 16; ++ks) umma_ts(dst, pa + ks * 8, sdesc_at(vd, mn_major_off<D>(ks)), IDESC_PV, 1u);
-      };
-      bool ok = mbar_wait(sm.q_full, 0, ctl, 10) && mbar_wait(sm.k_full, 0, ctl, 11);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < QT; ++t)
-          if (n_kv[t] > 0) issue_s(t, 0);
-        umma_commit(sm.k_empty);
-      }
-      for (int j = 0; j < n_max && ok; ++j) {
-        const int s = j % C::NST;
-        if (!mbar_wait(sm.v_full + s, uint32_t(j / C::NST) & 1, ctl, 12)) { ok = false; break; }
-        const bool more = j + 1 < n_max;
-        if (more && !mbar_wait(sm.k_full + (j + 1) % C::NST, uint32_t((j + 1) / C::NST) & 1, ctl, 13)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        for (int t = 0; t < QT && ok; ++t) {
-          if (j >= n_kv[t]) continue;
-          if (!mbar_wait(sm.p_ready + t, uint32_t(j) & 1, ctl, 14)) { ok = false; break; }
+    } else if (warp == 1) {
+      // =================== tcgen05 MMA issuer ===================
+      if (lane == 0) {
+        constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
+        constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, C::OW, 0, 1);
+        const uint32_t k_s = sbase + C::OFF_K;
+        const uint32_t v_s = sbase + C::OFF_V;
+        int gj = 0, uc = 0;
+        int cnt[QT] = {0, 0};  // key tiles of query tile t so far (s_full / p_ready phases)
+        int oc[QT] = {0, 0};   // units in which tile t saw a key (o_full / o_empty phases)
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          const int ui = unit_index(cta, k, n_cta, n_units);
+          if (ui >= n_units) break;
+          const Unit w = unit_of(shp, ui);
+          if (w.n_max == 0) continue;
+          const int qb = uc % C::QB;
+          if (!mbar_wait(q_full + qb, uint32_t(uc / C::QB) & 1, ctl, 10)) { ok = false; break; }
+          // descriptor bases (the issue loops below only add constants)
+          SDesc qd[QT];
+  #pragma unroll
+          for (int t = 0; t < QT; ++t) qd[t] = desc_k_base<D>(sbase + C::OFF_Q + qb * C::Q_UNIT_BYTES + t * C::Q_TILE_BYTES);
+          auto issue_s = [&](int t, int g) {
+            const SDesc kd = desc_k_base<D>(k_s + (g % C::NST) * C::KV_TILE_BYTES);
+            const uint32_t dst = tmem + C::S_COL0 + t * BN;
+  #pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks)
+              umma_ss(dst, sdesc_at(qd[t], k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)), IDESC_S,
+                      ks > 0);
+            umma_commit(s_full + t);
+          };
+          auto issue_pv = [&](int t, int g, bool acc) {
+            // the D columns of V span NBOX boxes BN*SW bytes apart (LBO)
+            const SDesc vd = desc_mn_base<D, BN>(v_s + (g % C::NST) * C::KV_TILE_BYTES);
+            const uint32_t dst = tmem + C::O_COL0 + t * C::OW;
+            const uint32_t pa = tmem + C::S_COL0 + t * BN;
+            umma_ts(dst, pa, sdesc_at(vd, 0), IDESC_PV, acc ? 1u : 0u);
+  #pragma unroll
+            for (int ks = 1; ks < BN / 16; ++ks)
+              umma_ts(dst, pa + ks * 8, sdesc_at(vd, mn_major_off<D>(ks)), IDESC_PV, 1u);
+          };
+          if (!mbar_wait(k_full + gj % C::NST, uint32_t(gj / C::NST) & 1, ctl, 11)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < n_kv[t]) issue_s(t, j + 1);
+          for (int t = 0; t < QT; ++t)
+            if (w.n_kv[t] > 0) issue_s(t, gj);
+          umma_commit(k_empty + gj % C::NST);
+          for (int j = 0; j < w.n_max && ok; ++j) {
+            const int g = gj + j;
+            const int s = g % C::NST;
+            if (!mbar_wait(v_full + s, uint32_t(g / C::NST) & 1, ctl, 12)) { ok = false; break; }
+            const bool more = j + 1 < w.n_max;
+            if (more && !mbar_wait(k_full + (g + 1) % C::NST, uint32_t((g + 1) / C::NST) & 1, ctl, 13)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            for (int t = 0; t < QT && ok; ++t) {
+              if (j >= w.n_kv[t]) continue;
+              if (!mbar_wait(p_ready + t, uint32_t(cnt[t]) & 1, ctl, 14)) { ok = false; break; }
+              // O_t of the previous unit was read by its epilogue
+              if (j == 0 && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv(t, g, j > 0);
+              ++cnt[t];
+              if (j + 1 < w.n_kv[t]) issue_s(t, g + 1);
+            }
+            if (!ok) break;
+            umma_commit(v_empty + s);
+            if (more) umma_commit(k_empty + (g + 1) % C::NST);
+          }
+          if (!ok) break;
+          for (int t = 0; t < QT; ++t)
+            if (w.n_kv[t] > 0) {
+              umma_commit(o_full + t);
+              ++oc[t];
+            }
+          umma_commit(q_empty + qb);
+          gj += w.n_max;
+          ++uc;
         }
-        if (!ok) break;
-        umma_commit(sm.v_empty + s);
-        if (more) umma_commit(sm.k_empty + (j + 1) % C::NST);
+        // Drain every MMA this thread issued before the CTA tears down TMEM.
+        umma_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, ctl, 15);
       }
-      if (ok) {
-        for (int t = 0; t < QT; ++t)
-          if (n_kv[t] > 0) umma_commit(sm.o_full + t);
-      }
-      // Drain every MMA this thread issued before the CTA tears down TMEM.
-      umma_commit(sm.mma_done);
-      mbar_wait_drain(sm.mma_done, 0, ctl, 15);
     }
-  } else if (warp >= 4) {
+  } else {
+    regs_claim<SOFT_REGS>();
     // =================== softmax warpgroups ===================
     const int t = (warp - 4) / 4;       // query tile of this warpgroup
     const int wq = warp & 3;            // TMEM lane quadrant this warp may access
     const int row_local = wq * 32 + lane;
-    const int r = row0 + t * BM + row_local;  // query row
-    const int nt = n_kv[t];
-    // last visible key column of this row (local key index)
-    int lim = shp.Nk - 1;
-    if (shp.causal) {
-      const long long c = (long long)r + shp.q_off - shp.k_off;
-      lim = c < lim ? int(c) : lim;  // may be negative: no visible key
-    }
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::S_COL0 + t * BN));
     const uint32_t tO = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::O_COL0 + t * C::OW));
     const float c2 = shp.scale_log2;
     const uint64_t c2x2 = f2pack(c2, c2);
-    float m = -INFINITY;  // running exponent base (scaled log2 units)
-    float l = 0.f;        // running row sum of exp2(s * c2 - m)
+    int cnt = 0, oc = 0;  // phases of s_full / o_full of this tile
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (!mbar_wait_warp(sm.s_full + t, uint32_t(j) & 1, ctl, 20 + t)) { ok = false; break; }
-      tc_fence_after();
-      float s[BN];
-      tmem_ld64(tS, *reinterpret_cast<float(*)[64]>(&s[0]));
-      tmem_ld64(tS + 64, *reinterpret_cast<float(*)[64]>(&s[64]));
-      const int lim_j = lim - j * BN;  // last visible local column in this tile
-      if (lim_j < BN - 1) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
+    for (int k = 0; ok; ++k) {
+      const int ui = unit_index(cta, k, n_cta, n_units);
+      if (ui >= n_units) break;
+      const Unit w = unit_of(shp, ui);
+      const int r = w.row0 + t * BM + row_local;  // query row
+      const int nt = w.n_kv[t];
+      // last visible key column of this row (local key index)
+      int lim = shp.Nk - 1;
+      if (shp.causal) {
+        const long long c = (long long)r + shp.q_off - shp.k_off;
+        lim = c < lim ? int(c) : lim;  // may be negative: no visible key
       }
-      // row max: 8 independent 3-input max chains, then a short tree
-      float a8[8];
+      float m = -INFINITY;  // running exponent base (scaled log2 units)
+      float l = 0.f;        // running row sum of exp2(s * c2 - m)
+      for (int j = 0; j < nt; ++j) {
+        if (!mbar_wait_warp(s_full + t, uint32_t(cnt) & 1, ctl, 20 + t)) { ok = false; break; }
+        tc_fence_after();
+        float s[BN];
+        tmem_ld64(tS, *reinterpret_cast<float(*)[64]>(&s[0]));
+        tmem_ld64(tS + 64, *reinterpret_cast<float(*)[64]>(&s[64]));
+        const int lim_j = lim - j * BN;  // last visible local column in this tile
+        if (lim_j < BN - 1) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float acc = fmax3(s[k * 16], s[k * 16 + 1], s[k * 16 + 2]);
-#pragma unroll
-        for (int i = 3; i < 15; i += 2) acc = fmax3(acc, s[k * 16 + i], s[k * 16 + i + 1]);
-        a8[k] = fmaxf(acc, s[k * 16 + 15]);
-      }
-      const float mx = fmax3(fmax3(a8[0], a8[1], a8[2]), fmax3(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
-      const float m_tile = mx * c2;
-      bool rescale = false;
-      float m_new = m;
-      if (m_tile > m + RESCALE_THRESHOLD) {  // false while m_tile == -inf
-        m_new = m_tile;
-        rescale = true;
-      }
-      const float alpha = rescale ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 on the first tile
-      const float base = m_new == -INFINITY ? 0.f : m_new;
-      const uint64_t nb2 = f2pack(-base, -base);
-      uint64_t sum2[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c0 = cc * 32 + 2 * i;
-          const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
-          // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
-          const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
-          packed[i] = h2_from_f2(e);
-          sum2[i & 3] = fadd2(sum2[i & 3], e);
+          for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
         }
-        tmem_st16(tS + cc * 16, packed);
-      }
-      {
-        float s0, s1, s2, s3, s4, s5, s6, s7;
-        f2unpack(sum2[0], s0, s1);
-        f2unpack(sum2[1], s2, s3);
-        f2unpack(sum2[2], s4, s5);
-        f2unpack(sum2[3], s6, s7);
-        l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)));
-      }
-      m = m_new;
-      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        // O *= alpha
+        // row max: 8 independent 3-input max chains, then a short tree
+        float a8[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          float acc = fmax3(s[kk * 16], s[kk * 16 + 1], s[kk * 16 + 2]);
+#pragma unroll
+          for (int i = 3; i < 15; i += 2) acc = fmax3(acc, s[kk * 16 + i], s[kk * 16 + i + 1]);
+          a8[kk] = fmaxf(acc, s[kk * 16 + 15]);
+        }
+        const float mx = fmax3(fmax3(a8[0], a8[1], a8[2]), fmax3(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
+        const float m_tile = mx * c2;
+        bool rescale = false;
+        float m_new = m;
+        if (m_tile > m + RESCALE_THRESHOLD) {  // false while m_tile == -inf
+          m_new = m_tile;
+          rescale = true;
+        }
+        const float alpha = rescale ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 on the first tile
+        const float base = m_new == -INFINITY ? 0.f : m_new;
+        const uint64_t nb2 = f2pack(-base, -base);
+        uint64_t sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c0 = cc * 32 + 2 * i;
+            const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
+            // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
+            const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
+            packed[i] = h2_from_f2(e);
+            sum2[i & 3] = fadd2(sum2[i & 3], e);
+          }
+          tmem_st16(tS + cc * 16, packed);
+        }
+        {
+          float s0, s1, s2, s3, s4, s5, s6, s7;
+          f2unpack(sum2[0], s0, s1);
+          f2unpack(sum2[1], s2, s3);
+          f2unpack(sum2[2], s4, s5);
+          f2unpack(sum2[3], s6, s7);
+          l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)));
+        }
+        m = m_new;
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          // O *= alpha
 #pragma unroll 1
-        for (int cc = 0; cc < C::OW / 16; ++cc) {
-          float o[16];
-          tmem_ld16(tO + cc * 16, o);
+          for (int cc = 0; cc < C::OW / 16; ++cc) {
+            float o[16];
+            tmem_ld16(tO + cc * 16, o);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] *= alpha;
-          uint32_t u[16];
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            uint32_t u[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i]);
-          tmem_st16(tO + cc * 16, u);
+            for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i]);
+            tmem_st16(tO + cc * 16, u);
+          }
         }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_ready + t);
+        ++cnt;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(sm.p_ready + t);
-    }
-    // ---- epilogue: O / l -> fp16, lse2 = m + log2(l) ----
-    if (ok && nt > 0) ok = mbar_wait_warp(sm.o_full + t, 0, ctl, 22 + t);
-    if (ok) {
+      if (!ok) break;
+      // ---- epilogue: O / l -> fp16, lse2 = m + log2(l) ----
+      if (nt > 0) {
+        if (!mbar_wait_warp(o_full + t, uint32_t(oc) & 1, ctl, 22 + t)) { ok = false; break; }
+        tc_fence_after();
+      }
       const bool row_ok = r < shp.Nq;
-      if (nt > 0) tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      __half* orow = o_ptr + (long long)b * o_sb + (long long)h * o_sh + (long long)r * o_sn;
+      __half* orow = o_ptr + (long long)w.b * o_sb + (long long)w.h * o_sh + (long long)r * o_sn;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
         if (nt > 0) {
           tmem_ld32(tO + cc * 32, o);
+          if (cc == D / 32 - 1) {
+            // O_t is read: the next unit's first PV may overwrite it
+            tc_fence_before();
+            mbar_arrive(o_empty + t);
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0.f;
@@ -380,7 +454,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           }
         }
       }
-      if (row_ok) lse_ptr[(long long)bh * shp.Nq + r] = l > 0.f ? m + lg2(l) : -INFINITY;
+      if (nt > 0) ++oc;
+      if (row_ok) {
+        lse_ptr[((long long)w.b * shp.Hq + w.h) * shp.Nq + r] = l > 0.f ? m + lg2(l) : -INFINITY;
+      }
     }
   }
 
@@ -397,12 +474,23 @@ int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
   auto kern = fa_fwd_kernel<D>;
+  // The register split inside the kernel assumes the launch count; a build
+  // that allocated a different number must not run (an increase that does
+  // not fit would wait forever).
+  static int regs_ok = -1;
+  if (regs_ok < 0) {
+    cudaFuncAttributes fa_attr;
+    regs_ok = cudaFuncGetAttributes(&fa_attr, kern) == cudaSuccess && fa_attr.numRegs == int(fwd::LAUNCH_REGS) ? 1 : 0;
+  }
+  if (!regs_ok) return FA_ERR_LAUNCH;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return FA_ERR_LAUNCH;
   const int n_qblk = (a.shape.Nq + fwd::QT * fwd::BM - 1) / (fwd::QT * fwd::BM);
-  dim3 grid(unsigned(n_qblk * a.shape.B * a.shape.Hq));
-  kern<<<grid, fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, a.o, a.o_sb, a.o_sh,
-                                                   a.o_sn, a.lse);
+  const int n_units = n_qblk * a.shape.B * a.shape.Hq;
+  const int sms = device_sm_count();
+  const int n_cta = n_units < sms ? n_units : sms;
+  kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, a.o,
+                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

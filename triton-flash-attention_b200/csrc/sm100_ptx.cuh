@@ -303,6 +303,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) 
       : "memory");
 }
 
+// Per-warpgroup register reallocation (setmaxnreg): every warp of a
+// warpgroup must execute the same instruction.  The counts of all
+// warpgroups must fit in what the CTA was launched with (threads x
+// registers per thread), or an increase waits forever.
+template <uint32_t N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_claim() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // 8 consecutive 32-bit columns -> 8 registers, with the wait.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&r)[8]) {
   uint32_t* u = reinterpret_cast<uint32_t*>(r);
