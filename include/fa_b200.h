@@ -23,6 +23,12 @@
  * context parallelism, where one call sees one K/V chunk.  A query row with
  * no visible key gets o = 0 and lse = -inf.
  *
+ * Every entry point has a _bf16 twin with the same signature that takes
+ * bf16 instead of fp16 for q, k, v, o, dO and the non-fp32 gradients (the
+ * reference's kernel path is fp16 only and sends bf16 inputs to PyTorch's
+ * SDPA, attention.py:653-656; here both run on the B200 kernels, with P and
+ * dS rounded to the operand type).
+ *
  * accumulate_fp32 (backward only): 0 writes the gradient as fp16; nonzero
  * treats the gradient pointers as fp32 buffers with the same element strides
  * and adds this call's contribution to them (ring context parallelism sums a
@@ -107,6 +113,37 @@ FA_API int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part,
                      const float* lse_part, int B, int H, int N, int D,
                      void* stream);
 
+/* bf16 twins of the five entry points above (same arguments). */
+FA_API int fa_fwd_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, const int64_t* o_strides,
+                float softmax_scale, int causal, int q_offset, int k_offset,
+                void* stream);
+FA_API int fa_bwd_delta_bf16(const void* o, const void* dO, float* delta,
+                      int B, int H, int N, int D,
+                      const int64_t* o_strides, const int64_t* do_strides,
+                      void* stream);
+FA_API int fa_bwd_dq_bf16(const void* q, const void* k, const void* v, const void* dO,
+                   const float* lse, const float* delta, void* dq,
+                   int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                   const int64_t* q_strides, const int64_t* k_strides,
+                   const int64_t* v_strides, const int64_t* do_strides,
+                   const int64_t* dq_strides,
+                   float softmax_scale, int causal, int q_offset, int k_offset,
+                   int accumulate_fp32, void* stream);
+FA_API int fa_bwd_dkdv_bf16(const void* q, const void* k, const void* v, const void* dO,
+                     const float* lse, const float* delta, void* dk, void* dv,
+                     int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                     const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* do_strides,
+                     const int64_t* dk_strides, const int64_t* dv_strides,
+                     float softmax_scale, int causal, int q_offset, int k_offset,
+                     int accumulate_fp32, void* stream);
+FA_API int fa_merge_partial_bf16(float* o_acc, float* lse_acc, const void* o_part,
+                          const float* lse_part, int B, int H, int N, int D,
+                          void* stream);
+
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
  * low byte and the barrier site in bits 8..15.  Synchronises the device. */
@@ -115,7 +152,7 @@ FA_API int fa_device_status(int reset);
 /* Human-readable text of an FA_ERR_* code. */
 FA_API const char* fa_status_string(int code);
 
-/* Library version: major * 10000 + minor * 100 + patch. */
+/* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

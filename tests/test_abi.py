@@ -21,8 +21,8 @@ def _declared():
 
 def test_header_declares_entry_points():
     names = _declared()
-    assert {"fa_fwd", "fa_bwd_delta", "fa_bwd_dq", "fa_bwd_dkdv", "fa_merge_partial",
-            "fa_device_status", "fa_status_string", "fa_version"} <= set(names)
+    core = {"fa_fwd", "fa_bwd_delta", "fa_bwd_dq", "fa_bwd_dkdv", "fa_merge_partial"}
+    assert core | {n + "_bf16" for n in core} | {"fa_device_status", "fa_status_string", "fa_version"} <= set(names)
 
 
 def test_library_exports_every_declared_symbol():
@@ -44,10 +44,11 @@ def _strides():
     return (ctypes.c_int64 * 3)(4096, 1024, 64)
 
 
+@pytest.mark.parametrize("name", ["fa_fwd", "fa_fwd_bf16"])
 @pytest.mark.parametrize("d,expect", [(48, _abi.FA_ERR_UNSUPPORTED_HEAD_DIM), (256, _abi.FA_ERR_UNSUPPORTED_HEAD_DIM)])
-def test_rejects_head_dim_before_any_cuda_call(d, expect):
+def test_rejects_head_dim_before_any_cuda_call(name, d, expect):
     s = _strides()
-    rc = _abi.lib().fa_fwd(16, 16, 16, 16, 16, 1, 1, 1, 8, 8, d, s, s, s, s, 0.1, 1, 0, 0, None)
+    rc = getattr(_abi.lib(), name)(16, 16, 16, 16, 16, 1, 1, 1, 8, 8, d, s, s, s, s, 0.1, 1, 0, 0, None)
     assert rc == expect
 
 

@@ -39,10 +39,14 @@ SIGNATURES = {
     "fa_bwd_dkdv": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
                          _s, _s, _s, _s, _s, _s, _f, _i, _i, _i, _i, _p]),
     "fa_merge_partial": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
+}
+# the bf16 twins take the same arguments
+SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in list(SIGNATURES)})
+SIGNATURES.update({
     "fa_device_status": (_i, [_i]),
     "fa_status_string": (ctypes.c_char_p, [_i]),
     "fa_version": (_i, []),
-}
+})
 
 
 def library_path() -> str:
@@ -67,6 +71,14 @@ def lib() -> ctypes.CDLL:
                 fn.argtypes = args
             _lib = handle
     return _lib
+
+
+def entry(name: str, dtype) -> ctypes._CFuncPtr:
+    """The entry point ``name`` for operands of ``dtype`` (torch.float16 or
+    torch.bfloat16): the fp16 symbol or its ``_bf16`` twin."""
+    import torch
+
+    return getattr(lib(), name + "_bf16" if dtype == torch.bfloat16 else name)
 
 
 def status_string(code: int) -> str:

@@ -21,6 +21,9 @@ import torch
 from . import _abi
 
 SUPPORTED_HEAD_DIMS = (32, 64, 128)
+# float16 is the reference's kernel dtype (attention.py:653-656); bfloat16 is
+# served by the same kernels here, where the reference falls back to SDPA.
+SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
 Backend = Literal["auto", "triton", "cuda"]
 _BACKENDS = ("auto", "triton", "cuda")
 
@@ -81,9 +84,9 @@ def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> Dispatch
         return DispatchDecision("unsupported", "the B200 kernel requires a CUDA tensor")
     if torch.version.hip is not None:
         return DispatchDecision("unsupported", "this project targets NVIDIA CUDA, not ROCm")
-    if query.dtype != torch.float16:
+    if query.dtype not in SUPPORTED_DTYPES:
         return DispatchDecision(
-            "unsupported", "the custom mixed-precision path currently supports float16")
+            "unsupported", "the custom mixed-precision path currently supports float16 and bfloat16")
     if query.shape[-1] not in SUPPORTED_HEAD_DIMS:
         supported = ", ".join(str(dim) for dim in SUPPORTED_HEAD_DIMS)
         return DispatchDecision(
@@ -93,7 +96,7 @@ def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> Dispatch
         return DispatchDecision(
             "unsupported", "the kernels are built for sm_100a (B200) GPUs only")
     return DispatchDecision(
-        "cuda", "CUDA float16 attention on sm_100a with a supported head dimension")
+        "cuda", f"CUDA {str(query.dtype).replace('torch.', '')} attention on sm_100a with a supported head dimension")
 
 
 def _stream_handle(device: torch.device) -> int:
@@ -107,8 +110,7 @@ def attention_forward(q, k, v, causal: bool, softmax_scale: float, *, q_offset: 
     hkv, nk = k.shape[1], k.shape[2]
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)  # contiguous even for strided q
     lse = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
-    lib = _abi.lib()
-    rc = lib.fa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+    rc = _abi.entry("fa_fwd", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                     b, hq, hkv, nq, nk, d,
                     _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(o),
                     float(softmax_scale), 1 if causal else 0, int(q_offset), int(k_offset),
@@ -121,7 +123,7 @@ def attention_delta(o, do):
     """Delta = rowsum(O * dO) in fp32 (attention.py:237-255)."""
     b, h, n, d = o.shape
     delta = torch.empty((b, h, n), device=o.device, dtype=torch.float32)
-    rc = _abi.lib().fa_bwd_delta(o.data_ptr(), do.data_ptr(), delta.data_ptr(), b, h, n, d,
+    rc = _abi.entry("fa_bwd_delta", o.dtype)(o.data_ptr(), do.data_ptr(), delta.data_ptr(), b, h, n, d,
                                  _abi.strides3(o), _abi.strides3(do), _stream_handle(o.device))
     _abi.check(rc, "fa_bwd_delta")
     return delta
@@ -139,7 +141,7 @@ def attention_backward_dq(q, k, v, do, lse, delta, causal: bool, softmax_scale: 
             raise ValueError("dq accumulator must be an fp32 tensor shaped like q")
     else:
         dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-    rc = _abi.lib().fa_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+    rc = _abi.entry("fa_bwd_dq", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
                               lse.data_ptr(), delta.data_ptr(), dq.data_ptr(),
                               b, hq, hkv, nq, nk, d,
                               _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(do),
@@ -165,7 +167,7 @@ def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale
     else:
         dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
         dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
-    rc = _abi.lib().fa_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+    rc = _abi.entry("fa_bwd_dkdv", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
                                 lse.data_ptr(), delta.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                 b, hq, hkv, nq, nk, d,
                                 _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(do),

@@ -7,6 +7,7 @@
 //    SM streaming.
 //  * fa_merge_kernel: the log-sum-exp merge of ring context parallelism
 //    (no counterpart in the reference).
+// Both take fp16 or bf16 operands (template parameter DT).
 #include "fa_kernels.h"
 
 namespace fa {
@@ -19,26 +20,29 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return r;
 }
 
-__device__ __forceinline__ float dot8_h(uint4 a, uint4 b) {
-  const __half2* ha = reinterpret_cast<const __half2*>(&a);
-  const __half2* hb = reinterpret_cast<const __half2*>(&b);
+// Dot product of 8 + 8 packed elements (fp16 or bf16) in fp32.
+template <int DT>
+__device__ __forceinline__ float dot8(uint4 a, uint4 b) {
+  const uint32_t* ua = reinterpret_cast<const uint32_t*>(&a);
+  const uint32_t* ub = reinterpret_cast<const uint32_t*>(&b);
   float acc = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float2 fa = __half22float2(ha[i]);
-    const float2 fb = __half22float2(hb[i]);
+    const float2 fa = unpack2<DT>(ua[i]);
+    const float2 fb = unpack2<DT>(ub[i]);
     acc = fmaf(fa.x, fb.x, acc);
     acc = fmaf(fa.y, fb.y, acc);
   }
   return acc;
 }
 
-template <int D>
-__global__ void __launch_bounds__(256) fa_delta_kernel(const __half* __restrict__ o, long long o_sb, long long o_sh,
-                                                       long long o_sn, const __half* __restrict__ dO, long long do_sb,
+template <int D, int DT>
+__global__ void __launch_bounds__(256) fa_delta_kernel(const uint16_t* __restrict__ o, long long o_sb,
+                                                       long long o_sh, long long o_sn,
+                                                       const uint16_t* __restrict__ dO, long long do_sb,
                                                        long long do_sh, long long do_sn, float* __restrict__ delta,
                                                        int H, int N, long long rows) {
-  constexpr int TPR = D / 8;  // lanes per row, 8 fp16 each
+  constexpr int TPR = D / 8;  // lanes per row, 8 elements each
   const long long total = rows * TPR;
   const long long nthreads = (long long)gridDim.x * blockDim.x;
   for (long long base = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total;
@@ -55,9 +59,9 @@ __global__ void __launch_bounds__(256) fa_delta_kernel(const __half* __restrict_
       const long long bh = row / N;
       const int h = int(bh % H);
       const long long b = bh / H;
-      const __half* po = o + b * o_sb + h * o_sh + n * o_sn + part * 8;
-      const __half* pd = dO + b * do_sb + h * do_sh + n * do_sn + part * 8;
-      acc = dot8_h(ld_nc_v4(po), ld_nc_v4(pd));
+      const uint16_t* po = o + b * o_sb + h * o_sh + n * o_sn + part * 8;
+      const uint16_t* pd = dO + b * do_sb + h * do_sh + n * do_sn + part * 8;
+      acc = dot8<DT>(ld_nc_v4(po), ld_nc_v4(pd));
     }
 #pragma unroll
     for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
@@ -65,12 +69,11 @@ __global__ void __launch_bounds__(256) fa_delta_kernel(const __half* __restrict_
   }
 }
 
-int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long o_sn, const __half* dO,
-                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
-                     cudaStream_t stream) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+template <int DT>
+int launch_bwd_delta_t(const uint16_t* o, long long o_sb, long long o_sh, long long o_sn, const uint16_t* dO,
+                       long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
+                       cudaStream_t stream) {
+  const int sms = device_sm_count();
   const long long rows = (long long)B * H * N;
   const long long work = rows * (D / 8);
   long long blocks = (work + 255) / 256;
@@ -79,16 +82,16 @@ int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long 
   if (blocks < 1) blocks = 1;
   switch (D) {
     case 32:
-      fa_delta_kernel<32><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                 delta, H, N, rows);
+      fa_delta_kernel<32, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                     delta, H, N, rows);
       break;
     case 64:
-      fa_delta_kernel<64><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                 delta, H, N, rows);
+      fa_delta_kernel<64, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                     delta, H, N, rows);
       break;
     case 128:
-      fa_delta_kernel<128><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                  delta, H, N, rows);
+      fa_delta_kernel<128, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
+                                                                      delta, H, N, rows);
       break;
     default:
       return FA_ERR_UNSUPPORTED_HEAD_DIM;
@@ -96,9 +99,20 @@ int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long 
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-// o_acc (rows x D fp32), lse_acc (rows) <- merge with o_part (fp16), lse_part.
+int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_sn, const void* dO,
+                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
+                     int dtype, cudaStream_t stream) {
+  const uint16_t* o16 = static_cast<const uint16_t*>(o);
+  const uint16_t* d16 = static_cast<const uint16_t*>(dO);
+  return dtype == DT_BF16
+             ? launch_bwd_delta_t<DT_BF16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta, B, H, N, D, stream)
+             : launch_bwd_delta_t<DT_F16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta, B, H, N, D, stream);
+}
+
+// o_acc (rows x D fp32), lse_acc (rows) <- merge with o_part (fp16 or bf16), lse_part.
+template <int DT>
 __global__ void __launch_bounds__(256) fa_merge_kernel(float* __restrict__ o_acc, float* __restrict__ lse_acc,
-                                                       const __half* __restrict__ o_part,
+                                                       const uint16_t* __restrict__ o_part,
                                                        const float* __restrict__ lse_part, long long rows, int D) {
   const int vec_per_row = D / 8;
   const long long total = rows * vec_per_row;
@@ -119,11 +133,10 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(float* __restrict__ o_acc
     }
     float* po = o_acc + row * D + part * 8;
     const uint4 pk = *reinterpret_cast<const uint4*>(o_part + row * D + part * 8);
-    const __half2* h2 = reinterpret_cast<const __half2*>(&pk);
     float4 x0 = reinterpret_cast<float4*>(po)[0];
     float4 x1 = reinterpret_cast<float4*>(po)[1];
-    const float2 p0 = __half22float2(h2[0]), p1 = __half22float2(h2[1]);
-    const float2 p2 = __half22float2(h2[2]), p3 = __half22float2(h2[3]);
+    const float2 p0 = unpack2<DT>(pk.x), p1 = unpack2<DT>(pk.y);
+    const float2 p2 = unpack2<DT>(pk.z), p3 = unpack2<DT>(pk.w);
     x0.x = x0.x * wa + p0.x * wb;
     x0.y = x0.y * wa + p0.y * wb;
     x0.z = x0.z * wa + p1.x * wb;
@@ -142,16 +155,18 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(float* __restrict__ o_acc
   }
 }
 
-int launch_merge_partial(float* o_acc, float* lse_acc, const __half* o_part, const float* lse_part, long long rows,
-                         int D, cudaStream_t stream) {
+int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
+                         int D, int dtype, cudaStream_t stream) {
   if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
   long long blocks = (rows * (D / 8) + 255) / 256;
   if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
   if (blocks < 1) blocks = 1;
-  fa_merge_kernel<<<unsigned(blocks), 256, 0, stream>>>(o_acc, lse_acc, o_part, lse_part, rows, D);
+  const uint16_t* p16 = static_cast<const uint16_t*>(o_part);
+  if (dtype == DT_BF16)
+    fa_merge_kernel<DT_BF16><<<unsigned(blocks), 256, 0, stream>>>(o_acc, lse_acc, p16, lse_part, rows, D);
+  else
+    fa_merge_kernel<DT_F16><<<unsigned(blocks), 256, 0, stream>>>(o_acc, lse_acc, p16, lse_part, rows, D);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

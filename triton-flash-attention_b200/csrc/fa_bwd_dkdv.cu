@@ -59,7 +59,7 @@ struct Cfg {
 
 }  // namespace bkv
 
-template <int D>
+template <int D, int DT>
 __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
     if (lane == 0 && n_items > 0) {
-      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0);
-      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1);
+      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0, DT);
+      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1, DT);
       const uint32_t k_s = sbase + C::OFF_K;
       const uint32_t v_s = sbase + C::OFF_V;
       const SDesc kd = desc_k_base<D>(k_s);
@@ -321,14 +321,14 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         const float4 nl = l4[c4];
         const float4 nd = d4[c4];
         const int c = c4 * 4;
-        const uint32_t p01 = h2_from_f2(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
-        const uint32_t p23 = h2_from_f2(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
-        const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-        const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+        const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
+        const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
+        const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+        const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
         pk_p[c4 * 2] = p01;
         pk_p[c4 * 2 + 1] = p23;
-        pk_ds[c4 * 2] = hmul2(p01, d01);
-        pk_ds[c4 * 2 + 1] = hmul2(p23, d23);
+        pk_ds[c4 * 2] = mul2<DT>(p01, d01);
+        pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
       }
       tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
       tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
@@ -371,14 +371,14 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
             dst[v4] = x;
           }
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out) + off0 + cc * 32);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + off0 + cc * 32);
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            pk.x = pack2<DT>(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
+            pk.y = pack2<DT>(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
+            pk.z = pack2<DT>(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
+            pk.w = pack2<DT>(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
@@ -484,7 +484,7 @@ __device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
 }
 }  // namespace bkvw
 
-template <int D>
+template <int D, int DT>
 __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     fa_bwd_dkdv_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                             const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -673,8 +673,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
     if (lane == 0) {
-      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0);
-      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1);
+      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0, DT);
+      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1, DT);
       auto q_tile = [&](int g) { return sbase + C::OFF_Q + (g % C::NST) * C::Q_TILE_BYTES; };
       auto do_tile = [&](int g) { return sbase + C::OFF_DO + (g % C::NST) * C::Q_TILE_BYTES; };
       SDesc kd = desc_k_base<D>(sbase + C::OFF_K);
@@ -812,8 +812,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
               const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
               const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
               const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
-              pk_p[c4 * 2] = h2_from_f2(e01);
-              pk_p[c4 * 2 + 1] = h2_from_f2(e23);
+              pk_p[c4 * 2] = pack2_f2<DT>(e01);
+              pk_p[c4 * 2 + 1] = pack2_f2<DT>(e23);
             }
             tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
             tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
@@ -839,10 +839,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             for (int c4 = 0; c4 < 16; ++c4) {
               const float4 nd = d4[c4];
               const int c = c4 * 4;
-              const uint32_t d01 = h2_from_f2(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-              const uint32_t d23 = h2_from_f2(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-              pk_ds[c4 * 2] = hmul2(__float_as_uint(pf[c4 * 2]), d01);
-              pk_ds[c4 * 2 + 1] = hmul2(__float_as_uint(pf[c4 * 2 + 1]), d23);
+              const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+              const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+              pk_ds[c4 * 2] = mul2<DT>(__float_as_uint(pf[c4 * 2]), d01);
+              pk_ds[c4 * 2 + 1] = mul2<DT>(__float_as_uint(pf[c4 * 2 + 1]), d23);
             }
             tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
             tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
@@ -887,14 +887,14 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             dst[v4] = x;
           }
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out) + off0 + cc * 32);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + off0 + cc * 32);
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
+            pk.x = pack2<DT>(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
+            pk.y = pack2<DT>(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
+            pk.z = pack2<DT>(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
+            pk.w = pack2<DT>(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
@@ -916,10 +916,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   }
 }
 
-template <int D>
+template <int D, int DT>
 int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   using C = bkvw::Cfg<D>;
-  auto kern = fa_bwd_dkdv_wide_kernel<D>;
+  auto kern = fa_bwd_dkdv_wide_kernel<D, DT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkvw::BM - 1) / bkvw::BM;
@@ -932,10 +932,10 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D>
+template <int D, int DT>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
-  auto kern = fa_bwd_dkdv_kernel<D>;
+  auto kern = fa_bwd_dkdv_kernel<D, DT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkv::BM - 1) / bkv::BM;
@@ -948,9 +948,9 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
 
 int launch_bwd_dkdv(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return launch_bwd_dkdv_wide_t<32>(a);
-    case 64: return launch_bwd_dkdv_wide_t<64>(a);
-    case 128: return launch_bwd_dkdv_t<128>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_bwd_dkdv_wide_t<32, DT_BF16>(a) : launch_bwd_dkdv_wide_t<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_bwd_dkdv_wide_t<64, DT_BF16>(a) : launch_bwd_dkdv_wide_t<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_bwd_dkdv_t<128, DT_BF16>(a) : launch_bwd_dkdv_t<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

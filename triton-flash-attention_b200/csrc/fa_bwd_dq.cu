@@ -53,7 +53,7 @@ struct Cfg {
 
 }  // namespace bdq
 
-template <int D>
+template <int D, int DT>
 __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                      const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -167,8 +167,8 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
     if (lane == 0 && n_max > 0) {
-      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
-      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1);
+      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0, DT);
+      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1, DT);
       const uint32_t q_s = sbase + C::OFF_Q;
       const uint32_t do_s = sbase + C::OFF_DO;
       const uint32_t k_s = sbase + C::OFF_K;
@@ -276,9 +276,9 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
         for (int i = 0; i < 16; ++i) {
           const int c0 = cc * 32 + 2 * i;
           // P = 2^(s*scale*log2e - lse2) in fp16x2, dS = P * (dP - Delta)
-          const uint32_t p = h2_from_f2(exp2_mufu2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
-          const uint32_t d = h2_from_f2(fadd2(f2pack(dp[c0], dp[c0 + 1]), ndelta2));
-          packed[i] = hmul2(p, d);
+          const uint32_t p = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
+          const uint32_t d = pack2_f2<DT>(fadd2(f2pack(dp[c0], dp[c0 + 1]), ndelta2));
+          packed[i] = mul2<DT>(p, d);
         }
         tmem_st16(tS + cc * 16, packed);
       }
@@ -315,14 +315,14 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
             dst[v4] = x;
           }
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(dq_out) + off);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dq_out) + off);
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            pk.x = pack2<DT>(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
+            pk.y = pack2<DT>(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
+            pk.z = pack2<DT>(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
+            pk.w = pack2<DT>(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
@@ -406,7 +406,7 @@ __device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
 }
 }  // namespace bdqw
 
-template <int D>
+template <int D, int DT>
 __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     fa_bwd_dq_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -516,8 +516,8 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   } else if (warp == 1) {
     // =================== tcgen05 MMA issuer ===================
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
-      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1);
+      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0, DT);
+      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1, DT);
       auto k_tile = [&](int j) { return sbase + C::OFF_K + (j % C::NST) * C::KV_TILE_BYTES; };
       auto v_tile = [&](int j) { return sbase + C::OFF_V + (j % C::NST) * C::KV_TILE_BYTES; };
       auto wait_kv = [&](int j, int site) {
@@ -649,7 +649,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const uint64_t x = ffma2(f2pack(sv[2 * i], sv[2 * i + 1]), c2x2, nlse2);
-          pk_p[i] = h2_from_f2((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
+          pk_p[i] = pack2_f2<DT>((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
         }
         if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 152 + w)) { ok = false; break; }
         tc_fence_after();
@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         uint32_t pk_ds[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          pk_ds[i] = hmul2(pk_p[i], h2_from_f2(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+          pk_ds[i] = mul2<DT>(pk_p[i], pack2_f2<DT>(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
         tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
         tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
         tmem_st_wait();
@@ -700,14 +700,14 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
             dst[v4] = x;
           }
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(dq_out) + off);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dq_out) + off);
 #pragma unroll
           for (int v8 = 0; v8 < HALF / 8; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
-            pk.y = pack_half2(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
-            pk.z = pack_half2(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
-            pk.w = pack_half2(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
+            pk.x = pack2<DT>(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
+            pk.y = pack2<DT>(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
+            pk.z = pack2<DT>(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
+            pk.w = pack2<DT>(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
@@ -727,10 +727,10 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   }
 }
 
-template <int D>
+template <int D, int DT>
 int launch_bwd_dq_wide_t(const BwdArgs& a) {
   using C = bdqw::Cfg<D>;
-  auto kern = fa_bwd_dq_wide_kernel<D>;
+  auto kern = fa_bwd_dq_wide_kernel<D, DT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
@@ -743,10 +743,10 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D>
+template <int D, int DT>
 int launch_bwd_dq_t(const BwdArgs& a) {
   using C = bdq::Cfg<D>;
-  auto kern = fa_bwd_dq_kernel<D>;
+  auto kern = fa_bwd_dq_kernel<D, DT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qblk = (a.shape.Nq + bdq::QT * bdq::BM - 1) / (bdq::QT * bdq::BM);
@@ -759,9 +759,9 @@ int launch_bwd_dq_t(const BwdArgs& a) {
 
 int launch_bwd_dq(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return launch_bwd_dq_wide_t<32>(a);
-    case 64: return launch_bwd_dq_wide_t<64>(a);
-    case 128: return launch_bwd_dq_t<128>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<32, DT_BF16>(a) : launch_bwd_dq_wide_t<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<64, DT_BF16>(a) : launch_bwd_dq_wide_t<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_bwd_dq_t<128, DT_BF16>(a) : launch_bwd_dq_t<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

@@ -50,10 +50,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 bool supported_d(int D) { return D == 32 || D == 64 || D == 128; }
 
-// 4-D fp16 tensor map over (B, H, N, D) with element strides {sb, sh, sn, 1}.
-// The box is {min(D, 64), rows, 1, 1} with the swizzle the kernels' shared
-// memory descriptors assume (128 B for D >= 64, 64 B for D = 32).
-int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, const int64_t* strides, int rows) {
+// 4-D tensor map (fp16 or bf16 elements) over (B, H, N, D) with element
+// strides {sb, sh, sn, 1}.  The box is {min(D, 64), rows, 1, 1} with the
+// swizzle the kernels' shared memory descriptors assume (128 B for D >= 64,
+// 64 B for D = 32).
+int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, const int64_t* strides, int rows,
+             int dtype) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DRIVER;
   if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
@@ -64,7 +66,8 @@ int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, cons
   cuuint64_t gstr[3] = {cuuint64_t(strides[2]) * 2, cuuint64_t(strides[1]) * 2, cuuint64_t(strides[0]) * 2};
   cuuint32_t box[4] = {cuuint32_t(box_d), cuuint32_t(rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
+  const CUtensorMapDataType ty = dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, ty, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
                    D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -101,26 +104,22 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   return s;
 }
 
-}  // namespace
-}  // namespace fa
-
-using namespace fa;
-
-extern "C" int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
-                      int Nq, int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
-                      const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
-                      int q_offset, int k_offset, void* stream) {
+int fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
+             int Nk, int D, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+             const int64_t* o_strides, float softmax_scale, int causal, int q_offset, int k_offset, void* stream,
+             int dtype) {
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
   if (rc) return rc;
   if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides || !o_strides) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
   FwdArgs a;
-  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, 128))) return rc;
-  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, 128))) return rc;
-  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, 128))) return rc;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, 128, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, 128, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, 128, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
-  a.o = static_cast<__half*>(o);
+  a.dtype = dtype;
+  a.o = o;
   a.o_sb = o_strides[0];
   a.o_sh = o_strides[1];
   a.o_sn = o_strides[2];
@@ -129,22 +128,21 @@ extern "C" int fa_fwd(const void* q, const void* k, const void* v, void* o, floa
   return launch_fwd(a, D);
 }
 
-extern "C" int fa_bwd_delta(const void* o, const void* dO, float* delta, int B, int H, int N, int D,
-                            const int64_t* o_strides, const int64_t* do_strides, void* stream) {
+int delta_impl(const void* o, const void* dO, float* delta, int B, int H, int N, int D, const int64_t* o_strides,
+               const int64_t* do_strides, void* stream, int dtype) {
   if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
   if (!o || !dO || !delta || !o_strides || !do_strides) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2)) return FA_ERR_MISALIGNED;
-  return launch_bwd_delta(static_cast<const __half*>(o), o_strides[0], o_strides[1], o_strides[2],
-                          static_cast<const __half*>(dO), do_strides[0], do_strides[1], do_strides[2], delta, B, H,
-                          N, D, static_cast<cudaStream_t>(stream));
+  return launch_bwd_delta(o, o_strides[0], o_strides[1], o_strides[2], dO, do_strides[0], do_strides[1],
+                          do_strides[2], delta, B, H, N, D, dtype, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const float* lse,
-                         const float* delta, void* dq, int B, int Hq, int Hkv, int Nq, int Nk, int D,
-                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
-                         const int64_t* do_strides, const int64_t* dq_strides, float softmax_scale, int causal,
-                         int q_offset, int k_offset, int accumulate_fp32, void* stream) {
+int dq_impl(const void* q, const void* k, const void* v, const void* dO, const float* lse, const float* delta,
+            void* dq, int B, int Hq, int Hkv, int Nq, int Nk, int D, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, const int64_t* do_strides,
+            const int64_t* dq_strides, float softmax_scale, int causal, int q_offset, int k_offset,
+            int accumulate_fp32, void* stream, int dtype) {
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
   if (rc) return rc;
   if (!q || !k || !v || !dO || !lse || !delta || !dq) return FA_ERR_BAD_SHAPE;
@@ -152,11 +150,12 @@ extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(dq, dq_strides, accumulate_fp32 ? 4 : 2)) return FA_ERR_MISALIGNED;
   BwdArgs a;
-  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dq_cfg::BM))) return rc;
-  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dq_cfg::BM))) return rc;
+  a.dtype = dtype;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dq_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dq_cfg::BM, dtype))) return rc;
   const int bn = D <= 64 ? dq_cfg::BN_WIDE : dq_cfg::BN;
-  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, bn))) return rc;
-  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, bn))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, bn, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, bn, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
   a.lse = lse;
   a.delta = delta;
@@ -171,12 +170,11 @@ extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void
   return launch_bwd_dq(a, D);
 }
 
-extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, const float* lse,
-                           const float* delta, void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk, int D,
-                           const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
-                           const int64_t* do_strides, const int64_t* dk_strides, const int64_t* dv_strides,
-                           float softmax_scale, int causal, int q_offset, int k_offset, int accumulate_fp32,
-                           void* stream) {
+int dkdv_impl(const void* q, const void* k, const void* v, const void* dO, const float* lse, const float* delta,
+              void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk, int D, const int64_t* q_strides,
+              const int64_t* k_strides, const int64_t* v_strides, const int64_t* do_strides,
+              const int64_t* dk_strides, const int64_t* dv_strides, float softmax_scale, int causal, int q_offset,
+              int k_offset, int accumulate_fp32, void* stream, int dtype) {
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
   if (rc) return rc;
   if (!q || !k || !v || !dO || !lse || !delta || !dk || !dv) return FA_ERR_BAD_SHAPE;
@@ -185,11 +183,12 @@ extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const vo
   const int eb = accumulate_fp32 ? 4 : 2;
   if (!out_strides_ok(dk, dk_strides, eb) || !out_strides_ok(dv, dv_strides, eb)) return FA_ERR_MISALIGNED;
   BwdArgs a;
+  a.dtype = dtype;
   const int bq = D <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
-  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, bq))) return rc;
-  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq))) return rc;
-  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM))) return rc;
-  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM))) return rc;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
   a.lse = lse;
   a.delta = delta;
@@ -208,14 +207,91 @@ extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const vo
   return launch_bwd_dkdv(a, D);
 }
 
-extern "C" int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B,
-                                int H, int N, int D, void* stream) {
+int merge_impl(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B, int H, int N, int D,
+               void* stream, int dtype) {
   if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
   if (!o_acc || !lse_acc || !o_part || !lse_part) return FA_ERR_BAD_SHAPE;
   if (!aligned16(o_acc) || !aligned16(o_part)) return FA_ERR_MISALIGNED;
-  return launch_merge_partial(o_acc, lse_acc, static_cast<const __half*>(o_part), lse_part,
-                              (long long)B * H * N, D, static_cast<cudaStream_t>(stream));
+  return launch_merge_partial(o_acc, lse_acc, o_part, lse_part, (long long)B * H * N, D, dtype,
+                              static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace fa
+
+using namespace fa;
+
+// fp16 entry points (the reference's only dtype) and their bf16 twins.
+extern "C" int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                      int Nq, int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
+                      int q_offset, int k_offset, void* stream) {
+  return fwd_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides, o_strides, softmax_scale,
+                  causal, q_offset, k_offset, stream, DT_F16);
+}
+extern "C" int fa_fwd_bf16(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                           int Nq, int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
+                           const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
+                           int q_offset, int k_offset, void* stream) {
+  return fwd_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides, o_strides, softmax_scale,
+                  causal, q_offset, k_offset, stream, DT_BF16);
+}
+
+extern "C" int fa_bwd_delta(const void* o, const void* dO, float* delta, int B, int H, int N, int D,
+                            const int64_t* o_strides, const int64_t* do_strides, void* stream) {
+  return delta_impl(o, dO, delta, B, H, N, D, o_strides, do_strides, stream, DT_F16);
+}
+extern "C" int fa_bwd_delta_bf16(const void* o, const void* dO, float* delta, int B, int H, int N, int D,
+                                 const int64_t* o_strides, const int64_t* do_strides, void* stream) {
+  return delta_impl(o, dO, delta, B, H, N, D, o_strides, do_strides, stream, DT_BF16);
+}
+
+extern "C" int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                         const float* delta, void* dq, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                         const int64_t* do_strides, const int64_t* dq_strides, float softmax_scale, int causal,
+                         int q_offset, int k_offset, int accumulate_fp32, void* stream) {
+  return dq_impl(q, k, v, dO, lse, delta, dq, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides, do_strides,
+                 dq_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32, stream, DT_F16);
+}
+extern "C" int fa_bwd_dq_bf16(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                              const float* delta, void* dq, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                              const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                              const int64_t* do_strides, const int64_t* dq_strides, float softmax_scale, int causal,
+                              int q_offset, int k_offset, int accumulate_fp32, void* stream) {
+  return dq_impl(q, k, v, dO, lse, delta, dq, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides, do_strides,
+                 dq_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32, stream, DT_BF16);
+}
+
+extern "C" int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                           const float* delta, void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                           const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                           const int64_t* do_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                           float softmax_scale, int causal, int q_offset, int k_offset, int accumulate_fp32,
+                           void* stream) {
+  return dkdv_impl(q, k, v, dO, lse, delta, dk, dv, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides,
+                   do_strides, dk_strides, dv_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32,
+                   stream, DT_F16);
+}
+extern "C" int fa_bwd_dkdv_bf16(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                                const float* delta, void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk,
+                                int D, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                const int64_t* do_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                                float softmax_scale, int causal, int q_offset, int k_offset, int accumulate_fp32,
+                                void* stream) {
+  return dkdv_impl(q, k, v, dO, lse, delta, dk, dv, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides,
+                   do_strides, dk_strides, dv_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32,
+                   stream, DT_BF16);
+}
+
+extern "C" int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B,
+                                int H, int N, int D, void* stream) {
+  return merge_impl(o_acc, lse_acc, o_part, lse_part, B, H, N, D, stream, DT_F16);
+}
+extern "C" int fa_merge_partial_bf16(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B,
+                                     int H, int N, int D, void* stream) {
+  return merge_impl(o_acc, lse_acc, o_part, lse_part, B, H, N, D, stream, DT_BF16);
 }
 
 extern "C" int fa_device_status(int reset) {
@@ -244,4 +320,4 @@ extern "C" const char* fa_status_string(int code) {
   }
 }
 
-extern "C" int fa_version(void) { return 100; }
+extern "C" int fa_version(void) { return 10100; }

@@ -111,10 +111,10 @@ __device__ __forceinline__ int unit_index(int c, int k, int G, int n) {
 
 }  // namespace fwd
 
-template <int D>
+template <int D, int DT>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                  const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, __half* __restrict__ o_ptr,
+                  const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
                   const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr,
                   const int n_units) {
   using namespace fwd;
@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     } else if (warp == 1) {
       // =================== tcgen05 MMA issuer ===================
       if (lane == 0) {
-        constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0);
-        constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, C::OW, 0, 1);
+        constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0, DT);
+        constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, C::OW, 0, 1, DT);
         const uint32_t k_s = sbase + C::OFF_K;
         const uint32_t v_s = sbase + C::OFF_V;
         int gj = 0, uc = 0;
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
             // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
             const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
-            packed[i] = h2_from_f2(e);
+            packed[i] = pack2_f2<DT>(e);
             sum2[i & 3] = fadd2(sum2[i & 3], e);
           }
           tmem_st16(tS + cc * 16, packed);
@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       const bool row_ok = r < shp.Nq;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      __half* orow = o_ptr + (long long)w.b * o_sb + (long long)w.h * o_sh + (long long)r * o_sn;
+      uint16_t* orow = o_ptr + (long long)w.b * o_sb + (long long)w.h * o_sh + (long long)r * o_sn;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
@@ -446,10 +446,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack_half2(o[v8 * 8 + 0] * inv_l, o[v8 * 8 + 1] * inv_l);
-            pk.y = pack_half2(o[v8 * 8 + 2] * inv_l, o[v8 * 8 + 3] * inv_l);
-            pk.z = pack_half2(o[v8 * 8 + 4] * inv_l, o[v8 * 8 + 5] * inv_l);
-            pk.w = pack_half2(o[v8 * 8 + 6] * inv_l, o[v8 * 8 + 7] * inv_l);
+            pk.x = pack2<DT>(o[v8 * 8 + 0] * inv_l, o[v8 * 8 + 1] * inv_l);
+            pk.y = pack2<DT>(o[v8 * 8 + 2] * inv_l, o[v8 * 8 + 3] * inv_l);
+            pk.z = pack2<DT>(o[v8 * 8 + 4] * inv_l, o[v8 * 8 + 5] * inv_l);
+            pk.w = pack2<DT>(o[v8 * 8 + 6] * inv_l, o[v8 * 8 + 7] * inv_l);
             *reinterpret_cast<uint4*>(orow + cc * 32 + v8 * 8) = pk;
           }
         }
@@ -469,11 +469,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D>
+template <int D, int DT>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D>;
+  auto kern = fa_fwd_kernel<D, DT>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -489,16 +489,16 @@ int launch_fwd_t(const FwdArgs& a) {
   const int n_units = n_qblk * a.shape.B * a.shape.Hq;
   const int sms = device_sm_count();
   const int n_cta = n_units < sms ? n_units : sms;
-  kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, a.o,
+  kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, static_cast<uint16_t*>(a.o),
                                                                     a.o_sb, a.o_sh, a.o_sn, a.lse, n_units);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 int launch_fwd(const FwdArgs& a, int D) {
   switch (D) {
-    case 32: return launch_fwd_t<32>(a);
-    case 64: return launch_fwd_t<64>(a);
-    case 128: return launch_fwd_t<128>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_fwd_t<32, DT_BF16>(a) : launch_fwd_t<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_fwd_t<64, DT_BF16>(a) : launch_fwd_t<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_fwd_t<128, DT_BF16>(a) : launch_fwd_t<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

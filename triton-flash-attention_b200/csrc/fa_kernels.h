@@ -11,21 +11,26 @@
 
 namespace fa {
 
+// Operand element types (dtype fields below).
+enum : int { DT_F16 = 0, DT_BF16 = 1 };
+
 struct FwdArgs {
-  CUtensorMap tmap_q, tmap_k, tmap_v;  // 4-D {D, N, H, B} fp16, box {<=64, 128, 1, 1}
+  CUtensorMap tmap_q, tmap_k, tmap_v;  // 4-D {D, N, H, B}, box {<=64, 128, 1, 1}
   AttnShape shape;
-  __half* o;
+  int dtype;  // DT_F16 or DT_BF16: q, k, v and o
+  void* o;
   long long o_sb, o_sh, o_sn;
   float* lse;
   cudaStream_t stream;
 };
 
 struct BwdArgs {
-  CUtensorMap tmap_q, tmap_k, tmap_v, tmap_do;  // 4-D fp16 maps
+  CUtensorMap tmap_q, tmap_k, tmap_v, tmap_do;  // 4-D maps of the operand type
   AttnShape shape;
+  int dtype;  // DT_F16 or DT_BF16: q, k, v, dO and the non-fp32 outputs
   const float* lse;
   const float* delta;
-  void* dq;  // fa_bwd_dq output (fp16, or fp32 when accumulate_fp32)
+  void* dq;  // fa_bwd_dq output (operand type, or fp32 when accumulate_fp32)
   long long dq_sb, dq_sh, dq_sn;
   void* dk;
   void* dv;
@@ -52,11 +57,11 @@ inline int device_sm_count() {
 int launch_fwd(const FwdArgs& a, int D);
 int launch_bwd_dq(const BwdArgs& a, int D);
 int launch_bwd_dkdv(const BwdArgs& a, int D);
-int launch_bwd_delta(const __half* o, long long o_sb, long long o_sh, long long o_sn, const __half* dO,
+int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_sn, const void* dO,
                      long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
-                     cudaStream_t stream);
-int launch_merge_partial(float* o_acc, float* lse_acc, const __half* o_part, const float* lse_part, long long rows,
-                         int D, cudaStream_t stream);
+                     int dtype, cudaStream_t stream);
+int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
+                         int D, int dtype, cudaStream_t stream);
 
 // Query-tile / key-tile sizes the host needs for TMA box shapes.
 namespace dq_cfg {

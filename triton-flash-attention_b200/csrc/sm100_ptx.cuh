@@ -191,12 +191,13 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// Instruction descriptor, kind::f16 with fp16 A/B and fp32 D.
-//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16), 10-12 B format,
-//   15 A major (0 = K, 1 = MN), 16 B major, 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn_major, int b_mn_major) {
-  return (1u << 4) | (uint32_t(a_mn_major) << 15) | (uint32_t(b_mn_major) << 16) | (uint32_t(N >> 3) << 17) |
-         (uint32_t(M >> 4) << 24);
+// Instruction descriptor, kind::f16 with fp16 (dt = 0) or bf16 (dt = 1) A/B
+// and fp32 D.
+//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16, 1 = bf16), 10-12 B
+//   format, 15 A major (0 = K, 1 = MN), 16 B major, 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn_major, int b_mn_major, int dt = 0) {
+  return (1u << 4) | (uint32_t(dt) << 7) | (uint32_t(dt) << 10) | (uint32_t(a_mn_major) << 15) |
+         (uint32_t(b_mn_major) << 16) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor (tcgen05 form):
@@ -392,6 +393,49 @@ __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
+// Operand element type DT of the attention kernels: 0 = fp16, 1 = bf16.  A
+// and B of every MMA share it (one kind::f16 MMA never mixes the two), and P
+// and dS are rounded to it before they feed the next MMA.
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t r;
+  if constexpr (DT == 0) {
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  } else {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  }
+  return r;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t pack2_f2(uint64_t v) {
+  float lo, hi;
+  f2unpack(v, lo, hi);
+  return pack2<DT>(lo, hi);
+}
+template <int DT>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (DT == 0) {
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  } else {
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  }
+  return d;
+}
+// Two packed elements -> (lo, hi) floats.
+template <int DT>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (DT == 0) {
+    float lo, hi;
+    asm("{.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(v));
+    return make_float2(lo, hi);
+  } else {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
+}
+
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));

@@ -112,8 +112,9 @@ def cuda_block_ops() -> BlockOps:
         b, h, n, d = o.shape
         if not (o_acc.is_contiguous() and o.is_contiguous() and lse_acc.is_contiguous() and lse.is_contiguous()):
             raise ValueError("merge operands must be contiguous")
-        rc = _abi.lib().fa_merge_partial(o_acc.data_ptr(), lse_acc.data_ptr(), o.data_ptr(), lse.data_ptr(),
-                                         b, h, n, d, torch.cuda.current_stream(o.device).cuda_stream)
+        rc = _abi.entry("fa_merge_partial", o.dtype)(o_acc.data_ptr(), lse_acc.data_ptr(), o.data_ptr(),
+                                                     lse.data_ptr(), b, h, n, d,
+                                                     torch.cuda.current_stream(o.device).cuda_stream)
         _abi.check(rc, "fa_merge_partial")
 
     def bwd_dq(q, k, v, do, lse, delta, causal, scale, dq_acc, q_off, k_off):
