@@ -224,13 +224,23 @@ def run_ours(args) -> None:
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         barrier(world)
+        step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
         start.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            step_ev[i][0].record(stream)
             step(True)
+            step_ev[i][1].record(stream)
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
+    # per-step distribution, as the reference's benchmark reports it
+    # (benchmarks/benchmark_attention.py:153-158): median, p20, p80
+    per_step = sorted(a.elapsed_time(b) for a, b in step_ev)
+
+    def pct(p):
+        return per_step[min(len(per_step) - 1, int(round(p * (len(per_step) - 1))))]
     ms = barrier_max(world, ms_local)
     kv_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_kv)
     value = world * fl / (ms * 1e-3) / 1e12
@@ -316,6 +326,7 @@ def run_ours(args) -> None:
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(ms, 4),
+            "step_ms_quantiles": {"p20": round(pct(0.2), 4), "p50": round(pct(0.5), 4), "p80": round(pct(0.8), 4)},
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
