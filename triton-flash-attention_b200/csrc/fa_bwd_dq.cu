@@ -4,346 +4,28 @@
 // (triton_flash_attention/attention.py:507-573, inner loop :311-350):
 //   P = exp2(scale*log2(e) * Q K^T - lse2),  dP = dO V^T,
 //   dS = P (dP - Delta),  dQ = scale * dS K.
-// Layout of the work:
-//  * one CTA owns 2 query tiles of 128 rows of one (batch, head) and sweeps
-//    the key tiles (64 keys each) that are visible to them;
-//  * warp 0 streams K/V tiles through shared-memory stages with TMA;
-//  * warp 1 (one thread) issues tcgen05.mma: S_t = Q_t K^T and dP_t = dO_t V^T
-//    into TMEM, then dQ_t += dS_t K with dS_t read from TMEM (fp16, aliasing
-//    S_t) and K read as an MN-major operand of the same shared tile;
-//  * warps 4-7 / 8-11 turn S_t, dP_t into dS_t, one thread per query row,
-//    with that row's lse2 and Delta held in registers;
-//  * the two query tiles ping-pong between the tensor core and the warps.
-// TMEM: S_t at cols [128t, 128t+64), dP_t at [128t+64, 128t+128),
-//       dQ_t at [256 + t*D, 256 + (t+1)*D).
+// Layout of the work (one persistent kernel for every head dim):
+//  * a work tile is 128 query rows of one (batch, head); one CTA per SM walks
+//    its share of the tiles and sweeps the 128-key tiles visible to each;
+//  * warps 0 and 3 stream Q/dO and K/V through shared-memory stages with TMA;
+//  * warp 1 (one thread) issues tcgen05.mma: S = Q K^T and dP = dO V^T into
+//    TMEM, then dQ += dS K with dS read from TMEM (fp16/bf16, aliasing S) and
+//    K read as an MN-major operand of the same shared tile;
+//  * warps 4-7 / 8-11 turn S, dP into dS for key columns [0,64) / [64,128),
+//    one thread per query row, with that row's lse2 and Delta in registers.
 #include "fa_common.cuh"
 #include "fa_kernels.h"
 
 namespace fa {
 
-namespace bdq {
-
-constexpr int BM = dq_cfg::BM;  // query rows per tile
-constexpr int BN = dq_cfg::BN;  // keys per tile
-constexpr int QT = 2;
-constexpr int NUM_THREADS = 384;
-
-template <int D>
-struct Cfg {
-  using G = TileGeom<D>;
-  static constexpr int NST = D == 128 ? 2 : 4;
-  static constexpr int Q_TILE_BYTES = BM * D * 2;
-  static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = OFF_Q + QT * Q_TILE_BYTES;
-  static constexpr int OFF_K = OFF_DO + QT * Q_TILE_BYTES;
-  static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
-  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
-  // s_full[QT], ds_ready[QT], dq_full[QT], mma_done
-  static constexpr int NUM_BARS = 1 + 4 * NST + 3 * QT + 1;
-  static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
-  static constexpr int OFF_MISC = OFF_CTL + 16;
-  static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
-  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int DQ_COL0 = 256;
-  static_assert(DQ_COL0 + QT * D <= TMEM_COLS, "TMEM budget");
-};
-
-}  // namespace bdq
-
-template <int D, int DT>
-__global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
-    fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
-                     const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                     const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
-                     void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh, const long long dq_sn,
-                     const int accumulate_fp32) {
-  using namespace bdq;
-  using C = Cfg<D>;
-  using G = TileGeom<D>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_saddr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((raw_saddr + 1023u) & ~1023u) - raw_saddr);
-  const uint32_t sbase = smem_u32(smem);
-
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::NST;
-  uint64_t* v_full = k_empty + C::NST;
-  uint64_t* v_empty = v_full + C::NST;
-  uint64_t* s_full = v_empty + C::NST;
-  uint64_t* ds_ready = s_full + QT;
-  uint64_t* dq_full = ds_ready + QT;
-  uint64_t* mma_done = dq_full + QT;
-  CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
-  volatile CtaCtl* ctl = ctl_w;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
-
-  const int warp = int(warp_id());
-  const int lane = int(lane_id());
-
-  const int BH = shp.B * shp.Hq;
-  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
-  const int qblk = n_qblk - 1 - int(blockIdx.x) / BH;
-  const int bh = int(blockIdx.x) % BH;
-  const int b = bh / shp.Hq;
-  const int h = bh % shp.Hq;
-  const int kvh = h / (shp.Hq / shp.Hkv);
-  const int row0 = qblk * QT * BM;
-  int n_kv[QT];
-#pragma unroll
-  for (int t = 0; t < QT; ++t) n_kv[t] = kv_tiles_for_rows(shp, row0 + t * BM, BM, BN);
-  const int n_max = n_kv[0] > n_kv[1] ? n_kv[0] : n_kv[1];
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 2);
-    for (int s = 0; s < C::NST; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
-      mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
-    }
-    for (int t = 0; t < QT; ++t) {
-      mbar_init(s_full + t, 1);
-      mbar_init(ds_ready + t, 128);
-      mbar_init(dq_full + t, 1);
-    }
-    mbar_init(mma_done, 1);
-    ctl_w->abort = 0;
-    ctl_w->status = shp.status;
-    fence_mbar_init();
-  }
-  if (warp == 2) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 || warp == 3) {
-    // =================== TMA producers ===================
-    // Warp 0 loads Q and the K tiles, warp 3 dO and the V tiles: one
-    // thread's TMA loads are processed one after another, so two threads
-    // double the stream rate.  q_full expects one arrival from each.
-    const bool is_k = warp == 0;
-    if (lane == 0 && n_max > 0) {
-      const CUtensorMap* tmap_kv = is_k ? &tmap_k : &tmap_v;
-      const CUtensorMap* tmap_qd = is_k ? &tmap_q : &tmap_do;
-      uint64_t* kv_full = is_k ? k_full : v_full;
-      uint64_t* kv_empty = is_k ? k_empty : v_empty;
-      const int kv_off = is_k ? C::OFF_K : C::OFF_V;
-      const int qd_off = is_k ? C::OFF_Q : C::OFF_DO;
-      tma_prefetch_desc(tmap_qd);
-      tma_prefetch_desc(tmap_kv);
-      int q_bytes = 0;
-      for (int t = 0; t < QT; ++t) q_bytes += n_kv[t] > 0 ? C::Q_TILE_BYTES : 0;
-      mbar_arrive_expect_tx(q_full, q_bytes);
-      for (int t = 0; t < QT; ++t) {
-        if (n_kv[t] == 0) continue;
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + qd_off + t * C::Q_TILE_BYTES + bx * BM * G::SW, tmap_qd, q_full, bx * G::BOX,
-                      row0 + t * BM, h, b);
-      }
-      int n_iss = 0;
-      for (int j = 0; j < n_max; ++j) {
-        const int s = j % C::NST;
-        const uint32_t u = uint32_t(j / C::NST);
-        if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, is_k ? 31 : 32)) break;
-        mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                      j * BN, kvh, b);
-        ++n_iss;
-      }
-      mbar_wait_drain(q_full, 0, ctl, 33);
-      for (int j = (n_iss > C::NST ? n_iss - C::NST : 0); j < n_iss; ++j)
-        mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, is_k ? 34 : 35);
-    }
-  } else if (warp == 1) {
-    // =================== tcgen05 MMA issuer ===================
-    if (lane == 0 && n_max > 0) {
-      constexpr uint32_t IDESC_S = idesc_f16_f32(BM, BN, 0, 0, DT);
-      constexpr uint32_t IDESC_DQ = idesc_f16_f32(BM, D, 0, 1, DT);
-      const uint32_t q_s = sbase + C::OFF_Q;
-      const uint32_t do_s = sbase + C::OFF_DO;
-      const uint32_t k_s = sbase + C::OFF_K;
-      const uint32_t v_s = sbase + C::OFF_V;
-      SDesc qd[QT], dd[QT];
-#pragma unroll
-      for (int t = 0; t < QT; ++t) {
-        qd[t] = desc_k_base<D>(q_s + t * C::Q_TILE_BYTES);
-        dd[t] = desc_k_base<D>(do_s + t * C::Q_TILE_BYTES);
-      }
-      auto issue_sdp = [&](int t, int j) {
-        const SDesc kd = desc_k_base<D>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
-        const SDesc vd = desc_k_base<D>(v_s + (j % C::NST) * C::KV_TILE_BYTES);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + t * 128, sdesc_at(qd[t], k_major_off<D, BM>(ks)), sdesc_at(kd, k_major_off<D, BN>(ks)),
-                  IDESC_S, ks > 0);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + t * 128 + 64, sdesc_at(dd[t], k_major_off<D, BM>(ks)), sdesc_at(vd, k_major_off<D, BN>(ks)),
-                  IDESC_S, ks > 0);
-        umma_commit(s_full + t);
-      };
-      auto issue_dq = [&](int t, int j) {
-        const SDesc kd = desc_mn_base<D, BN>(k_s + (j % C::NST) * C::KV_TILE_BYTES);
-        const uint32_t dst = tmem + C::DQ_COL0 + t * D;
-        umma_ts(dst, tmem + t * 128, sdesc_at(kd, 0), IDESC_DQ, j > 0 ? 1u : 0u);
-#pragma unroll
-        for (int ks = 1; ks < BN / 16; ++ks)
-          umma_ts(dst, tmem + t * 128 + ks * 8, sdesc_at(kd, mn_major_off<D>(ks)), IDESC_DQ, 1u);
-      };
-      bool ok = mbar_wait(q_full, 0, ctl, 40) && mbar_wait(k_full, 0, ctl, 41) && mbar_wait(v_full, 0, ctl, 42);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < QT; ++t)
-          if (n_kv[t] > 0) issue_sdp(t, 0);
-        umma_commit(v_empty);
-      }
-      for (int j = 0; j < n_max && ok; ++j) {
-        const bool more = j + 1 < n_max;
-        if (more) {
-          const int s1 = (j + 1) % C::NST;
-          const uint32_t par = uint32_t((j + 1) / C::NST) & 1;
-          if (!mbar_wait(k_full + s1, par, ctl, 43) || !mbar_wait(v_full + s1, par, ctl, 44)) { ok = false; break; }
-        }
-        tc_fence_after();
-        for (int t = 0; t < QT && ok; ++t) {
-          if (j >= n_kv[t]) continue;
-          if (!mbar_wait(ds_ready + t, uint32_t(j) & 1, ctl, 45)) { ok = false; break; }
-          tc_fence_after();
-          issue_dq(t, j);
-          if (j + 1 < n_kv[t]) issue_sdp(t, j + 1);
-        }
-        if (!ok) break;
-        umma_commit(k_empty + j % C::NST);
-        if (more) umma_commit(v_empty + (j + 1) % C::NST);
-      }
-      if (ok) {
-        for (int t = 0; t < QT; ++t)
-          if (n_kv[t] > 0) umma_commit(dq_full + t);
-      }
-      umma_commit(mma_done);
-      mbar_wait_drain(mma_done, 0, ctl, 46);
-    }
-  } else if (warp >= 4) {
-    // =================== dS warpgroups ===================
-    const int t = (warp - 4) / 4;
-    const int wq = warp & 3;
-    const int r = row0 + t * BM + wq * 32 + lane;
-    const int nt = n_kv[t];
-    int lim = shp.Nk - 1;
-    if (shp.causal) {
-      const long long c = (long long)r + shp.q_off - shp.k_off;
-      lim = c < lim ? int(c) : lim;
-    }
-    const bool row_ok = r < shp.Nq;
-    float lse_r = INFINITY, delta_r = 0.f;
-    if (row_ok) {
-      const float x = lse[(long long)bh * shp.Nq + r];
-      lse_r = x == -INFINITY ? INFINITY : x;  // no visible key: every P is 0
-      delta_r = delta[(long long)bh * shp.Nq + r];
-    }
-    const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(t * 128));
-    const uint32_t tQ = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::DQ_COL0 + t * D));
-    const float c2 = shp.scale_log2;
-    const uint64_t c2x2 = f2pack(c2, c2);
-    const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
-    const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
-    bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (!mbar_wait_warp(s_full + t, uint32_t(j) & 1, ctl, 50 + t)) { ok = false; break; }
-      tc_fence_after();
-      float s[BN], dp[BN];
-      tmem_ld64(tS, s);
-      tmem_ld64(tS + 64, dp);
-      const int lim_j = lim - j * BN;
-      if (lim_j < BN - 1) {  // diagonal / boundary tile: hide invisible keys
-#pragma unroll
-        for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
-      }
-#pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c0 = cc * 32 + 2 * i;
-          // P = 2^(s*scale*log2e - lse2) in fp16x2, dS = P * (dP - Delta)
-          const uint32_t p = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nlse2)));
-          const uint32_t d = pack2_f2<DT>(fadd2(f2pack(dp[c0], dp[c0 + 1]), ndelta2));
-          packed[i] = mul2<DT>(p, d);
-        }
-        tmem_st16(tS + cc * 16, packed);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(ds_ready + t);
-    }
-    if (ok && nt > 0) ok = mbar_wait_warp(dq_full + t, 0, ctl, 52 + t);
-    if (ok && row_ok) {
-      if (nt > 0) tc_fence_after();
-    }
-    if (ok) {
-      const float sc = shp.scale;
-#pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
-        float g[32];
-        if (nt > 0) {
-          tmem_ld32(tQ + cc * 32, g);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) g[i] = 0.f;
-        }
-        if (!row_ok) continue;
-        const long long off = (long long)b * dq_sb + (long long)h * dq_sh + (long long)r * dq_sn + cc * 32;
-        if (accumulate_fp32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
-#pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4) {
-            float4 x = dst[v4];
-            x.x += g[v4 * 4 + 0] * sc;
-            x.y += g[v4 * 4 + 1] * sc;
-            x.z += g[v4 * 4 + 2] * sc;
-            x.w += g[v4 * 4 + 3] * sc;
-            dst[v4] = x;
-          }
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dq_out) + off);
-#pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            uint4 pk;
-            pk.x = pack2<DT>(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack2<DT>(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack2<DT>(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack2<DT>(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
-            dst[v8] = pk;
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
-  }
-}
-
 // ---------------------------------------------------------------------------
-// D <= 64: persistent kernel with 128-key tiles.  S = Q K^T and dP = dO V^T
-// become N = 128 MMAs (full tensor rate; N = 64 runs at ~70%).  One CTA per SM
-// walks its share of the work tiles (128 query rows of one batch and head)
-// back to back, with Q and dO double-buffered so that the next tile's loads
-// and first MMAs overlap the current tile's last key tiles and its epilogue.
+// Persistent kernel with 128-key tiles, used for every D.  S = Q K^T and
+// dP = dO V^T become N = 128 MMAs (full tensor rate; N = 64 runs at ~70%).
+// One CTA per SM walks its share of the work tiles (128 query rows of one
+// batch and head) back to back.  At D <= 64, Q and dO are double-buffered so
+// that the next tile's loads and first MMAs overlap the current tile's last
+// key tiles and its epilogue; at D = 128 shared memory holds one Q/dO buffer
+// and two K/V stages.
 // Both warpgroups work on every key tile, warpgroup w on key columns
 // [64w, 64w+64), and S is double-buffered in TMEM so the tensor core computes
 // S of tile j+2 and dP of tile j+1 while the warpgroups exponentiate tile j+1.
@@ -351,20 +33,21 @@ __global__ void __launch_bounds__(bdq::NUM_THREADS, 1)
 // Warpgroup w writes dS into its S buffer's columns [64w, 64w+32), inside the
 // range it read.
 namespace bdqw {
-constexpr int BM = 128;  // query rows per tile
-constexpr int BN = 128;  // keys per key tile
+constexpr int BM = dq_cfg::BM;  // query rows per tile
+constexpr int BN = dq_cfg::BN;  // keys per key tile
 constexpr int NUM_THREADS = 384;
 constexpr int POLY_MASK = 2;  // pairs (i & 7) < 2 use the FMA-pipe exp2: a quarter off MUFU
 
 template <int D>
 struct Cfg {
   using G = TileGeom<D>;
-  static constexpr int NST = 4;
+  static constexpr int NST = D == 128 ? 2 : 4;
+  static constexpr int QB = D == 128 ? 1 : 2;  // Q/dO buffers (tiles in flight)
   static constexpr int Q_TILE_BYTES = BM * D * 2;
   static constexpr int KV_TILE_BYTES = BN * D * 2;
-  static constexpr int OFF_Q = 0;                              // 2 buffers
-  static constexpr int OFF_DO = OFF_Q + 2 * Q_TILE_BYTES;      // 2 buffers
-  static constexpr int OFF_K = OFF_DO + 2 * Q_TILE_BYTES;      // NST stages
+  static constexpr int OFF_Q = 0;                              // QB buffers
+  static constexpr int OFF_DO = OFF_Q + QB * Q_TILE_BYTES;     // QB buffers
+  static constexpr int OFF_K = OFF_DO + QB * Q_TILE_BYTES;     // NST stages
   static constexpr int OFF_V = OFF_K + NST * KV_TILE_BYTES;    // NST stages
   static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
   // q_full[2], q_empty[2], kv_full[NST], kv_empty[NST], s_full[2], dp_full, ds_ready[2], dq_full, dq_empty, mma_done
@@ -376,7 +59,7 @@ struct Cfg {
   static constexpr int TMEM_COLS = 512;
   static constexpr int DP_COL = 256;
   static constexpr int DQ_COL = 384;
-  static_assert(D <= 64, "wide dQ path is for D <= 64");
+  static_assert(DQ_COL + D <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -491,8 +174,8 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         if (t >= n_tiles) break;
         const Tile w = tile_of(shp, t);
         if (w.n_kv == 0) continue;
-        const int tb = tcn & 1;
-        if (tcn >= 2 && !mbar_wait(q_empty + tb, uint32_t((tcn >> 1) - 1) & 1, ctl, 130)) break;
+        const int tb = tcn % C::QB;
+        if (tcn >= C::QB && !mbar_wait(q_empty + tb, uint32_t(tcn / C::QB - 1) & 1, ctl, 130)) break;
         mbar_arrive_expect_tx(q_full + tb, C::Q_TILE_BYTES);
         for (int bx = 0; bx < G::NBOX; ++bx)
           tma_load_4d(smem + qd_off + tb * C::Q_TILE_BYTES + bx * BM * G::SW, tmap_qd, q_full + tb, bx * G::BOX,
@@ -508,8 +191,8 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
                         j * BN, w.kvh, w.b);
         }
       }
-      for (int i = (tcn > 2 ? tcn - 2 : 0); i < tcn; ++i)
-        mbar_wait_drain(q_full + (i & 1), uint32_t(i >> 1) & 1, ctl, 132);
+      for (int i = (tcn > C::QB ? tcn - C::QB : 0); i < tcn; ++i)
+        mbar_wait_drain(q_full + i % C::QB, uint32_t(i / C::QB) & 1, ctl, 132);
       for (int j = (gj > C::NST ? gj - C::NST : 0); j < gj; ++j)
         mbar_wait_drain(kv_full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 133);
     }
@@ -533,8 +216,8 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         if (t >= n_tiles) break;
         const int n_kv = tile_of(shp, t).n_kv;
         if (n_kv == 0) continue;
-        const int tb = tcn & 1;
-        if (!mbar_wait(q_full + tb, uint32_t(tcn >> 1) & 1, ctl, 140)) { ok = false; break; }
+        const int tb = tcn % C::QB;
+        if (!mbar_wait(q_full + tb, uint32_t(tcn / C::QB) & 1, ctl, 140)) { ok = false; break; }
         tc_fence_after();
         const SDesc qd = desc_k_base<D>(sbase + C::OFF_Q + tb * C::Q_TILE_BYTES);
         const SDesc dd = desc_k_base<D>(sbase + C::OFF_DO + tb * C::Q_TILE_BYTES);
@@ -675,7 +358,9 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       constexpr int HALF = D / 2;
       float gv[HALF];
       if (cur.n_kv > 0) {
-        if constexpr (HALF == 32) {
+        if constexpr (HALF == 64) {
+          tmem_ld64(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[64]>(&gv[0]));
+        } else if constexpr (HALF == 32) {
           tmem_ld32(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[32]>(&gv[0]));
         } else {
           tmem_ld16(lane_base + uint32_t(C::DQ_COL + w * HALF), *reinterpret_cast<float(*)[16]>(&gv[0]));
@@ -743,25 +428,11 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, int DT>
-int launch_bwd_dq_t(const BwdArgs& a) {
-  using C = bdq::Cfg<D>;
-  auto kern = fa_bwd_dq_kernel<D, DT>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
-    return FA_ERR_LAUNCH;
-  const int n_qblk = (a.shape.Nq + bdq::QT * bdq::BM - 1) / (bdq::QT * bdq::BM);
-  dim3 grid(unsigned(n_qblk * a.shape.B * a.shape.Hq));
-  kern<<<grid, bdq::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse,
-                                                            a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
-                                                            a.accumulate_fp32);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
-}
-
 int launch_bwd_dq(const BwdArgs& a, int D) {
   switch (D) {
     case 32: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<32, DT_BF16>(a) : launch_bwd_dq_wide_t<32, DT_F16>(a);
     case 64: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<64, DT_BF16>(a) : launch_bwd_dq_wide_t<64, DT_F16>(a);
-    case 128: return a.dtype == DT_BF16 ? launch_bwd_dq_t<128, DT_BF16>(a) : launch_bwd_dq_t<128, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<128, DT_BF16>(a) : launch_bwd_dq_wide_t<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

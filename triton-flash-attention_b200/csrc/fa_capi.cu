@@ -153,7 +153,7 @@ int dq_impl(const void* q, const void* k, const void* v, const void* dO, const f
   a.dtype = dtype;
   if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dq_cfg::BM, dtype))) return rc;
   if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, dq_cfg::BM, dtype))) return rc;
-  const int bn = D <= 64 ? dq_cfg::BN_WIDE : dq_cfg::BN;
+  const int bn = dq_cfg::BN;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, bn, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, bn, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);

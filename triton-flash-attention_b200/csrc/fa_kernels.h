@@ -66,8 +66,7 @@ int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const
 // Query-tile / key-tile sizes the host needs for TMA box shapes.
 namespace dq_cfg {
 constexpr int BM = 128;  // query rows per tile
-constexpr int BN = 64;   // keys per tile (D = 128)
-constexpr int BN_WIDE = 128;  // keys per tile (D <= 64)
+constexpr int BN = 128;  // keys per key tile
 }  // namespace dq_cfg
 namespace dkdv_cfg {
 constexpr int BM = 128;  // key rows per tile (the MMA M dimension)
