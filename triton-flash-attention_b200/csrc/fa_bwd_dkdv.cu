@@ -8,17 +8,21 @@
 // over every query head of the key's group.  The reference sums the group
 // with fp16 atomics (attention.py:503-505); here one CTA owns a key tile and
 // loops over the group's heads itself, so the sum is deterministic.
-// Layout of the work:
-//  * one CTA owns 128 keys of one (batch, kv head): K and V stay resident in
-//    shared memory for the whole sweep;
-//  * warp 0 streams (query head, 64-row query tile) items: Q and dO tiles by
-//    TMA, and the tile's lse2 / Delta values with plain loads by its 32 lanes;
+// Layout of the work (D = 128 kernel; the D <= 64 kernel below differs in
+// the item width):
+//  * a persistent CTA per SM walks work tiles of 128 keys of one (batch, kv
+//    head) in snake order; K and V of a tile stay resident in shared memory
+//    for the tile's whole sweep and are double-buffered across tiles;
+//  * warps 0 and 3 stream (query head, 64-row query tile) items: Q and dO
+//    tiles by TMA, and the items' lse2 / Delta values with plain loads by the
+//    32 lanes of warp 0;
 //  * warp 1 (one thread) issues tcgen05.mma: S^T = K Q^T and dP^T = V dO^T
 //    into one of two TMEM buffers, then dV += P^T dO and dK += dS^T Q with
 //    P^T, dS^T read from TMEM (fp16) and Q, dO read as MN-major operands;
 //  * warps 4-7 and 8-11 take alternate items (two TMEM buffers), one thread
 //    per key row, and write P^T and dS^T back to TMEM;
-//  * at the end warpgroup 0 stores dV and warpgroup 1 stores dK.
+//  * after a tile's last item warpgroup 0 stores dV and warpgroup 1 stores
+//    dK while the MMA issuer already runs the next tile's first S^T / dP^T.
 // TMEM: buffer w: S^T at [128w, 128w+64), dP^T at [128w+64, 128w+128);
 //       dV at [256, 256+D), dK at [256+D, 256+2D).
 #include "fa_common.cuh"
@@ -28,33 +32,92 @@ namespace fa {
 
 namespace bkv {
 
-constexpr int BM = dkdv_cfg::BM;  // keys per CTA (MMA M)
+constexpr int BM = dkdv_cfg::BM;  // keys per tile (MMA M)
 constexpr int BQ = dkdv_cfg::BQ;  // query rows per item (MMA N, then K)
 constexpr int NUM_THREADS = 384;
+// Registers per thread: launched at 168 (384 threads); warps 0-3 (producers,
+// MMA issuer, TMEM owner) drop to CTRL_REGS and the two P^T / dS^T
+// warpgroups rise to SOFT_REGS.  128 * CTRL_REGS + 256 * SOFT_REGS must not
+// exceed 384 * 168 = 64512.
+constexpr uint32_t LAUNCH_REGS = 168;
+constexpr uint32_t CTRL_REGS = 64;
+constexpr uint32_t SOFT_REGS = 216;
+static_assert(128 * CTRL_REGS + 256 * SOFT_REGS <= NUM_THREADS * LAUNCH_REGS, "register split");
 
 template <int D>
 struct Cfg {
   using G = TileGeom<D>;
-  static constexpr int NST = D == 128 ? 3 : 4;
+  static constexpr int NST = 3;  // Q / dO stages (two K / V buffers take 4 x 32 KB at D = 128)
   static constexpr int KV_TILE_BYTES = BM * D * 2;
   static constexpr int Q_TILE_BYTES = BQ * D * 2;
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + KV_TILE_BYTES;
-  static constexpr int OFF_Q = OFF_V + KV_TILE_BYTES;              // NST stages
+  static constexpr int OFF_K = 0;                                  // 2 buffers
+  static constexpr int OFF_V = OFF_K + 2 * KV_TILE_BYTES;          // 2 buffers
+  static constexpr int OFF_Q = OFF_V + 2 * KV_TILE_BYTES;          // NST stages
   static constexpr int OFF_DO = OFF_Q + NST * Q_TILE_BYTES;        // NST stages
   static constexpr int OFF_LSE = OFF_DO + NST * Q_TILE_BYTES;      // NST x BQ floats
   static constexpr int OFF_DELTA = OFF_LSE + NST * BQ * 4;         // NST x BQ floats
   static constexpr int OFF_BAR = OFF_DELTA + NST * BQ * 4;
-  // kv_full, full[NST], empty[NST], st_full[2], ds_ready[2], acc_full, mma_done
-  static constexpr int NUM_BARS = 1 + 2 * NST + 2 + 2 + 1 + 1;
+  // kv_full[2], kv_empty[2], full[NST], empty[NST], st_full[2], ds_ready[2], acc_full, acc_empty, mma_done
+  static constexpr int NUM_BARS = 2 + 2 + 2 * NST + 2 + 2 + 1 + 1 + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
-  static constexpr int SMEM_BYTES = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+  static constexpr int SMEM_BYTES = SMEM_USED;
   static constexpr int TMEM_COLS = 512;
   static constexpr int DV_COL = 256;
   static constexpr int DK_COL = 256 + D;
   static_assert(DK_COL + D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+// A work tile: 128 keys of one (batch, kv head) and the 64-row query items
+// (query head of the group x query tile) that see them.
+struct Tile {
+  int kv0, b, kvh, i_start, per_head, n_items;
+};
+__device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
+  const int BHkv = shp.B * shp.Hkv;
+  const int kv_tile = t / BHkv;
+  const int bhk = t % BHkv;
+  Tile w;
+  w.b = bhk / shp.Hkv;
+  w.kvh = bhk % shp.Hkv;
+  w.kv0 = kv_tile * BM;
+  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  int i_start = 0;
+  if (shp.causal) {
+    // first query tile holding a row at or after this tile's first key
+    const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
+    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
+    if (i_start > n_qt) i_start = n_qt;
+  }
+  w.i_start = i_start;
+  w.per_head = n_qt - i_start;
+  w.n_items = w.per_head * (shp.Hq / shp.Hkv);
+  return w;
+}
+
+// Walks the items of a CTA's non-empty tiles in issue order.
+struct ItemCursor {
+  int k, it, pad;
+  Tile w;
+  // the first item of the first non-empty tile at snake position >= k
+  __device__ __forceinline__ bool seek(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
+    for (;; ++k) {
+      const int t = snake_unit(cta, k, n_cta, n_tiles);
+      if (t >= n_tiles) return false;
+      w = tile_of(shp, t);
+      if (w.n_items > 0) {
+        it = 0;
+        return true;
+      }
+    }
+  }
+  __device__ __forceinline__ bool next(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
+    if (++it < w.n_items) return true;
+    ++k;
+    return seek(shp, cta, n_cta, n_tiles);
+  }
 };
 
 }  // namespace bkv
@@ -66,7 +129,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
                        const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                        void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh, const long long dk_sn,
                        void* __restrict__ dv_out, const long long dv_sb, const long long dv_sh, const long long dv_sn,
-                       const int accumulate_fp32) {
+                       const int accumulate_fp32, const int n_tiles) {
   using namespace bkv;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -77,12 +140,16 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* full = bars + 1;
+  uint64_t* kv_empty = kv_full + 2;
+  uint64_t* full = kv_empty + 2;
   uint64_t* empty = full + C::NST;
+  // per item parity w (items alternate between the warpgroups, counted
+  // across the CTA's tiles)
   uint64_t* st_full = empty + C::NST;
   uint64_t* ds_ready = st_full + 2;
-  uint64_t* acc_full = ds_ready + 2;
-  uint64_t* mma_done = acc_full + 1;
+  uint64_t* acc_full = ds_ready + 2;   // one phase per non-empty tile: dV, dK complete
+  uint64_t* acc_empty = acc_full + 1;  // one phase per non-empty tile: the epilogue read them
+  uint64_t* mma_done = acc_empty + 1;
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
   volatile CtaCtl* ctl = ctl_w;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -91,28 +158,15 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 
   const int warp = int(warp_id());
   const int lane = int(lane_id());
-
-  // ---- work item: key tile (heavy = early tiles under causal first) ----
-  const int BHkv = shp.B * shp.Hkv;
-  const int kv_tile = int(blockIdx.x) / BHkv;
-  const int bhk = int(blockIdx.x) % BHkv;
-  const int b = bhk / shp.Hkv;
-  const int kvh = bhk % shp.Hkv;
   const int group = shp.Hq / shp.Hkv;
-  const int kv0 = kv_tile * BM;
-  const int n_qt = (shp.Nq + BQ - 1) / BQ;
-  int i_start = 0;
-  if (shp.causal) {
-    // first query tile holding a row at or after this tile's first key
-    const long long first_row = (long long)kv0 + shp.k_off - shp.q_off;
-    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
-    if (i_start > n_qt) i_start = n_qt;
-  }
-  const int per_head = n_qt - i_start;
-  const int n_items = per_head * group;
+  const int cta = int(blockIdx.x);
+  const int n_cta = int(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 2);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full + i, 2);  // K from warp 0, V from warp 3
+      mbar_init(kv_empty + i, 1);
+    }
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(full + s, 2 + 32);  // two TMA expect_tx arrives + one arrive per lane of warp 0
       mbar_init(empty + s, 1);
@@ -122,6 +176,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       mbar_init(ds_ready + w, 128);
     }
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
     mbar_init(mma_done, 1);
     ctl_w->abort = 0;
     ctl_w->status = shp.status;
@@ -136,152 +191,194 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 3) {
-    // =================== producer warps ===================
-    // Warp 0 loads K and the Q tiles and writes lse2 / Delta; warp 3 loads V
-    // and the dO tiles.  One thread's TMA loads are processed one after
-    // another, so the two streams come from two threads.
-    const bool is_q = warp == 0;
-    if (n_items > 0) {
+  if (warp < 4) {
+    regs_release<CTRL_REGS>();
+    if (warp == 0 || warp == 3) {
+      // =================== producer warps ===================
+      // Warp 0 loads K and the Q tiles and writes lse2 / Delta; warp 3 loads V
+      // and the dO tiles.  One thread's TMA loads are processed one after
+      // another, so the two streams come from two threads.
+      const bool is_q = warp == 0;
       const CUtensorMap* tmap_kv = is_q ? &tmap_k : &tmap_v;
       const CUtensorMap* tmap_qd = is_q ? &tmap_q : &tmap_do;
+      const int kv_off = is_q ? C::OFF_K : C::OFF_V;
       const int qd_off = is_q ? C::OFF_Q : C::OFF_DO;
       if (lane == 0) {
         tma_prefetch_desc(tmap_qd);
         tma_prefetch_desc(tmap_kv);
-        mbar_arrive_expect_tx(kv_full, C::KV_TILE_BYTES);
-        for (int bx = 0; bx < G::NBOX; ++bx)
-          tma_load_4d(smem + (is_q ? C::OFF_K : C::OFF_V) + bx * BM * G::SW, tmap_kv, kv_full, bx * G::BOX, kv0, kvh, b);
       }
-      // lse2 / Delta of the item's 64 query rows are read with plain
-      // loads issued two items ahead: under the TMA stream one L2 round trip
-      // (~1-2k cycles) would otherwise pace the whole loop.  Rows past Nq, or
-      // rows that see no key, get lse2 = +inf so that their P is 0.
+      // lse2 / Delta of an item's 64 query rows are read with plain loads
+      // issued PF items ahead (across tile boundaries): under the TMA stream one
+      // L2 round trip would otherwise pace the loop.  Rows past Nq, or rows
+      // that see no key, get lse2 = +inf so that their P is 0.
       constexpr int PF = 2;
-      float lv[PF + 1][2], dv[PF + 1][2];
-      auto fetch = [&](int it, float (&l)[2], float (&d)[2]) {
-        const int h = kvh * group + it / per_head;
-        const int q0 = (i_start + it % per_head) * BQ;
-        const long long rowbase = ((long long)b * shp.Hq + h) * shp.Nq;
+      float lv[PF + 1][2], dvv[PF + 1][2];
+      ItemCursor ahead{0, 0, 0, {}};
+      bool ahead_ok = is_q && ahead.seek(shp, cta, n_cta, n_tiles);
+      auto fetch = [&](float (&l)[2], float (&d)[2]) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          l[e] = INFINITY;
+          d[e] = 0.f;
+        }
+        if (!ahead_ok) return;
+        const int h = ahead.w.kvh * group + ahead.it / ahead.w.per_head;
+        const int q0 = (ahead.w.i_start + ahead.it % ahead.w.per_head) * BQ;
+        const long long rowbase = ((long long)ahead.w.b * shp.Hq + h) * shp.Nq;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int qi = q0 + lane * 2 + e;
-          l[e] = INFINITY;
-          d[e] = 0.f;
-          if (is_q && it < n_items && qi < shp.Nq) {
+          if (qi < shp.Nq) {
             l[e] = lse[rowbase + qi];
             d[e] = delta[rowbase + qi];
           }
         }
+        ahead_ok = ahead.next(shp, cta, n_cta, n_tiles);
       };
 #pragma unroll
-      for (int p = 0; p < PF; ++p) fetch(p, lv[p], dv[p]);
-      int n_iss = 0;
-      for (int it = 0; it < n_items; ++it) {
-        if (is_q) fetch(it + PF, lv[PF], dv[PF]);
-        const int s = it % C::NST;
-        const uint32_t u = uint32_t(it / C::NST);
-        if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 61)) break;
-        const int h = kvh * group + it / per_head;
-        const int q0 = (i_start + it % per_head) * BQ;
+      for (int p = 0; p < PF; ++p) fetch(lv[p], dvv[p]);
+      int gi = 0, tcn = 0;  // items and non-empty tiles issued
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = snake_unit(cta, k, n_cta, n_tiles);
+        if (t >= n_tiles) break;
+        const Tile w = tile_of(shp, t);
+        if (w.n_items == 0) continue;
+        const int kb = tcn & 1;
+        if (tcn >= 2 && !mbar_wait_warp(kv_empty + kb, uint32_t((tcn >> 1) - 1) & 1, ctl, 60)) { ok = false; break; }
         if (lane == 0) {
-          mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
+          mbar_arrive_expect_tx(kv_full + kb, C::KV_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
-            tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
-                        b);
+            tma_load_4d(smem + kv_off + kb * C::KV_TILE_BYTES + bx * BM * G::SW, tmap_kv, kv_full + kb, bx * G::BOX,
+                        w.kv0, w.kvh, w.b);
         }
-        if (is_q) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float l = lv[0][e] == -INFINITY ? INFINITY : lv[0][e];
-            s_nlse[s * BQ + lane * 2 + e] = -l;
-            s_ndelta[s * BQ + lane * 2 + e] = -dv[0][e];
+        ++tcn;
+        for (int it = 0; it < w.n_items; ++it) {
+          if (is_q) fetch(lv[PF], dvv[PF]);
+          const int s = gi % C::NST;
+          const uint32_t u = uint32_t(gi / C::NST);
+          if (u > 0 && !mbar_wait_warp(empty + s, (u - 1) & 1, ctl, 61)) { ok = false; break; }
+          const int h = w.kvh * group + it / w.per_head;
+          const int q0 = (w.i_start + it % w.per_head) * BQ;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
+            for (int bx = 0; bx < G::NBOX; ++bx)
+              tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
+                          w.b);
           }
-          mbar_arrive(full + s);
-#pragma unroll
-          for (int p = 0; p < PF; ++p) {
+          if (is_q) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              lv[p][e] = lv[p + 1][e];
-              dv[p][e] = dv[p + 1][e];
+              const float l = lv[0][e] == -INFINITY ? INFINITY : lv[0][e];
+              s_nlse[s * BQ + lane * 2 + e] = -l;
+              s_ndelta[s * BQ + lane * 2 + e] = -dvv[0][e];
+            }
+            mbar_arrive(full + s);
+#pragma unroll
+            for (int p = 0; p < PF; ++p) {
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                lv[p][e] = lv[p + 1][e];
+                dvv[p][e] = dvv[p + 1][e];
+              }
             }
           }
+          ++gi;
         }
-        ++n_iss;
       }
       if (lane == 0) {
-        mbar_wait_drain(kv_full, 0, ctl, 62);
-        for (int it = (n_iss > C::NST ? n_iss - C::NST : 0); it < n_iss; ++it)
-          mbar_wait_drain(full + it % C::NST, uint32_t(it / C::NST) & 1, ctl, 63);
+        for (int j = (tcn > 2 ? tcn - 2 : 0); j < tcn; ++j)
+          mbar_wait_drain(kv_full + (j & 1), uint32_t(j >> 1) & 1, ctl, 62);
+        for (int j = (gi > C::NST ? gi - C::NST : 0); j < gi; ++j)
+          mbar_wait_drain(full + j % C::NST, uint32_t(j / C::NST) & 1, ctl, 63);
       }
-    }
-  } else if (warp == 1) {
-    // =================== tcgen05 MMA issuer ===================
-    if (lane == 0 && n_items > 0) {
-      constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0, DT);
-      constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1, DT);
-      const uint32_t k_s = sbase + C::OFF_K;
-      const uint32_t v_s = sbase + C::OFF_V;
-      const SDesc kd = desc_k_base<D>(k_s);
-      const SDesc vd = desc_k_base<D>(v_s);
-      auto issue_st = [&](int w, int it) {
-        const int s = it % C::NST;
-        const SDesc qd = desc_k_base<D>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
-        const SDesc dd = desc_k_base<D>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
+    } else if (warp == 1) {
+      // =================== tcgen05 MMA issuer ===================
+      if (lane == 0) {
+        constexpr uint32_t IDESC_ST = idesc_f16_f32(BM, BQ, 0, 0, DT);
+        constexpr uint32_t IDESC_G = idesc_f16_f32(BM, D, 0, 1, DT);
+        SDesc kd = desc_k_base<D>(sbase + C::OFF_K);
+        SDesc vd = desc_k_base<D>(sbase + C::OFF_V);
+        auto issue_st = [&](int g) {  // S^T, dP^T of item g -> buffer g & 1
+          const int w = g & 1;
+          const int s = g % C::NST;
+          const SDesc qd = desc_k_base<D>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
+          const SDesc dd = desc_k_base<D>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + w * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)), IDESC_ST,
-                  ks > 0);
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_ss(tmem + w * 128, sdesc_at(kd, k_major_off<D, BM>(ks)), sdesc_at(qd, k_major_off<D, BQ>(ks)), IDESC_ST,
+                    ks > 0);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          umma_ss(tmem + w * 128 + 64, sdesc_at(vd, k_major_off<D, BM>(ks)), sdesc_at(dd, k_major_off<D, BQ>(ks)),
-                  IDESC_ST, ks > 0);
-        umma_commit(st_full + w);
-      };
-      auto issue_grad = [&](int w, int it) {
-        const int s = it % C::NST;
-        const SDesc qd = desc_mn_base<D, BQ>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
-        const SDesc dd = desc_mn_base<D, BQ>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
-        const uint32_t acc0 = it > 0 ? 1u : 0u;
-        umma_ts(tmem + C::DV_COL, tmem + w * 128, sdesc_at(dd, 0), IDESC_G, acc0);
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_ss(tmem + w * 128 + 64, sdesc_at(vd, k_major_off<D, BM>(ks)), sdesc_at(dd, k_major_off<D, BQ>(ks)),
+                    IDESC_ST, ks > 0);
+          umma_commit(st_full + w);
+        };
+        auto issue_grad = [&](int g, bool acc) {
+          const int w = g & 1;
+          const int s = g % C::NST;
+          const SDesc qd = desc_mn_base<D, BQ>(sbase + C::OFF_Q + s * C::Q_TILE_BYTES);
+          const SDesc dd = desc_mn_base<D, BQ>(sbase + C::OFF_DO + s * C::Q_TILE_BYTES);
+          const uint32_t acc0 = acc ? 1u : 0u;
+          umma_ts(tmem + C::DV_COL, tmem + w * 128, sdesc_at(dd, 0), IDESC_G, acc0);
 #pragma unroll
-        for (int ks = 1; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DV_COL, tmem + w * 128 + ks * 8, sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
-        umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64, sdesc_at(qd, 0), IDESC_G, acc0);
+          for (int ks = 1; ks < BQ / 16; ++ks)
+            umma_ts(tmem + C::DV_COL, tmem + w * 128 + ks * 8, sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G, 1u);
+          umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64, sdesc_at(qd, 0), IDESC_G, acc0);
 #pragma unroll
-        for (int ks = 1; ks < BQ / 16; ++ks)
-          umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64 + ks * 8, sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G, 1u);
-      };
-      bool ok = mbar_wait(kv_full, 0, ctl, 70) && mbar_wait(full, 0, ctl, 71);
-      if (ok) {
-        tc_fence_after();
-        issue_st(0, 0);
-        if (n_items > 1) {
-          ok = mbar_wait(full + 1 % C::NST, uint32_t(1 / C::NST) & 1, ctl, 72);
-          if (ok) {
-            tc_fence_after();
-            issue_st(1, 1);
-          }
-        }
-      }
-      for (int it = 0; it < n_items && ok; ++it) {
-        const int w = it & 1;
-        if (!mbar_wait(ds_ready + w, uint32_t(it >> 1) & 1, ctl, 73)) { ok = false; break; }
-        tc_fence_after();
-        issue_grad(w, it);
-        umma_commit(empty + it % C::NST);
-        if (it + 2 < n_items) {
-          const int n2 = it + 2;
-          if (!mbar_wait(full + n2 % C::NST, uint32_t(n2 / C::NST) & 1, ctl, 74)) { ok = false; break; }
+          for (int ks = 1; ks < BQ / 16; ++ks)
+            umma_ts(tmem + C::DK_COL, tmem + w * 128 + 64 + ks * 8, sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G, 1u);
+        };
+        auto wait_full = [&](int g, int site) {
+          const bool r = mbar_wait(full + g % C::NST, uint32_t(g / C::NST) & 1, ctl, site);
           tc_fence_after();
-          issue_st(w, n2);
+          return r;
+        };
+        int gi = 0, tcn = 0;
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          const int t = snake_unit(cta, k, n_cta, n_tiles);
+          if (t >= n_tiles) break;
+          const int n = tile_of(shp, t).n_items;
+          if (n == 0) continue;
+          const int kb = tcn & 1;
+          if (!mbar_wait(kv_full + kb, uint32_t(tcn >> 1) & 1, ctl, 70)) { ok = false; break; }
+          tc_fence_after();
+          kd = desc_k_base<D>(sbase + C::OFF_K + kb * C::KV_TILE_BYTES);
+          vd = desc_k_base<D>(sbase + C::OFF_V + kb * C::KV_TILE_BYTES);
+          // the tile's first two items run while the warpgroups finish the
+          // previous tile
+          if (!wait_full(gi, 71)) { ok = false; break; }
+          issue_st(gi);
+          if (n > 1) {
+            if (!wait_full(gi + 1, 72)) { ok = false; break; }
+            issue_st(gi + 1);
+          }
+          for (int it = 0; it < n; ++it) {
+            const int g = gi + it;
+            if (!mbar_wait(ds_ready + (g & 1), uint32_t(g >> 1) & 1, ctl, 73)) { ok = false; break; }
+            // dV / dK of the previous tile were read by the epilogue
+            if (it == 0 && tcn > 0 && !mbar_wait(acc_empty, uint32_t(tcn - 1) & 1, ctl, 76)) { ok = false; break; }
+            tc_fence_after();
+            issue_grad(g, it > 0);
+            umma_commit(empty + g % C::NST);
+            if (it + 2 < n) {
+              if (!wait_full(g + 2, 74)) { ok = false; break; }
+              issue_st(g + 2);
+            }
+          }
+          if (!ok) break;
+          umma_commit(acc_full);
+          umma_commit(kv_empty + kb);
+          gi += n;
+          ++tcn;
         }
+        umma_commit(mma_done);
+        mbar_wait_drain(mma_done, 0, ctl, 75);
       }
-      if (ok) umma_commit(acc_full);
-      umma_commit(mma_done);
-      mbar_wait_drain(mma_done, 0, ctl, 75);
     }
-  } else if (warp >= 4) {
+  } else {
+    regs_claim<SOFT_REGS>();
     // =================== P^T / dS^T warpgroups ===================
     const int w = (warp - 4) / 4;  // item parity and TMEM buffer of this warpgroup
     const int wq = warp & 3;
@@ -289,74 +386,88 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(w * 128));
     const float c2 = shp.scale_log2;
     const uint64_t c2x2 = f2pack(c2, c2);
-    // causal: key row rl sees query column c of an item at rows q0.. iff
-    // c >= cmin_base - q0
-    const long long cmin_base = (long long)kv0 + rl + shp.k_off - shp.q_off;
+    int gi = 0, tcn = 0;
     bool ok = true;
-    for (int it = w; it < n_items; it += 2) {
-      const int s = it % C::NST;
-      if (!mbar_wait_warp(st_full + w, uint32_t(it >> 1) & 1, ctl, 80 + w)) { ok = false; break; }
-      // the stage's lse2/Delta values: their phase completed before st_full
-      if (!mbar_wait_warp(full + s, uint32_t(it / C::NST) & 1, ctl, 82 + w)) { ok = false; break; }
-      tc_fence_after();
-      float st[BQ], dpt[BQ];
-      tmem_ld64(tS, st);
-      tmem_ld64(tS + 64, dpt);
-      const int q0 = (i_start + it % per_head) * BQ;
-      int cmin = 0;
-      if (shp.causal) {
-        const long long x = cmin_base - q0;
-        cmin = x <= 0 ? 0 : (x > BQ ? BQ : int(x));
-      }
-      if (cmin > 0) {  // causal diagonal: queries before this key are invisible
+    for (int k = 0; ok; ++k) {
+      const int t = snake_unit(cta, k, n_cta, n_tiles);
+      if (t >= n_tiles) break;
+      const Tile wt = tile_of(shp, t);
+      // causal: key row rl sees query column c of an item at rows q0.. iff
+      // c >= cmin_base - q0
+      const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
+      // this warpgroup's items of the tile: global parity w
+      for (int it = ((gi & 1) == w ? 0 : 1); it < wt.n_items; it += 2) {
+        const int g = gi + it;
+        const int s = g % C::NST;
+        if (!mbar_wait_warp(st_full + w, uint32_t(g >> 1) & 1, ctl, 80 + w)) { ok = false; break; }
+        // the stage's lse2/Delta values: their phase completed before st_full
+        if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 82 + w)) { ok = false; break; }
+        tc_fence_after();
+        float st[BQ], dpt[BQ];
+        tmem_ld64(tS, st);
+        tmem_ld64(tS + 64, dpt);
+        const int q0 = (wt.i_start + it % wt.per_head) * BQ;
+        int cmin = 0;
+        if (shp.causal) {
+          const long long x = cmin_base - q0;
+          cmin = x <= 0 ? 0 : (x > BQ ? BQ : int(x));
+        }
+        if (cmin > 0) {  // causal diagonal: queries before this key are invisible
 #pragma unroll
-        for (int c = 0; c < BQ; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
-      }
-      // stage values are stored negated: -lse2 and -Delta
-      const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ);
-      const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ);
-      uint32_t pk_p[BQ / 2], pk_ds[BQ / 2];
+          for (int c = 0; c < BQ; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+        }
+        // stage values are stored negated: -lse2 and -Delta
+        const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ);
+        const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ);
+        uint32_t pk_p[BQ / 2], pk_ds[BQ / 2];
 #pragma unroll
-      for (int c4 = 0; c4 < BQ / 4; ++c4) {
-        const float4 nl = l4[c4];
-        const float4 nd = d4[c4];
-        const int c = c4 * 4;
-        const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
-        const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
-        const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-        const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-        pk_p[c4 * 2] = p01;
-        pk_p[c4 * 2 + 1] = p23;
-        pk_ds[c4 * 2] = mul2<DT>(p01, d01);
-        pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+        for (int c4 = 0; c4 < BQ / 4; ++c4) {
+          const float4 nl = l4[c4];
+          const float4 nd = d4[c4];
+          const int c = c4 * 4;
+          const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
+          const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
+          const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+          const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+          pk_p[c4 * 2] = p01;
+          pk_p[c4 * 2 + 1] = p23;
+          pk_ds[c4 * 2] = mul2<DT>(p01, d01);
+          pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+        }
+        tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
+        tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
+        tmem_st16(tS + 64, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+        tmem_st16(tS + 80, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(ds_ready + w);
       }
-      tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
-      tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
-      tmem_st16(tS + 64, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
-      tmem_st16(tS + 80, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(ds_ready + w);
-    }
-    // ---- epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK ----
-    if (ok && n_items > 0) ok = mbar_wait_warp(acc_full, 0, ctl, 84 + w);
-    if (ok) {
-      const int kr = kv0 + rl;
+      if (!ok) break;
+      // ---- epilogue of the tile: warpgroup 0 stores dV, warpgroup 1 stores dK ----
+      if (wt.n_items > 0) {
+        if (!mbar_wait_warp(acc_full, uint32_t(tcn) & 1, ctl, 84 + w)) { ok = false; break; }
+        tc_fence_after();
+      }
+      const int kr = wt.kv0 + rl;
       const bool row_ok = kr < shp.Nk;
       const float sc = w == 0 ? 1.f : shp.scale;
       const uint32_t tAcc = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(w == 0 ? C::DV_COL : C::DK_COL));
       void* out = w == 0 ? dv_out : dk_out;
-      const long long off0 = w == 0 ? ((long long)b * dv_sb + (long long)kvh * dv_sh + (long long)kr * dv_sn)
-                                    : ((long long)b * dk_sb + (long long)kvh * dk_sh + (long long)kr * dk_sn);
-      if (n_items > 0) tc_fence_after();
+      const long long off0 = w == 0 ? ((long long)wt.b * dv_sb + (long long)wt.kvh * dv_sh + (long long)kr * dv_sn)
+                                    : ((long long)wt.b * dk_sb + (long long)wt.kvh * dk_sh + (long long)kr * dk_sn);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
-        float g[32];
-        if (n_items > 0) {
-          tmem_ld32(tAcc + cc * 32, g);
+        float gv[32];
+        if (wt.n_items > 0) {
+          tmem_ld32(tAcc + cc * 32, gv);
+          if (cc == D / 32 - 1) {
+            // both accumulators are read: the next tile may overwrite them
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+          }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) g[i] = 0.f;
+          for (int i = 0; i < 32; ++i) gv[i] = 0.f;
         }
         if (!row_ok) continue;
         if (accumulate_fp32) {
@@ -364,10 +475,10 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
             float4 x = dst[v4];
-            x.x += g[v4 * 4 + 0] * sc;
-            x.y += g[v4 * 4 + 1] * sc;
-            x.z += g[v4 * 4 + 2] * sc;
-            x.w += g[v4 * 4 + 3] * sc;
+            x.x += gv[v4 * 4 + 0] * sc;
+            x.y += gv[v4 * 4 + 1] * sc;
+            x.z += gv[v4 * 4 + 2] * sc;
+            x.w += gv[v4 * 4 + 3] * sc;
             dst[v4] = x;
           }
         } else {
@@ -375,13 +486,17 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;
-            pk.x = pack2<DT>(g[v8 * 8 + 0] * sc, g[v8 * 8 + 1] * sc);
-            pk.y = pack2<DT>(g[v8 * 8 + 2] * sc, g[v8 * 8 + 3] * sc);
-            pk.z = pack2<DT>(g[v8 * 8 + 4] * sc, g[v8 * 8 + 5] * sc);
-            pk.w = pack2<DT>(g[v8 * 8 + 6] * sc, g[v8 * 8 + 7] * sc);
+            pk.x = pack2<DT>(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
+            pk.y = pack2<DT>(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);
+            pk.z = pack2<DT>(gv[v8 * 8 + 4] * sc, gv[v8 * 8 + 5] * sc);
+            pk.w = pack2<DT>(gv[v8 * 8 + 6] * sc, gv[v8 * 8 + 7] * sc);
             dst[v8] = pk;
           }
         }
+      }
+      if (wt.n_items > 0) {
+        gi += wt.n_items;
+        ++tcn;
       }
     }
   }
@@ -474,13 +589,6 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.per_head = n_qt - i_start;
   w.n_items = w.per_head * (shp.Hq / shp.Hkv);
   return w;
-}
-// The k-th tile of CTA c when G CTAs share n tiles: snake order over rounds
-// of G (tiles are numbered heaviest first for causal masks), which evens out
-// the items per CTA.  Returns n when the CTA has no k-th tile.
-__device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
-  const int t = k * G + ((k & 1) ? G - 1 - c : c);
-  return t < n ? t : n;
 }
 }  // namespace bkvw
 
@@ -581,13 +689,13 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     constexpr int PF = 2;
     float lv[PF + 1][4], dv[PF + 1][4];
     int pf_k = 0, pf_it = 0;  // prefetch cursor: tile round k, item it
-    Tile pf_w = tile_of(shp, tile_index(cta, 0, n_cta, n_tiles) < n_tiles ? tile_index(cta, 0, n_cta, n_tiles) : 0);
-    bool pf_live = tile_index(cta, 0, n_cta, n_tiles) < n_tiles;
+    Tile pf_w = tile_of(shp, snake_unit(cta, 0, n_cta, n_tiles) < n_tiles ? snake_unit(cta, 0, n_cta, n_tiles) : 0);
+    bool pf_live = snake_unit(cta, 0, n_cta, n_tiles) < n_tiles;
     auto pf_skip_empty = [&]() {
       while (pf_live && pf_it >= pf_w.n_items) {
         pf_it = 0;
         ++pf_k;
-        const int t = tile_index(cta, pf_k, n_cta, n_tiles);
+        const int t = snake_unit(cta, pf_k, n_cta, n_tiles);
         pf_live = t < n_tiles;
         if (pf_live) pf_w = tile_of(shp, t);
       }
@@ -618,7 +726,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     int gi = 0, tcn = 0;  // items and non-empty tiles issued
     bool ok = true;
     for (int k = 0; ok; ++k) {
-      const int t = tile_index(cta, k, n_cta, n_tiles);
+      const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
       const Tile w = tile_of(shp, t);
       if (w.n_items == 0) continue;
@@ -706,7 +814,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
       int gi = 0, tcn = 0;
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int t = tile_index(cta, k, n_cta, n_tiles);
+        const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
         const int n = tile_of(shp, t).n_items;
         if (n == 0) continue;
@@ -776,7 +884,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     int gi = 0, tcn = 0;
     bool ok = true;
     for (int k = 0; ok; ++k) {
-      const int t = tile_index(cta, k, n_cta, n_tiles);
+      const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
       const Tile wt = tile_of(shp, t);
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
@@ -936,13 +1044,24 @@ template <int D, int DT>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
   auto kern = fa_bwd_dkdv_kernel<D, DT>;
+  // The register split inside the kernel assumes the launch count; a build
+  // that allocated a different number must not run (an increase that does
+  // not fit would wait forever).
+  static int regs_ok = -1;
+  if (regs_ok < 0) {
+    cudaFuncAttributes fa_attr;
+    regs_ok = cudaFuncGetAttributes(&fa_attr, kern) == cudaSuccess && fa_attr.numRegs == int(bkv::LAUNCH_REGS) ? 1 : 0;
+  }
+  if (!regs_ok) return FA_ERR_LAUNCH;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkv::BM - 1) / bkv::BM;
-  dim3 grid(unsigned(n_kt * a.shape.B * a.shape.Hkv));
-  kern<<<grid, bkv::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape,
-                                                            a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv,
-                                                            a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32);
+  const int n_tiles = n_kt * a.shape.B * a.shape.Hkv;
+  const int sms = device_sm_count();
+  const int n_cta = n_tiles < sms ? n_tiles : sms;
+  kern<<<dim3(unsigned(n_cta)), bkv::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
+      a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv, a.dv_sb,
+      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

@@ -81,12 +81,6 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.n_kv = kv_tiles_for_rows(shp, w.row0, BM, BN);
   return w;
 }
-// The k-th tile of CTA c when G CTAs share n tiles (snake order over rounds
-// of G); n when the CTA has no k-th tile.
-__device__ __forceinline__ int tile_index(int c, int k, int G, int n) {
-  const int t = k * G + ((k & 1) ? G - 1 - c : c);
-  return t < n ? t : n;
-}
 }  // namespace bdqw
 
 template <int D, int DT>
@@ -170,7 +164,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       int gj = 0, tcn = 0;  // key tiles and non-empty tiles issued
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int t = tile_index(cta, k, n_cta, n_tiles);
+        const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
         const Tile w = tile_of(shp, t);
         if (w.n_kv == 0) continue;
@@ -212,7 +206,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       int gj = 0, tcn = 0;
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int t = tile_index(cta, k, n_cta, n_tiles);
+        const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
         const int n_kv = tile_of(shp, t).n_kv;
         if (n_kv == 0) continue;
@@ -294,7 +288,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         d = delta[bh * shp.Nq + r];
       }
     };
-    int t_cur = tile_index(cta, 0, n_cta, n_tiles);
+    int t_cur = snake_unit(cta, 0, n_cta, n_tiles);
     Tile wt = tile_of(shp, t_cur < n_tiles ? t_cur : 0);
     float lse_n = INFINITY, delta_n = 0.f;
     if (t_cur < n_tiles) row_vals(wt, lse_n, delta_n);
@@ -303,7 +297,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     for (int k = 0; ok && t_cur < n_tiles; ++k) {
       const Tile cur = wt;
       const float lse_r = lse_n, delta_r = delta_n;
-      t_cur = tile_index(cta, k + 1, n_cta, n_tiles);
+      t_cur = snake_unit(cta, k + 1, n_cta, n_tiles);
       if (t_cur < n_tiles) {
         wt = tile_of(shp, t_cur);
         row_vals(wt, lse_n, delta_n);

@@ -65,4 +65,12 @@ __device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, int r0, int
   return last / BN + 1;
 }
 
+// Persistent kernels: the k-th work unit of CTA c when G CTAs share n units
+// numbered heaviest first.  Snake order over rounds of G evens out the work
+// per CTA; returns n when the CTA has no k-th unit.
+__device__ __forceinline__ int snake_unit(int c, int k, int G, int n) {
+  const int t = k * G + ((k & 1) ? G - 1 - c : c);
+  return t < n ? t : n;
+}
+
 }  // namespace fa

@@ -102,12 +102,6 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   }
   return w;
 }
-// The k-th unit of CTA c when G CTAs share n units (snake order over rounds
-// of G); n when the CTA has no k-th unit.
-__device__ __forceinline__ int unit_index(int c, int k, int G, int n) {
-  const int t = k * G + ((k & 1) ? G - 1 - c : c);
-  return t < n ? t : n;
-}
 
 }  // namespace fwd
 
@@ -198,7 +192,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         int gj = 0, uc = 0;  // key tiles and non-empty units issued
         bool ok = true;
         for (int k = 0; ok; ++k) {
-          const int ui = unit_index(cta, k, n_cta, n_units);
+          const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
           const Unit w = unit_of(shp, ui);
           if (w.n_max == 0) continue;
@@ -246,7 +240,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         int oc[QT] = {0, 0};   // units in which tile t saw a key (o_full / o_empty phases)
         bool ok = true;
         for (int k = 0; ok; ++k) {
-          const int ui = unit_index(cta, k, n_cta, n_units);
+          const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
           const Unit w = unit_of(shp, ui);
           if (w.n_max == 0) continue;
@@ -332,7 +326,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     int cnt = 0, oc = 0;  // phases of s_full / o_full of this tile
     bool ok = true;
     for (int k = 0; ok; ++k) {
-      const int ui = unit_index(cta, k, n_cta, n_units);
+      const int ui = snake_unit(cta, k, n_cta, n_units);
       if (ui >= n_units) break;
       const Unit w = unit_of(shp, ui);
       const int r = w.row0 + t * BM + row_local;  // query row
