@@ -7,17 +7,21 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-* ``value``: one step = forward + Delta + dQ + dK/dV on device-resident
-  synthetic inputs (seeded N(0,1) fp16), K steps timed with CUDA events,
-  max over ranks.  The per-step working set (q, k, v, o, dO, dq, dk, dv =
+* ``value``: one step = forward + backward on device-resident synthetic
+  inputs (seeded N(0,1) fp16), K steps timed with CUDA events, max over
+  ranks.  The backward is the product's default at D = 64: preprocess
+  (Delta, zeroed fp32 dQ accumulator), the fused dK/dV + dQ kernel, and the
+  dQ cast; ``--deterministic`` times the bitwise-reproducible path instead
+  (Delta, dQ kernel, dK/dV kernel).  The per-step working set (q, k, v, o, dO, dq, dk, dv =
   256 MiB) exceeds the 126 MB L2, so no flush is inserted.
 * ``e2e``: the same metric through the public API
   (``scaled_dot_product_attention`` + autograd backward) with pinned host
   buffers: each step copies q, k, v, dO host->device and O, dQ, dK, dV
   device->host inside the timed region; the copies of neighbouring steps
   overlap the compute (two copy streams, double-buffered device inputs).
-* ``roofline``: the dominant kernel (dK/dV) -- its GEMM FLOPs per launch over
-  its CUDA-event duration against the measured dense bf16/fp16 peak.
+* ``roofline``: the dominant kernel (the fused backward; dK/dV under
+  ``--deterministic``) -- its GEMM FLOPs per launch over its CUDA-event
+  duration against the measured dense bf16/fp16 peak.
 * ``cpu_baseline``: the oracle's float32 restatement of the reference's CPU
   path timed on the host cores on a bounded sample (whole heads of C2).
 * Multi-GPU (torchrun): weak scaling -- every rank runs its own C2-sized
@@ -49,7 +53,9 @@ if ROOT not in sys.path:
 B, H, N, D = 4, 16, 4096, 64
 CAUSAL = True
 WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
-DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472  # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch (--set full capture of this command)
+DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472
+FUSED_TRAFFIC_BYTES = None
 
 
 def flops_step() -> int:
@@ -201,9 +207,40 @@ def run_ours(args) -> None:
     stream = torch.cuda.current_stream(dev)
 
     ev_kv = []
+    if args.deterministic:
+        torch.use_deterministic_algorithms(True)
+    fused = fa.fused_backward_enabled(D)
+    if fused:
+        # the fused kernel alone, bracketed by events, for the roofline line
+        from triton_flash_attention_b200 import _abi
+        dq_acc = torch.empty(B, H, N, D, device=dev, dtype=torch.float32)
+        delta_buf = torch.empty(B, H, N, device=dev, dtype=torch.float32)
+        dk_buf, dv_buf = torch.empty_like(q), torch.empty_like(q)
 
     def step(record: bool):
         o, lse = fa.attention_forward(q, k, v, CAUSAL, scale)
+        if fused:
+            sh = stream.cuda_stream
+            _abi.check(_abi.lib().fa_bwd_preprocess(o.data_ptr(), do.data_ptr(), delta_buf.data_ptr(),
+                                                    dq_acc.data_ptr(), B, H, N, D, _abi.strides3(o),
+                                                    _abi.strides3(do), sh), "fa_bwd_preprocess")
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            _abi.check(_abi.lib().fa_bwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                               lse.data_ptr(), delta_buf.data_ptr(), dq_acc.data_ptr(),
+                                               dk_buf.data_ptr(), dv_buf.data_ptr(), B, H, H, N, N, D,
+                                               _abi.strides3(q), _abi.strides3(k), _abi.strides3(v),
+                                               _abi.strides3(do), _abi.strides3(dk_buf), _abi.strides3(dv_buf),
+                                               scale, 1 if CAUSAL else 0, 0, 0, 0, sh), "fa_bwd_fused")
+            if record:
+                e1.record(stream)
+                ev_kv.append((e0, e1))
+            dq = torch.empty_like(q)
+            _abi.check(_abi.lib().fa_bwd_dq_convert(dq_acc.data_ptr(), dq.data_ptr(), B, H, N, D,
+                                                    _abi.strides3(dq), sh), "fa_bwd_dq_convert")
+            return
         delta = fa.attention_delta(o, do)
         fa.attention_backward_dq(q, k, v, do, lse, delta, CAUSAL, scale)
         if record:
@@ -310,13 +347,15 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
 
-    # dK/dV kernel: 4 GEMMs of 2*pairs*D FLOPs per (b, h) = 2x the forward
-    kv_flops = 2 * fa.attention_flops(batch=B, query_heads=H, sequence=N, head_dim=D, causal=CAUSAL,
-                                      mode="forward")
+    # The forward's 2 GEMMs are 4*pairs*D FLOPs per (b, h); the dK/dV kernel
+    # runs 4 GEMMs of 2*pairs*D (2x the forward), the fused kernel 5 (2.5x).
+    fwd_flops = fa.attention_flops(batch=B, query_heads=H, sequence=N, head_dim=D, causal=CAUSAL, mode="forward")
+    kv_flops = fwd_flops * 5 // 2 if fused else 2 * fwd_flops
     achieved = kv_flops / (kv_ms * 1e-3) / 1e12
     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch of
-    # the dK/dV kernel, from a --set full capture of this command
-    traffic = DKDV_TRAFFIC_BYTES
+    # the kernel, from a --set full capture of this command
+    traffic = FUSED_TRAFFIC_BYTES if fused else DKDV_TRAFFIC_BYTES
+    rl_kernel = "fa_bwd_fused_kernel<64>" if fused else "fa_bwd_dkdv_wide_kernel<64>"
     if rank == 0:
         line = {
             "metric": "causal fp16 fwd+bwd TFLOP/s, B4 H16 N4096 D64; % of B200 FP16 tensor peak",
@@ -339,7 +378,9 @@ def run_ours(args) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "copies": "pinned host buffers; copies of neighbouring steps overlap the compute"},
-            "roofline": {"kernel": "fa_bwd_dkdv_wide_kernel<64>", "bound": "tensor", "achieved": round(achieved, 2),
+            "backward": "fused dK/dV + dQ (dQ summed by fp32 reduce-adds)" if fused
+                        else "deterministic: separate dQ and dK/dV kernels",
+            "roofline": {"kernel": rl_kernel, "bound": "tensor", "achieved": round(achieved, 2),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                          "peak_source": peaks["source"], "launch_ms": round(kv_ms, 4)},
@@ -600,6 +641,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="time the bitwise-reproducible backward (separate dQ and dK/dV kernels)")
     ap.add_argument("--workload", choices=["c2", "ring", "sweep"], default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
                          "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel")

@@ -113,7 +113,38 @@ FA_API int fa_merge_partial(float* o_acc, float* lse_acc, const void* o_part,
                      const float* lse_part, int B, int H, int N, int D,
                      void* stream);
 
-/* bf16 twins of the five entry points above (same arguments). */
+/* Fused backward, step 1 of 3: delta as fa_bwd_delta, and dq_accum -- the
+ * caller's contiguous (B, H, N, D) fp32 buffer -- set to zero on the way
+ * (dq_accum may be NULL).  Same role as fa_bwd_delta (attention.py:731-744). */
+FA_API int fa_bwd_preprocess(const void* o, const void* dO, float* delta, float* dq_accum,
+                      int B, int H, int N, int D,
+                      const int64_t* o_strides, const int64_t* do_strides,
+                      void* stream);
+
+/* Fused backward, step 2 of 3 (D = 32 or 64): dK, dV exactly as fa_bwd_dkdv
+ * and, in the same pass over the (key tile, query tile) pairs, dQ added into
+ * dq_accum, the caller's contiguous (B, Hq, Nq, D) fp32 buffer.  Replaces the
+ * whole _attn_bwd launch (attention.py:746-783, kernel :383-573), which
+ * rebuilds P and dS once for dK/dV and once for dQ; here they are built once.
+ * dQ is summed with fp32 reduce-adds whose order follows the schedule, so it
+ * is not bitwise reproducible run to run (dK, dV are).  The library
+ * allocates nothing: dq_accum is the only scratch and the caller owns it. */
+FA_API int fa_bwd_fused(const void* q, const void* k, const void* v, const void* dO,
+                 const float* lse, const float* delta, float* dq_accum,
+                 void* dk, void* dv,
+                 int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                 const int64_t* q_strides, const int64_t* k_strides,
+                 const int64_t* v_strides, const int64_t* do_strides,
+                 const int64_t* dk_strides, const int64_t* dv_strides,
+                 float softmax_scale, int causal, int q_offset, int k_offset,
+                 int accumulate_fp32, void* stream);
+
+/* Fused backward, step 3 of 3: dq (element strides {batch, head, seq}) =
+ * dq_accum (contiguous (B, H, N, D) fp32) rounded to fp16. */
+FA_API int fa_bwd_dq_convert(const float* dq_accum, void* dq, int B, int H, int N, int D,
+                      const int64_t* dq_strides, void* stream);
+
+/* bf16 twins of the entry points above (same arguments). */
 FA_API int fa_fwd_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
                 int B, int Hq, int Hkv, int Nq, int Nk, int D,
                 const int64_t* q_strides, const int64_t* k_strides,
@@ -143,6 +174,21 @@ FA_API int fa_bwd_dkdv_bf16(const void* q, const void* k, const void* v, const v
 FA_API int fa_merge_partial_bf16(float* o_acc, float* lse_acc, const void* o_part,
                           const float* lse_part, int B, int H, int N, int D,
                           void* stream);
+FA_API int fa_bwd_preprocess_bf16(const void* o, const void* dO, float* delta, float* dq_accum,
+                           int B, int H, int N, int D,
+                           const int64_t* o_strides, const int64_t* do_strides,
+                           void* stream);
+FA_API int fa_bwd_fused_bf16(const void* q, const void* k, const void* v, const void* dO,
+                      const float* lse, const float* delta, float* dq_accum,
+                      void* dk, void* dv,
+                      int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                      const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* do_strides,
+                      const int64_t* dk_strides, const int64_t* dv_strides,
+                      float softmax_scale, int causal, int q_offset, int k_offset,
+                      int accumulate_fp32, void* stream);
+FA_API int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, int H, int N, int D,
+                           const int64_t* dq_strides, void* stream);
 
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
@@ -152,7 +198,8 @@ FA_API int fa_device_status(int reset);
 /* Human-readable text of an FA_ERR_* code. */
 FA_API const char* fa_status_string(int code);
 
-/* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16). */
+/* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
+ * 1.2.0 the fused backward). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

@@ -68,3 +68,17 @@ def test_rejects_misaligned_output_and_nonfinite_scale():
         == _abi.FA_ERR_BAD_SHAPE
     odd = (ctypes.c_int64 * 3)(4096, 1024, 63)
     assert lib.fa_bwd_delta(16, 16, 16, 1, 1, 8, 64, odd, s, None) == _abi.FA_ERR_MISALIGNED
+
+
+def test_fused_backward_validation_without_cuda():
+    """The fused backward serves D = 32 and 64 only and wants a 16-byte
+    aligned fp32 dQ accumulator; both are refused before any CUDA call."""
+    s = _strides()
+    lib = _abi.lib()
+    for name in ("fa_bwd_fused", "fa_bwd_fused_bf16"):
+        rc = getattr(lib, name)(16, 16, 16, 16, 16, 16, 16, 16, 16, 1, 1, 1, 8, 8, 128, s, s, s, s, s, s,
+                                0.1, 1, 0, 0, 0, None)
+        assert rc == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
+    assert lib.fa_bwd_preprocess(16, 16, 16, 18, 1, 1, 8, 64, s, s, None) == _abi.FA_ERR_MISALIGNED
+    assert lib.fa_bwd_dq_convert(18, 16, 1, 1, 8, 64, s, None) == _abi.FA_ERR_MISALIGNED
+    assert lib.fa_bwd_dq_convert(16, 16, 1, 1, 8, 48, s, None) == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM

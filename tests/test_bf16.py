@@ -88,7 +88,7 @@ def test_bf16_full_size_c2_head():
         assert err <= 2 * terr + 2e-3, (err, terr)
 
 
-def test_bf16_bitwise_determinism():
+def test_bf16_bitwise_determinism(deterministic):
     q, k, v, do = _inputs(1, 8, 2, 500, 500, 64, seed=3)
     a = _grads(fa.scaled_dot_product_attention, q, k, v, do, True)
     b = _grads(fa.scaled_dot_product_attention, q, k, v, do, True)

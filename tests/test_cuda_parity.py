@@ -150,8 +150,9 @@ def test_golden_vectors():
 
 
 @pytest.mark.parametrize("hq,hkv", [(4, 4), (8, 2)])
-def test_bitwise_determinism(hq, hkv):
-    """No atomics anywhere: repeated runs are bitwise identical."""
+def test_bitwise_determinism(hq, hkv, deterministic):
+    """Deterministic mode (separate dQ and dK/dV kernels, no atomics):
+    repeated runs are bitwise identical."""
     q, k, v, do = _inputs(2, hq, hkv, 1000, 1000, 64, 9)
     a = _run_api(q, k, v, do, True)
     b = _run_api(q, k, v, do, True)

@@ -10,12 +10,15 @@ from .attention import (
     B200Attention,
     DispatchDecision,
     SUPPORTED_HEAD_DIMS,
+    FUSED_BWD_HEAD_DIMS,
     TritonAttention,
     attention_backward_dkdv,
     attention_backward_dq,
+    attention_backward_fused,
     attention_delta,
     attention_forward,
     explain_dispatch,
+    fused_backward_enabled,
     scaled_dot_product_attention,
 )
 from .flops import attention_flops, delta_bytes, memory_model
@@ -24,14 +27,17 @@ __all__ = [
     "B200Attention",
     "DispatchDecision",
     "SUPPORTED_HEAD_DIMS",
+    "FUSED_BWD_HEAD_DIMS",
     "TritonAttention",
     "attention_backward_dkdv",
     "attention_backward_dq",
+    "attention_backward_fused",
     "attention_delta",
     "attention_flops",
     "attention_forward",
     "delta_bytes",
     "explain_dispatch",
+    "fused_backward_enabled",
     "memory_model",
     "scaled_dot_product_attention",
 ]

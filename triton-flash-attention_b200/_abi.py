@@ -39,6 +39,10 @@ SIGNATURES = {
     "fa_bwd_dkdv": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
                          _s, _s, _s, _s, _s, _s, _f, _i, _i, _i, _i, _p]),
     "fa_merge_partial": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "fa_bwd_preprocess": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _s, _s, _p]),
+    "fa_bwd_fused": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
+                          _s, _s, _s, _s, _s, _s, _f, _i, _i, _i, _i, _p]),
+    "fa_bwd_dq_convert": (_i, [_p, _p, _i, _i, _i, _i, _s, _p]),
 }
 # the bf16 twins take the same arguments
 SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in list(SIGNATURES)})

@@ -178,6 +178,48 @@ def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale
     return dk, dv
 
 
+FUSED_BWD_HEAD_DIMS = (32, 64)
+
+
+def fused_backward_enabled(head_dim: int) -> bool:
+    """Whether the backward runs as one fused dK/dV + dQ pass: head dims 32
+    and 64, unless ``torch.use_deterministic_algorithms(True)`` asks for
+    bitwise-reproducible gradients (the fused pass sums dQ with fp32
+    reduce-adds in schedule order; the separate dQ kernel does not)."""
+    return head_dim in FUSED_BWD_HEAD_DIMS and not torch.are_deterministic_algorithms_enabled()
+
+
+def attention_backward_fused(q, k, v, o, do, lse, causal: bool, softmax_scale: float):
+    """dQ, dK, dV in one pass over the (key tile, query tile) pairs: the
+    preprocess computes Delta and zeroes an fp32 dQ accumulator, the fused
+    kernel adds every dQ partial into it with TMA reduce-adds while it keeps
+    dK/dV per key tile in TMEM, and a cast writes dQ in the operand type.
+    Replaces the reference's _attn_bwd_preprocess + _attn_bwd launches
+    (attention.py:731-783)."""
+    b, hq, nq, d = q.shape
+    hkv, nk = k.shape[1], k.shape[2]
+    stream = _stream_handle(q.device)
+    delta = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
+    dq_acc = torch.empty((b, hq, nq, d), device=q.device, dtype=torch.float32)
+    rc = _abi.entry("fa_bwd_preprocess", o.dtype)(o.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_acc.data_ptr(),
+                                                  b, hq, nq, d, _abi.strides3(o), _abi.strides3(do), stream)
+    _abi.check(rc, "fa_bwd_preprocess")
+    dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+    dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
+    rc = _abi.entry("fa_bwd_fused", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                             lse.data_ptr(), delta.data_ptr(), dq_acc.data_ptr(),
+                                             dk.data_ptr(), dv.data_ptr(), b, hq, hkv, nq, nk, d,
+                                             _abi.strides3(q), _abi.strides3(k), _abi.strides3(v),
+                                             _abi.strides3(do), _abi.strides3(dk), _abi.strides3(dv),
+                                             float(softmax_scale), 1 if causal else 0, 0, 0, 0, stream)
+    _abi.check(rc, "fa_bwd_fused")
+    dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    rc = _abi.entry("fa_bwd_dq_convert", q.dtype)(dq_acc.data_ptr(), dq.data_ptr(), b, hq, nq, d,
+                                                  _abi.strides3(dq), stream)
+    _abi.check(rc, "fa_bwd_dq_convert")
+    return dq, dk, dv
+
+
 class B200Attention(torch.autograd.Function):
     """Autograd bridge for the B200 forward and backward kernels
     (counterpart of ``TritonAttention``, attention.py:673-771).
@@ -197,6 +239,10 @@ class B200Attention(torch.autograd.Function):
     def backward(ctx, grad_output):
         query, key, value, output, lse = ctx.saved_tensors
         grad_output = grad_output.contiguous()
+        if fused_backward_enabled(query.shape[-1]):
+            grad_query, grad_key, grad_value = attention_backward_fused(
+                query, key, value, output, grad_output, lse, ctx.causal, ctx.softmax_scale)
+            return grad_query, grad_key, grad_value, None, None
         delta = attention_delta(output, grad_output)
         grad_query = attention_backward_dq(query, key, value, grad_output, lse, delta,
                                            ctx.causal, ctx.softmax_scale)

@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(256) fa_delta_kernel(const uint16_t* __restric
                                                        long long o_sh, long long o_sn,
                                                        const uint16_t* __restrict__ dO, long long do_sb,
                                                        long long do_sh, long long do_sn, float* __restrict__ delta,
-                                                       int H, int N, long long rows) {
+                                                       float* __restrict__ zero_acc, int H, int N, long long rows) {
   constexpr int TPR = D / 8;  // lanes per row, 8 elements each
   const long long total = rows * TPR;
   const long long nthreads = (long long)gridDim.x * blockDim.x;
@@ -62,6 +62,11 @@ __global__ void __launch_bounds__(256) fa_delta_kernel(const uint16_t* __restric
       const uint16_t* po = o + b * o_sb + h * o_sh + n * o_sn + part * 8;
       const uint16_t* pd = dO + b * do_sb + h * do_sh + n * do_sn + part * 8;
       acc = dot8<DT>(ld_nc_v4(po), ld_nc_v4(pd));
+      if (zero_acc) {  // the fused backward's dQ accumulator, rows x D fp32
+        float4* z = reinterpret_cast<float4*>(zero_acc + row * D + part * 8);
+        z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
 #pragma unroll
     for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
@@ -71,8 +76,8 @@ __global__ void __launch_bounds__(256) fa_delta_kernel(const uint16_t* __restric
 
 template <int DT>
 int launch_bwd_delta_t(const uint16_t* o, long long o_sb, long long o_sh, long long o_sn, const uint16_t* dO,
-                       long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
-                       cudaStream_t stream) {
+                       long long do_sb, long long do_sh, long long do_sn, float* delta, float* zero_acc, int B,
+                       int H, int N, int D, cudaStream_t stream) {
   const int sms = device_sm_count();
   const long long rows = (long long)B * H * N;
   const long long work = rows * (D / 8);
@@ -83,15 +88,15 @@ int launch_bwd_delta_t(const uint16_t* o, long long o_sb, long long o_sh, long l
   switch (D) {
     case 32:
       fa_delta_kernel<32, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                     delta, H, N, rows);
+                                                                     delta, zero_acc, H, N, rows);
       break;
     case 64:
       fa_delta_kernel<64, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                     delta, H, N, rows);
+                                                                     delta, zero_acc, H, N, rows);
       break;
     case 128:
       fa_delta_kernel<128, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                      delta, H, N, rows);
+                                                                      delta, zero_acc, H, N, rows);
       break;
     default:
       return FA_ERR_UNSUPPORTED_HEAD_DIM;
@@ -100,13 +105,58 @@ int launch_bwd_delta_t(const uint16_t* o, long long o_sb, long long o_sh, long l
 }
 
 int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_sn, const void* dO,
-                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
-                     int dtype, cudaStream_t stream) {
+                     long long do_sb, long long do_sh, long long do_sn, float* delta, float* zero_acc, int B, int H,
+                     int N, int D, int dtype, cudaStream_t stream) {
   const uint16_t* o16 = static_cast<const uint16_t*>(o);
   const uint16_t* d16 = static_cast<const uint16_t*>(dO);
-  return dtype == DT_BF16
-             ? launch_bwd_delta_t<DT_BF16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta, B, H, N, D, stream)
-             : launch_bwd_delta_t<DT_F16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta, B, H, N, D, stream);
+  return dtype == DT_BF16 ? launch_bwd_delta_t<DT_BF16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta,
+                                                        zero_acc, B, H, N, D, stream)
+                          : launch_bwd_delta_t<DT_F16>(o16, o_sb, o_sh, o_sn, d16, do_sb, do_sh, do_sn, delta,
+                                                       zero_acc, B, H, N, D, stream);
+}
+
+// dq (operand type, element strides {sb, sh, sn, 1}) <- acc (contiguous
+// [B, H, N, D] fp32), eight elements per thread.
+template <int DT>
+__global__ void __launch_bounds__(256) fa_dq_convert_kernel(const float* __restrict__ acc, uint16_t* __restrict__ dq,
+                                                            long long sb, long long sh, long long sn, int H, int N,
+                                                            int D, long long rows) {
+  const int vec_per_row = D / 8;
+  const long long total = rows * vec_per_row;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long row = idx / vec_per_row;
+    const int part = int(idx % vec_per_row);
+    const int n = int(row % N);
+    const long long bh = row / N;
+    const int h = int(bh % H);
+    const long long b = bh / H;
+    const float4* src = reinterpret_cast<const float4*>(acc + row * D + part * 8);
+    const float4 x = src[0];
+    const float4 y = src[1];
+    uint4 pk;
+    pk.x = pack2<DT>(x.x, x.y);
+    pk.y = pack2<DT>(x.z, x.w);
+    pk.z = pack2<DT>(y.x, y.y);
+    pk.w = pack2<DT>(y.z, y.w);
+    *reinterpret_cast<uint4*>(dq + b * sb + h * sh + n * sn + part * 8) = pk;
+  }
+}
+
+int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
+                      int dtype, cudaStream_t stream) {
+  const long long rows = (long long)B * H * N;
+  const long long work = rows * (D / 8);
+  long long blocks = (work + 255) / 256;
+  const long long cap = (long long)device_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  uint16_t* d16 = static_cast<uint16_t*>(dq);
+  if (dtype == DT_BF16)
+    fa_dq_convert_kernel<DT_BF16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, rows);
+  else
+    fa_dq_convert_kernel<DT_F16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, rows);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 // o_acc (rows x D fp32), lse_acc (rows) <- merge with o_part (fp16 or bf16), lse_part.

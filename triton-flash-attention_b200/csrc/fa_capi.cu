@@ -135,7 +135,43 @@ int delta_impl(const void* o, const void* dO, float* delta, int B, int H, int N,
   if (!o || !dO || !delta || !o_strides || !do_strides) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2)) return FA_ERR_MISALIGNED;
   return launch_bwd_delta(o, o_strides[0], o_strides[1], o_strides[2], dO, do_strides[0], do_strides[1],
-                          do_strides[2], delta, B, H, N, D, dtype, static_cast<cudaStream_t>(stream));
+                          do_strides[2], delta, nullptr, B, H, N, D, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int preprocess_impl(const void* o, const void* dO, float* delta, float* dq_accum, int B, int H, int N, int D,
+                    const int64_t* o_strides, const int64_t* do_strides, void* stream, int dtype) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
+  if (!o || !dO || !delta || !o_strides || !do_strides) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2)) return FA_ERR_MISALIGNED;
+  if (dq_accum && !aligned16(dq_accum)) return FA_ERR_MISALIGNED;
+  return launch_bwd_delta(o, o_strides[0], o_strides[1], o_strides[2], dO, do_strides[0], do_strides[1],
+                          do_strides[2], delta, dq_accum, B, H, N, D, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// 4-D fp32 tensor map over the contiguous (B, H, N, D) dQ accumulator: box
+// {32, 128, 1, 1} with the 128-byte swizzle the fused kernel stages with.
+int make_acc_map(CUtensorMap* map, float* ptr, int B, int H, int N, int D) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return FA_ERR_DRIVER;
+  if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t gstr[3] = {cuuint64_t(D) * 4, cuuint64_t(N) * D * 4, cuuint64_t(H) * N * D * 4};
+  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TENSOR_MAP;
+}
+
+int convert_impl(const float* acc, void* dq, int B, int H, int N, int D, const int64_t* dq_strides, void* stream,
+                 int dtype) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || H <= 0 || N <= 0) return FA_ERR_BAD_SHAPE;
+  if (!acc || !dq || !dq_strides) return FA_ERR_BAD_SHAPE;
+  if (!aligned16(acc) || !out_strides_ok(dq, dq_strides, 2)) return FA_ERR_MISALIGNED;
+  return launch_dq_convert(acc, dq, dq_strides[0], dq_strides[1], dq_strides[2], B, H, N, D, dtype,
+                           static_cast<cudaStream_t>(stream));
 }
 
 int dq_impl(const void* q, const void* k, const void* v, const void* dO, const float* lse, const float* delta,
@@ -205,6 +241,46 @@ int dkdv_impl(const void* q, const void* k, const void* v, const void* dO, const
   a.accumulate_fp32 = accumulate_fp32 ? 1 : 0;
   a.stream = static_cast<cudaStream_t>(stream);
   return launch_bwd_dkdv(a, D);
+}
+
+int fused_impl(const void* q, const void* k, const void* v, const void* dO, const float* lse, const float* delta,
+               float* dq_accum, void* dk, void* dv, int B, int Hq, int Hkv, int Nq, int Nk, int D,
+               const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+               const int64_t* do_strides, const int64_t* dk_strides, const int64_t* dv_strides, float softmax_scale,
+               int causal, int q_offset, int k_offset, int accumulate_fp32, void* stream, int dtype) {
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc) return rc;
+  if (D > 64) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (!q || !k || !v || !dO || !lse || !delta || !dq_accum || !dk || !dv) return FA_ERR_BAD_SHAPE;
+  if (!q_strides || !k_strides || !v_strides || !do_strides || !dk_strides || !dv_strides) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const int eb = accumulate_fp32 ? 4 : 2;
+  if (!out_strides_ok(dk, dk_strides, eb) || !out_strides_ok(dv, dv_strides, eb)) return FA_ERR_MISALIGNED;
+  BwdArgs a;
+  a.dtype = dtype;
+  const int bq = dkdv_cfg::BQ_WIDE;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM, dtype))) return rc;
+  CUtensorMap tmap_dq;
+  if ((rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, D))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
+  a.lse = lse;
+  a.delta = delta;
+  a.dq = dq_accum;
+  a.dq_sb = a.dq_sh = a.dq_sn = 0;
+  a.dk = dk;
+  a.dv = dv;
+  a.dk_sb = dk_strides[0];
+  a.dk_sh = dk_strides[1];
+  a.dk_sn = dk_strides[2];
+  a.dv_sb = dv_strides[0];
+  a.dv_sh = dv_strides[1];
+  a.dv_sn = dv_strides[2];
+  a.accumulate_fp32 = accumulate_fp32 ? 1 : 0;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_bwd_fused(a, tmap_dq, D);
 }
 
 int merge_impl(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, int B, int H, int N, int D,
@@ -294,6 +370,46 @@ extern "C" int fa_merge_partial_bf16(float* o_acc, float* lse_acc, const void* o
   return merge_impl(o_acc, lse_acc, o_part, lse_part, B, H, N, D, stream, DT_BF16);
 }
 
+extern "C" int fa_bwd_preprocess(const void* o, const void* dO, float* delta, float* dq_accum, int B, int H, int N,
+                                 int D, const int64_t* o_strides, const int64_t* do_strides, void* stream) {
+  return preprocess_impl(o, dO, delta, dq_accum, B, H, N, D, o_strides, do_strides, stream, DT_F16);
+}
+extern "C" int fa_bwd_preprocess_bf16(const void* o, const void* dO, float* delta, float* dq_accum, int B, int H,
+                                      int N, int D, const int64_t* o_strides, const int64_t* do_strides,
+                                      void* stream) {
+  return preprocess_impl(o, dO, delta, dq_accum, B, H, N, D, o_strides, do_strides, stream, DT_BF16);
+}
+
+extern "C" int fa_bwd_fused(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                            const float* delta, float* dq_accum, void* dk, void* dv, int B, int Hq, int Hkv, int Nq,
+                            int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, const int64_t* do_strides, const int64_t* dk_strides,
+                            const int64_t* dv_strides, float softmax_scale, int causal, int q_offset, int k_offset,
+                            int accumulate_fp32, void* stream) {
+  return fused_impl(q, k, v, dO, lse, delta, dq_accum, dk, dv, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides,
+                    do_strides, dk_strides, dv_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32,
+                    stream, DT_F16);
+}
+extern "C" int fa_bwd_fused_bf16(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                                 const float* delta, float* dq_accum, void* dk, void* dv, int B, int Hq, int Hkv,
+                                 int Nq, int Nk, int D, const int64_t* q_strides, const int64_t* k_strides,
+                                 const int64_t* v_strides, const int64_t* do_strides, const int64_t* dk_strides,
+                                 const int64_t* dv_strides, float softmax_scale, int causal, int q_offset,
+                                 int k_offset, int accumulate_fp32, void* stream) {
+  return fused_impl(q, k, v, dO, lse, delta, dq_accum, dk, dv, B, Hq, Hkv, Nq, Nk, D, q_strides, k_strides, v_strides,
+                    do_strides, dk_strides, dv_strides, softmax_scale, causal, q_offset, k_offset, accumulate_fp32,
+                    stream, DT_BF16);
+}
+
+extern "C" int fa_bwd_dq_convert(const float* dq_accum, void* dq, int B, int H, int N, int D,
+                                 const int64_t* dq_strides, void* stream) {
+  return convert_impl(dq_accum, dq, B, H, N, D, dq_strides, stream, DT_F16);
+}
+extern "C" int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, int H, int N, int D,
+                                      const int64_t* dq_strides, void* stream) {
+  return convert_impl(dq_accum, dq, B, H, N, D, dq_strides, stream, DT_BF16);
+}
+
 extern "C" int fa_device_status(int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_LAUNCH;
   int v = 0;
@@ -320,4 +436,4 @@ extern "C" const char* fa_status_string(int code) {
   }
 }
 
-extern "C" int fa_version(void) { return 10100; }
+extern "C" int fa_version(void) { return 10200; }

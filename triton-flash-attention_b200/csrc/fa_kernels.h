@@ -57,9 +57,15 @@ inline int device_sm_count() {
 int launch_fwd(const FwdArgs& a, int D);
 int launch_bwd_dq(const BwdArgs& a, int D);
 int launch_bwd_dkdv(const BwdArgs& a, int D);
+// zero_acc: when not null, the contiguous [B, H, N, D] fp32 buffer is zeroed
+// on the way (the fused backward's dQ accumulator).
 int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_sn, const void* dO,
-                     long long do_sb, long long do_sh, long long do_sn, float* delta, int B, int H, int N, int D,
-                     int dtype, cudaStream_t stream);
+                     long long do_sb, long long do_sh, long long do_sn, float* delta, float* zero_acc, int B, int H,
+                     int N, int D, int dtype, cudaStream_t stream);
+// Fused dK/dV + dQ backward (D <= 64); tmap_dq maps the fp32 accumulator.
+int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D);
+int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
+                      int dtype, cudaStream_t stream);
 int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
                          int D, int dtype, cudaStream_t stream);
 
