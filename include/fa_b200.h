@@ -58,7 +58,8 @@ enum {
   FA_ERR_TENSOR_MAP = 5,           /* cuTensorMapEncodeTiled refused a descriptor */
   FA_ERR_DRIVER = 6,               /* the driver entry point could not be resolved */
   FA_ERR_DEVICE_TIMEOUT = 7,       /* a kernel's bounded wait gave up (see fa_device_status) */
-  FA_ERR_NO_DEVICE = 8             /* no sm_100 device is current */
+  FA_ERR_NO_DEVICE = 8,            /* no sm_100 device is current */
+  FA_ERR_SCRATCH_LIMIT = 9         /* the call needs more than FA_NOALLOC_SCRATCH_BYTES */
 };
 
 /* Forward: O = softmax(scale * Q K^T [+ causal mask]) V and the base-2 LSE.
@@ -189,6 +190,36 @@ FA_API int fa_bwd_fused_bf16(const void* q, const void* k, const void* v, const 
                       int accumulate_fp32, void* stream);
 FA_API int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, int H, int N, int D,
                            const int64_t* dq_strides, void* stream);
+
+/* Size of the scratch array fa_bwd_fused_noalloc uses: 32 MiB per device. */
+#define FA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* The whole fused backward (fa_bwd_preprocess + fa_bwd_fused +
+ * fa_bwd_dq_convert; fp16, D = 32 or 64, zero position offsets) with no
+ * scratch from the caller.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory -- engines and plugin hosts that
+ * plan all device memory up front and forbid allocation while running, and
+ * thin FFI bindings that hold tensor pointers but no device allocator.  The
+ * caller passes the inputs (q, k, v, o, dO, lse) and the outputs (dq, dk, dv,
+ * fp16, with their own element strides); Delta and the fp32 dQ accumulator
+ * live in one file-scope __device__ array of FA_NOALLOC_SCRATCH_BYTES that
+ * every device loading the library holds until exit.  A call needs
+ * 4 * (roundup(B*Hq*Nq, 64) + B*Hq*Nq*D) bytes of it; larger calls return
+ * FA_ERR_SCRATCH_LIMIT before touching the GPU.  The library allocates
+ * nothing on this path.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  All calls share the array and it
+ * keeps the last call's contents (each call re-zeroes what must start at
+ * zero), so calls that overlap on the GPU -- on two streams, or from two
+ * host threads on one device -- race and give wrong gradients. */
+FA_API int fa_bwd_fused_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                const float* lse, void* dq, void* dk, void* dv,
+                                int B, int Hq, int Hkv, int Nq, int Nk, int D,
+                                const int64_t* q_strides, const int64_t* k_strides,
+                                const int64_t* v_strides, const int64_t* o_strides,
+                                const int64_t* do_strides, const int64_t* dq_strides,
+                                const int64_t* dk_strides, const int64_t* dv_strides,
+                                float softmax_scale, int causal, void* stream);
 
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the

@@ -24,6 +24,7 @@ FA_ERR_TENSOR_MAP = 5
 FA_ERR_DRIVER = 6
 FA_ERR_DEVICE_TIMEOUT = 7
 FA_ERR_NO_DEVICE = 8
+FA_ERR_SCRATCH_LIMIT = 9
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -47,6 +48,8 @@ SIGNATURES = {
 # the bf16 twins take the same arguments
 SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in list(SIGNATURES)})
 SIGNATURES.update({
+    "fa_bwd_fused_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
+                                  _s, _s, _s, _s, _s, _s, _s, _s, _f, _i, _p]),
     "fa_device_status": (_i, [_i]),
     "fa_status_string": (ctypes.c_char_p, [_i]),
     "fa_version": (_i, []),

@@ -432,6 +432,7 @@ extern "C" const char* fa_status_string(int code) {
     case FA_ERR_DRIVER: return "CUDA driver entry point cuTensorMapEncodeTiled unavailable";
     case FA_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out on the device";
     case FA_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case FA_ERR_SCRATCH_LIMIT: return "the call needs more scratch than FA_NOALLOC_SCRATCH_BYTES (32 MiB)";
     default: return "unknown error";
   }
 }
