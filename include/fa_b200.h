@@ -122,7 +122,7 @@ FA_API int fa_bwd_preprocess(const void* o, const void* dO, float* delta, float*
                       const int64_t* o_strides, const int64_t* do_strides,
                       void* stream);
 
-/* Fused backward, step 2 of 3 (D = 32 or 64): dK, dV exactly as fa_bwd_dkdv
+/* Fused backward, step 2 of 3 (D = 32 or 64): dK, dV as fa_bwd_dkdv
  * and, in the same pass over the (key tile, query tile) pairs, dQ added into
  * dq_accum, the caller's contiguous (B, Hq, Nq, D) fp32 buffer.  Replaces the
  * whole _attn_bwd launch (attention.py:746-783, kernel :383-573), which

@@ -2,13 +2,12 @@
 D = 32, 64) against the separate dQ and dK/dV kernels and the float64
 oracle (GPU only).
 
-dK and dV come from the same per-element arithmetic and the same MMA
-accumulation order as the dK/dV kernel, so they must match it bitwise.  dQ
-differs from the dQ kernel's by rounding: it is summed over key tiles with
-fp32 reduce-adds in schedule order, and its P and dS come from the dK/dV
-side's arithmetic (a different split of the exponentials between MUFU and
-the polynomial), so single elements of P and dS may differ by one ulp of the
-operand type.  The bars: max |a - b| <= 1e-3 + 1e-2 |b| for fp16 and
+dK and dV follow the dK/dV kernel's MMA accumulation order, but the two
+kernels split the exponentials differently between MUFU and the FMA-pipe
+polynomial (each kernel uses its own measured-fastest split), so single
+elements of P and dS may differ by one ulp of the operand type.  dQ is also
+summed over key tiles with fp32 reduce-adds in schedule order.  The bars for
+all three gradients: max |a - b| <= 1e-3 + 1e-2 |b| for fp16 and
 1e-2 + 5e-2 |b| for bf16 (8 mantissa bits); against float64, the fused dQ's
 max-abs error may exceed the dQ kernel's by at most 25% plus 5e-4 (fp16) /
 4e-3 (bf16), and stays within the parity suite's 1e-2 for fp16.
@@ -72,10 +71,9 @@ def test_fused_matches_separate_kernels(case, dtype):
     b, hq, hkv, nq, nk, d, causal = case
     q, k, v, do = _inputs(b, hq, hkv, nq, nk, d, seed=nq + 3 * nk + d, dtype=dtype)
     (fdq, fdk, fdv), (dq, dk, dv) = _both(q, k, v, do, causal)
-    assert torch.equal(fdk, dk)
-    assert torch.equal(fdv, dv)
-    diff = (fdq.float() - dq.float()).abs()
-    assert bool((diff <= _close_bound(dq, dtype)).all()), float(diff.max())
+    for name, a, ref_t in (("dq", fdq, dq), ("dk", fdk, dk), ("dv", fdv, dv)):
+        diff = (a.float() - ref_t.float()).abs()
+        assert bool((diff <= _close_bound(ref_t, dtype)).all()), (name, float(diff.max()))
     if nq * hq <= 4096:
         ref = orc.sdpa_reference(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
                                  causal=causal, scale=d ** -0.5, do=do.float().cpu().numpy())["dq"]
@@ -125,9 +123,9 @@ def test_full_size_c2_against_separate_kernels():
     """The benchmark shape (B4 H16 N4096 D64, causal): fused vs separate."""
     q, k, v, do = _inputs(4, 16, 16, 4096, 4096, 64, seed=1)
     (fdq, fdk, fdv), (dq, dk, dv) = _both(q, k, v, do, True)
-    assert torch.equal(fdk, dk) and torch.equal(fdv, dv)
-    diff = (fdq.float() - dq.float()).abs()
-    assert bool((diff <= 5e-3 + 2e-2 * dq.float().abs()).all()), float(diff.max())
-    rel = float(torch.linalg.vector_norm(fdq.float() - dq.float()) / torch.linalg.vector_norm(dq.float()))
-    assert rel <= 2e-3, rel
+    for name, a, ref_t in (("dq", fdq, dq), ("dk", fdk, dk), ("dv", fdv, dv)):
+        diff = (a.float() - ref_t.float()).abs()
+        assert bool((diff <= 5e-3 + 2e-2 * ref_t.float().abs()).all()), (name, float(diff.max()))
+        rel = float(torch.linalg.vector_norm(a.float() - ref_t.float()) / torch.linalg.vector_norm(ref_t.float()))
+        assert rel <= 2e-3, (name, rel)
     assert fa._abi.device_status() == 0

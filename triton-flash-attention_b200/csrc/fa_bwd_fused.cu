@@ -43,7 +43,7 @@ namespace bfz {
 constexpr int BM = 128;  // keys per tile
 constexpr int BQ = 128;  // query rows per item
 constexpr int NUM_THREADS = 512;
-constexpr int POLY_MASK = 3;  // pairs (i & 7) < 3 use the FMA-pipe exp2
+constexpr int POLY_MASK = 0;  // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2 (none: measured fastest)
 // Registers per thread: launched at 128 (512 threads); warps 0-3 drop to
 // CTRL_REGS and the dQ warpgroup to DQ_REGS, and the two elementwise
 // warpgroups rise to SOFT_REGS (ptxas -v shows no spills at this split).

@@ -13,7 +13,7 @@
 //  * warps 0 and 3 stream K and V tiles of 128 keys through a ring of
 //    shared-memory stages with TMA (128- or 64-byte swizzle);
 //  * warp 1 (one thread) issues tcgen05.mma: S_t = Q_t K^T into TMEM, then
-//    O_t += P_t V with P_t read straight from TMEM (fp16, aliasing S_t);
+//    O_t += P_t V with P_t read straight from TMEM (fp16);
 //  * warps 4-7 and 8-11 are the softmax warpgroups of tile 0 and tile 1, one
 //    thread per query row: they read S from TMEM, run the online softmax in
 //    the base-2 domain (exp2 with scale * log2(e) folded in, as
@@ -22,12 +22,17 @@
 //  * the softmax arithmetic is packed: a 3-input max tree and fma.rn.f32x2
 //    for s * scale*log2(e) - m; the exponentials run on the MUFU unit
 //    (ex2.approx, 16 per clock per SM).  A share of them can go to a
-//    polynomial on the FMA pipe (POLY_MASK); measured, that no longer pays
-//    here: its extra ALU/FMA instructions slow the MMA issue on the same SM
-//    more than they relieve MUFU;
-//  * the two tiles ping-pong: while one warpgroup turns S into P, the tensor
-//    core runs the other tile's GEMMs.
-// TMEM: S_0 cols [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [256+D,256+2D).
+//    polynomial on the FMA pipe (POLY_MASK); measured, that does not pay
+//    here;
+//  * D <= 64 (TMEM to spare): P_t has its own TMEM buffer, so S_t of the
+//    next key tile is issued as soon as the warpgroup has read S_t (not after
+//    P_t V), and the warpgroup finds it ready when it finishes P_t.  The two
+//    warpgroups take turns at their exponentials (tile 0, tile 1, tile 0,
+//    ...), so that one's S reads, row maxima and P writes overlap the other's
+//    exponentials instead of both contending for MUFU and then idling
+//    together.  D = 128: P_t aliases S_t, and S_t(j+1) follows P_t(j) V.
+// TMEM: S_0 cols [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [256+D,256+2D),
+// and for D <= 64 P_0 [256+2D, 320+2D), P_1 [320+2D, 384+2D).
 #include "fa_common.cuh"
 #include "fa_kernels.h"
 
@@ -39,6 +44,7 @@ constexpr int BM = 128;  // query rows per tile
 constexpr int BN = 128;  // keys per K/V tile
 constexpr int QT = 2;    // query tiles per work unit
 constexpr int NUM_THREADS = 384;
+constexpr bool TURNS = true;  // separate-P layout: the softmax warpgroups take turns at their exponentials
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int POLY_MASK = 0;               // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
 // Registers per thread: launched at 168 (384 threads); the control
@@ -64,8 +70,8 @@ struct Cfg {
   static constexpr int OW = D;  // O columns in TMEM
   static constexpr int OFF_BAR = OFF_V + NST * KV_TILE_BYTES;
   // barriers: q_full[QB], q_empty[QB], k_full[NST], k_empty[NST], v_full[NST], v_empty[NST],
-  //           s_full[QT], p_ready[QT], o_full[QT], o_empty[QT], mma_done
-  static constexpr int NUM_BARS = 2 * QB + 4 * NST + 4 * QT + 1;
+  //           s_full[QT], p_ready[QT], o_full[QT], o_empty[QT], s_read[QT], pv_done[QT], turn[QT], mma_done
+  static constexpr int NUM_BARS = 2 * QB + 4 * NST + 7 * QT + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   // + alignment slack; at least 116 KB so that one CTA (and its 512 TMEM
@@ -76,6 +82,14 @@ struct Cfg {
   static constexpr int O_COL0 = QT * BN;
   static constexpr int TMEM_COLS = 512;
   static_assert(O_COL0 + QT * OW <= TMEM_COLS, "TMEM budget");
+  // D <= 64 leaves TMEM room for a P buffer per query tile (BN/2 columns of
+  // packed fp16 pairs) beside S: S of the next key tile is then issued as
+  // soon as the softmax warpgroup has read S, instead of after P V, so the
+  // warpgroup finds its next S ready when it finishes P.  At D = 128, P
+  // aliases S.
+  static constexpr bool SEP_P = D <= 64;
+  static constexpr int P_COL0 = O_COL0 + QT * OW;
+  static_assert(!SEP_P || P_COL0 + QT * BN / 2 <= TMEM_COLS, "TMEM budget (separate P)");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -133,7 +147,14 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   uint64_t* p_ready = s_full + QT;
   uint64_t* o_full = p_ready + QT;
   uint64_t* o_empty = o_full + QT;
-  uint64_t* mma_done = o_empty + QT;
+  // per query tile t (separate-P layout): s_read completes once the
+  // warpgroup has read S_t into registers, pv_done once P_t V has run
+  uint64_t* s_read = o_empty + QT;
+  uint64_t* pv_done = s_read + QT;
+  // turn[t]: the other softmax warpgroup finished its exponentials and
+  // hands the MUFU unit to tile t's (one phase per hand-off)
+  uint64_t* turn = pv_done + QT;
+  uint64_t* mma_done = turn + QT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
   volatile CtaCtl* ctl = ctl_w;
@@ -159,7 +180,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       mbar_init(p_ready + t, 128);
       mbar_init(o_full + t, 1);
       mbar_init(o_empty + t, 128);
+      mbar_init(s_read + t, 128);
+      mbar_init(pv_done + t, 1);
     }
+    for (int t = 0; t < QT; ++t) mbar_init(turn + t, 128);
     mbar_init(mma_done, 1);
     ctl_w->abort = 0;
     ctl_w->status = shp.status;
@@ -263,7 +287,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             // the D columns of V span NBOX boxes BN*SW bytes apart (LBO)
             const SDesc vd = desc_mn_base<D, BN>(v_s + (g % C::NST) * C::KV_TILE_BYTES);
             const uint32_t dst = tmem + C::O_COL0 + t * C::OW;
-            const uint32_t pa = tmem + C::S_COL0 + t * BN;
+            const uint32_t pa = C::SEP_P ? tmem + C::P_COL0 + t * (BN / 2) : tmem + C::S_COL0 + t * BN;
             umma_ts(dst, pa, sdesc_at(vd, 0), IDESC_PV, acc ? 1u : 0u);
   #pragma unroll
             for (int ks = 1; ks < BN / 16; ++ks)
@@ -274,6 +298,37 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           for (int t = 0; t < QT; ++t)
             if (w.n_kv[t] > 0) issue_s(t, gj);
           umma_commit(k_empty + gj % C::NST);
+          if constexpr (C::SEP_P) {
+            // S_t(j+1) once the warpgroup read S_t(j); P_t(j) V once it wrote P_t(j)
+            for (int j = 0; j < w.n_max && ok; ++j) {
+              const int g = gj + j;
+              const int s = g % C::NST;
+              const bool more = j + 1 < w.n_max;
+              if (more) {
+                if (!mbar_wait(k_full + (g + 1) % C::NST, uint32_t((g + 1) / C::NST) & 1, ctl, 13)) { ok = false; break; }
+                for (int t = 0; t < QT && ok; ++t) {
+                  if (j + 1 >= w.n_kv[t]) continue;
+                  if (!mbar_wait(s_read + t, uint32_t(cnt[t]) & 1, ctl, 17)) { ok = false; break; }
+                  tc_fence_after();
+                  issue_s(t, g + 1);
+                }
+                if (!ok) break;
+                umma_commit(k_empty + (g + 1) % C::NST);
+              }
+              if (!mbar_wait(v_full + s, uint32_t(g / C::NST) & 1, ctl, 12)) { ok = false; break; }
+              for (int t = 0; t < QT && ok; ++t) {
+                if (j >= w.n_kv[t]) continue;
+                if (!mbar_wait(p_ready + t, uint32_t(cnt[t]) & 1, ctl, 14)) { ok = false; break; }
+                if (j == 0 && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(t, g, j > 0);
+                umma_commit(pv_done + t);
+                ++cnt[t];
+              }
+              if (!ok) break;
+              umma_commit(v_empty + s);
+            }
+          } else
           for (int j = 0; j < w.n_max && ok; ++j) {
             const int g = gj + j;
             const int s = g % C::NST;
@@ -321,9 +376,25 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     const int row_local = wq * 32 + lane;
     const uint32_t tS = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::S_COL0 + t * BN));
     const uint32_t tO = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::O_COL0 + t * C::OW));
+    const uint32_t tP = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(C::SEP_P ? C::P_COL0 + t * (BN / 2) : 0));
     const float c2 = shp.scale_log2;
     const uint64_t c2x2 = f2pack(c2, c2);
     int cnt = 0, oc = 0;  // phases of s_full / o_full of this tile
+    // Turns: the exponential phases of the two warpgroups strictly
+    // alternate, tile 0 first, (0, j), (1, j) for each key tile j of each
+    // unit; a warpgroup with fewer key tiles in a unit takes empty turns.
+    // While one warpgroup has the MUFU unit, the other reads its next S,
+    // finds the row maxima and writes P, which keeps the MUFU unit busy
+    // instead of both warpgroups contending for it and then idling together.
+    int pc = 0;  // turns taken by this warpgroup
+    auto take_turn = [&]() -> bool {
+      if (t == 0 && pc == 0) return true;
+      return mbar_wait_warp(turn + t, uint32_t(t == 0 ? pc - 1 : pc) & 1, ctl, 26 + t);
+    };
+    auto pass_turn = [&]() {
+      mbar_arrive(turn + (1 - t));
+      ++pc;
+    };
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int ui = snake_unit(cta, k, n_cta, n_units);
@@ -345,6 +416,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         float s[BN];
         tmem_ld64(tS, *reinterpret_cast<float(*)[64]>(&s[0]));
         tmem_ld64(tS + 64, *reinterpret_cast<float(*)[64]>(&s[64]));
+        if constexpr (C::SEP_P) {
+          // S_t is in registers: the MMA may overwrite it with the next key tile's
+          tc_fence_before();
+          mbar_arrive(s_read + t);
+        }
         const int lim_j = lim - j * BN;  // last visible local column in this tile
         if (lim_j < BN - 1) {
 #pragma unroll
@@ -369,8 +445,13 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         }
         const float alpha = rescale ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 on the first tile
         const float base = m_new == -INFINITY ? 0.f : m_new;
-        const uint64_t nb2 = f2pack(-base, -base);
+        uint64_t nb2 = f2pack(-base, -base);
+        if constexpr (C::SEP_P && TURNS) {
+          if (!take_turn()) { ok = false; break; }
+          asm volatile("" : "+l"(nb2));  // the exponentials below depend on the turn
+        }
         uint64_t sum2[4] = {0, 0, 0, 0};
+        uint32_t pk[C::SEP_P ? BN / 2 : 1];  // P_t, packed, until the previous P_t V has run
 #pragma unroll
         for (int cc = 0; cc < BN / 32; ++cc) {
           uint32_t packed[16];
@@ -383,7 +464,23 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             packed[i] = pack2_f2<DT>(e);
             sum2[i & 3] = fadd2(sum2[i & 3], e);
           }
-          tmem_st16(tS + cc * 16, packed);
+          if constexpr (C::SEP_P) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[cc * 16 + i] = packed[i];
+          } else {
+            tmem_st16(tS + cc * 16, packed);
+          }
+        }
+        if constexpr (C::SEP_P && TURNS) {
+          // the turn ends once every exponential of this key tile is summed
+          const uint64_t q01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+          asm volatile("" ::"l"(q01));
+          pass_turn();
+        }
+        if constexpr (C::SEP_P) {
+          // P_t(j-1) V has read the P buffer and finished accumulating O_t
+          if (j > 0 && !mbar_wait_warp(pv_done + t, uint32_t(cnt - 1) & 1, ctl, 24 + t)) { ok = false; break; }
+          tc_fence_after();
         }
         {
           float s0, s1, s2, s3, s4, s5, s6, s7;
@@ -394,6 +491,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)));
         }
         m = m_new;
+        if constexpr (C::SEP_P) {
+#pragma unroll
+          for (int cc = 0; cc < BN / 32; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc * 16]));
+        }
         if (j > 0 && __any_sync(0xffffffffu, rescale)) {
           // O *= alpha
 #pragma unroll 1
@@ -414,6 +515,14 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         ++cnt;
       }
       if (!ok) break;
+      if constexpr (C::SEP_P && TURNS) {
+        // empty turns for the key tiles the other query tile has and this one lacks
+        for (int j = nt; j < w.n_max; ++j) {
+          if (!take_turn()) { ok = false; break; }
+          pass_turn();
+        }
+        if (!ok) break;
+      }
       // ---- epilogue: O / l -> fp16, lse2 = m + log2(l) ----
       if (nt > 0) {
         if (!mbar_wait_warp(o_full + t, uint32_t(oc) & 1, ctl, 22 + t)) { ok = false; break; }
