@@ -34,6 +34,9 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
   configuration, with the reference's Triton kernel (``backend="triton"``,
   from baseline/_ref) timed beside it when installed.  Informational; the
   metric line is the default workload.
+* ``--workload varlen``: a packed batch of 16 causal sequences of ragged
+  lengths through ``scaled_dot_product_attention_varlen``, beside the same
+  sequences padded and run dense.  Informational.
 """
 
 from __future__ import annotations
@@ -634,6 +637,80 @@ def run_sweep(args) -> None:
         torch.cuda.empty_cache()
 
 
+VARLEN_SEQS, VARLEN_H, VARLEN_D, VARLEN_MAX = 16, 16, 64, 4096
+
+
+def run_varlen(args) -> None:
+    """Packed variable-length batch (no counterpart in the reference): 16
+    causal sequences of seeded random lengths in [256, 4096] (H16, D64,
+    fp16), forward and forward+backward through
+    ``scaled_dot_product_attention_varlen``, beside the same sequences padded
+    to the longest and run dense.  FLOPs count each sequence's own pairs
+    (the reference's convention per sequence); informational, one JSON line."""
+    import numpy as np
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(2024)
+    lens = rng.integers(256, VARLEN_MAX + 1, size=VARLEN_SEQS)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    total, mx = int(lens.sum()), int(lens.max())
+    g = torch.Generator(device=dev).manual_seed(3)
+    q, k, v, do = (torch.randn(total, VARLEN_H, VARLEN_D, device=dev, dtype=torch.float16, generator=g)
+                   for _ in range(4))
+    fl_f = sum(fa.attention_flops(batch=1, query_heads=VARLEN_H, sequence=int(n), head_dim=VARLEN_D, causal=True,
+                                  mode="forward") for n in lens)
+    fl_fb = sum(fa.attention_flops(batch=1, query_heads=VARLEN_H, sequence=int(n), head_dim=VARLEN_D, causal=True,
+                                   mode="forward-backward") for n in lens)
+    steps = max(1, min(args.steps, 20))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    qc, kc, vc = (t.clone().requires_grad_() for t in (q, k, v))
+    with torch.no_grad():
+        ms_f = timed(lambda: fa.scaled_dot_product_attention_varlen(qc, kc, vc, cu, cu, mx, mx, is_causal=True))
+
+    def fwd_bwd():
+        fa.scaled_dot_product_attention_varlen(qc, kc, vc, cu, cu, mx, mx, is_causal=True).backward(do)
+
+    ms_fb = timed(fwd_bwd)
+    # the same sequences padded to the longest, dense (B, H, N, D)
+    pad = lambda t: torch.stack([torch.nn.functional.pad(t[int(a):int(b)], (0, 0, 0, 0, 0, mx - int(b - a)))
+                                 for a, b in zip(cu[:-1].tolist(), cu[1:].tolist())]).transpose(1, 2).contiguous()
+    qp, kp, vp, dop = (pad(t) for t in (q, k, v, do))
+    qp, kp, vp = (t.requires_grad_() for t in (qp, kp, vp))
+    with torch.no_grad():
+        ms_pf = timed(lambda: fa.scaled_dot_product_attention(qp, kp, vp, is_causal=True))
+
+    def fwd_bwd_pad():
+        fa.scaled_dot_product_attention(qp, kp, vp, is_causal=True).backward(dop)
+
+    ms_pfb = timed(fwd_bwd_pad)
+    print(json.dumps({
+        "workload": "varlen", "sequences": VARLEN_SEQS, "heads": VARLEN_H, "head_dim": VARLEN_D, "causal": True,
+        "dtype": "fp16", "total_tokens": total, "max_seqlen": mx, "unit": "TFLOP/s", "steps": steps,
+        "data": "synthetic: seeded N(0,1), seeded random lengths in [256, 4096]",
+        "varlen": {"fwd_ms": round(ms_f, 4), "fwd_tflops": round(fl_f / ms_f / 1e9, 1),
+                   "fwd_bwd_ms": round(ms_fb, 4), "fwd_bwd_tflops": round(fl_fb / ms_fb / 1e9, 1)},
+        "padded_dense": {"fwd_ms": round(ms_pf, 4), "fwd_bwd_ms": round(ms_pfb, 4),
+                         "note": "same sequences padded to max_seqlen; TFLOP/s counts only the real pairs",
+                         "fwd_tflops": round(fl_f / ms_pf / 1e9, 1), "fwd_bwd_tflops": round(fl_fb / ms_pfb / 1e9, 1)},
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -643,9 +720,10 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--deterministic", action="store_true",
                     help="time the bitwise-reproducible backward (separate dQ and dK/dV kernels)")
-    ap.add_argument("--workload", choices=["c2", "ring", "sweep"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen"], default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
-                         "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel")
+                         "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel; "
+                         "varlen: a packed batch of ragged sequences beside its padded dense equivalent")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -658,6 +736,8 @@ def main() -> None:
         run_ring(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "varlen":
+        run_varlen(args)
     else:
         run_ours(args)
 

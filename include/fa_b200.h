@@ -191,6 +191,43 @@ FA_API int fa_bwd_fused_bf16(const void* q, const void* k, const void* v, const 
 FA_API int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, int H, int N, int D,
                            const int64_t* dq_strides, void* stream);
 
+/* Packed variable-length batches (varlen).  No counterpart in the reference,
+ * which takes (B, H, N, D) tensors of one length only (attention.py:584-626);
+ * this is the layout serving and packed-sequence training use.  q, o, dO, dq
+ * are contiguous (total_q, Hq, D) and k, v, dk, dv contiguous
+ * (total_k, Hkv, D) in the operand type; cu_seqlens_q / cu_seqlens_k are
+ * device int32 arrays of B + 1 prefix sums (cu[0] = 0, cu[B] = total):
+ * batch b owns query rows [cu_q[b], cu_q[b+1]) and key rows
+ * [cu_k[b], cu_k[b+1]).  max_seqlen_q / max_seqlen_k must be at least the
+ * longest batch's lengths (they size the launch).  lse and delta are
+ * (Hq, total_q) fp32.  Causal masking is per batch and top-left aligned
+ * (query i of a batch sees its keys j <= i), as in the dense calls.  A
+ * batch may be empty; a query row with no visible key gets o = 0 and
+ * lse = -inf.  total_q and total_k must be positive. */
+FA_API int fa_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
+                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                  int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                  float softmax_scale, int causal, void* stream);
+/* The whole varlen backward: delta (caller's (Hq, total_q) fp32 buffer) and
+ * dq, dk, dv.  D <= 64 with deterministic == 0 runs the fused pass and needs
+ * dq_accum, a caller's (Hq, total_q, D) fp32 scratch buffer (zeroed here);
+ * otherwise the separate dQ and dK/dV kernels run (bitwise reproducible) and
+ * dq_accum may be NULL. */
+FA_API int fa_bwd_varlen(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                  const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                  int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                  float softmax_scale, int causal, int deterministic, void* stream);
+FA_API int fa_fwd_varlen_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                       const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                       int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                       float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                       const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                       const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                       int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                       float softmax_scale, int causal, int deterministic, void* stream);
+
 /* Size of the scratch array fa_bwd_fused_noalloc uses: 32 MiB per device. */
 #define FA_NOALLOC_SCRATCH_BYTES (32u << 20)
 
@@ -230,7 +267,7 @@ FA_API int fa_device_status(int reset);
 FA_API const char* fa_status_string(int code);
 
 /* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
- * 1.2.0 the fused backward). */
+ * 1.2.0 the fused backward, 1.3.0 packed variable-length batches). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

@@ -109,6 +109,40 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
     return out
 
 
+def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | None = None, do=None):
+    """Packed variable-length attention in float64: ``q`` (total_q, Hq, D),
+    ``k``/``v`` (total_k, Hkv, D), prefix sums ``cu_q``/``cu_k``; each
+    sequence is dense attention over its own rows (``sdpa_reference``, causal
+    top-left aligned per sequence).  Returns packed ``o``, ``dq``, ``dk``,
+    ``dv`` and ``lse2`` laid out (Hq, total_q).  No counterpart in the
+    reference, which has no packed layout; this is its dense math applied per
+    sequence."""
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    total_q, hq, d = q.shape
+    if scale is None:
+        scale = d ** -0.5
+    out = {"o": np.zeros_like(q), "lse2": np.full((hq, total_q), -np.inf)}
+    if do is not None:
+        do = np.asarray(do, dtype=np.float64)
+        out.update(dq=np.zeros_like(q), dk=np.zeros_like(k), dv=np.zeros_like(v))
+    for b in range(len(cu_q) - 1):
+        q0, q1, k0, k1 = int(cu_q[b]), int(cu_q[b + 1]), int(cu_k[b]), int(cu_k[b + 1])
+        if q1 == q0 or k1 == k0:
+            continue  # no query rows, or no keys: o = 0, lse = -inf, no gradient
+        to4 = lambda x: x.transpose(1, 0, 2)[None]  # (n, H, D) -> (1, H, n, D)
+        r = sdpa_reference(to4(q[q0:q1]), to4(k[k0:k1]), to4(v[k0:k1]), causal=causal, scale=scale,
+                           do=None if do is None else to4(do[q0:q1]))
+        out["o"][q0:q1] = r["o"][0].transpose(1, 0, 2)
+        out["lse2"][:, q0:q1] = r["lse2"][0]
+        if do is not None:
+            out["dq"][q0:q1] = r["dq"][0].transpose(1, 0, 2)
+            out["dk"][k0:k1] = r["dk"][0].transpose(1, 0, 2)
+            out["dv"][k0:k1] = r["dv"][0].transpose(1, 0, 2)
+    return out
+
+
 def _f16(x):
     return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
 

@@ -22,9 +22,16 @@ from .attention import (
     scaled_dot_product_attention,
 )
 from .flops import attention_flops, delta_bytes, memory_model
+from .varlen import (
+    B200VarlenAttention,
+    scaled_dot_product_attention_varlen,
+    varlen_attention_backward,
+    varlen_attention_forward,
+)
 
 __all__ = [
     "B200Attention",
+    "B200VarlenAttention",
     "DispatchDecision",
     "SUPPORTED_HEAD_DIMS",
     "FUSED_BWD_HEAD_DIMS",
@@ -40,4 +47,7 @@ __all__ = [
     "fused_backward_enabled",
     "memory_model",
     "scaled_dot_product_attention",
+    "scaled_dot_product_attention_varlen",
+    "varlen_attention_backward",
+    "varlen_attention_forward",
 ]

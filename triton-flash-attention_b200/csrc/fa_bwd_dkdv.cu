@@ -74,7 +74,9 @@ struct Cfg {
 // (query head of the group x query tile) that see them.
 struct Tile {
   int kv0, b, kvh, i_start, per_head, n_items;
+  Seq sq;
 };
+template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   const int BHkv = shp.B * shp.Hkv;
   const int kv_tile = t / BHkv;
@@ -83,7 +85,8 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.b = bhk / shp.Hkv;
   w.kvh = bhk % shp.Hkv;
   w.kv0 = kv_tile * BM;
-  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  w.sq = seq_of_v<VL>(shp, w.b);
+  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
   int i_start = 0;
   if (shp.causal) {
     // first query tile holding a row at or after this tile's first key
@@ -98,6 +101,7 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 
 // Walks the items of a CTA's non-empty tiles in issue order.
+template <bool VL>
 struct ItemCursor {
   int k, it, pad;
   Tile w;
@@ -106,7 +110,7 @@ struct ItemCursor {
     for (;; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) return false;
-      w = tile_of(shp, t);
+      w = tile_of<VL>(shp, t);
       if (w.n_items > 0) {
         it = 0;
         return true;
@@ -122,7 +126,7 @@ struct ItemCursor {
 
 }  // namespace bkv
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       // that see no key, get lse2 = +inf so that their P is 0.
       constexpr int PF = 2;
       float lv[PF + 1][2], dvv[PF + 1][2];
-      ItemCursor ahead{0, 0, 0, {}};
+      ItemCursor<VL> ahead{0, 0, 0, {}};
       bool ahead_ok = is_q && ahead.seek(shp, cta, n_cta, n_tiles);
       auto fetch = [&](float (&l)[2], float (&d)[2]) {
 #pragma unroll
@@ -224,11 +228,11 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         if (!ahead_ok) return;
         const int h = ahead.w.kvh * group + ahead.it / ahead.w.per_head;
         const int q0 = (ahead.w.i_start + ahead.it % ahead.w.per_head) * BQ;
-        const long long rowbase = ((long long)ahead.w.b * shp.Hq + h) * shp.Nq;
+        const long long rowbase = row_stat_index_v<VL>(shp, ahead.w.sq, ahead.w.b, h, 0);
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int qi = q0 + lane * 2 + e;
-          if (qi < shp.Nq) {
+          if (qi < ahead.w.sq.nq) {
             l[e] = lse[rowbase + qi];
             d[e] = delta[rowbase + qi];
           }
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       for (int k = 0; ok; ++k) {
         const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
-        const Tile w = tile_of(shp, t);
+        const Tile w = tile_of<VL>(shp, t);
         if (w.n_items == 0) continue;
         const int kb = tcn & 1;
         if (tcn >= 2 && !mbar_wait_warp(kv_empty + kb, uint32_t((tcn >> 1) - 1) & 1, ctl, 60)) { ok = false; break; }
@@ -250,7 +254,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
           mbar_arrive_expect_tx(kv_full + kb, C::KV_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
             tma_load_4d(smem + kv_off + kb * C::KV_TILE_BYTES + bx * BM * G::SW, tmap_kv, kv_full + kb, bx * G::BOX,
-                        w.kv0, w.kvh, w.b);
+                        w.sq.k0 + w.kv0, w.kvh, w.sq.tb);
         }
         ++tcn;
         for (int it = 0; it < w.n_items; ++it) {
@@ -263,8 +267,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
           if (lane == 0) {
             mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
             for (int bx = 0; bx < G::NBOX; ++bx)
-              tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
-                          w.b);
+              tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX,
+                          w.sq.q0 + q0, h, w.sq.tb);
           }
           if (is_q) {
 #pragma unroll
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int t = snake_unit(cta, k, n_cta, n_tiles);
           if (t >= n_tiles) break;
-          const int n = tile_of(shp, t).n_items;
+          const int n = tile_of<VL>(shp, t).n_items;
           if (n == 0) continue;
           const int kb = tcn & 1;
           if (!mbar_wait(kv_full + kb, uint32_t(tcn >> 1) & 1, ctl, 70)) { ok = false; break; }
@@ -391,10 +395,12 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
-      const Tile wt = tile_of(shp, t);
+      const Tile wt = tile_of<VL>(shp, t);
       // causal: key row rl sees query column c of an item at rows q0.. iff
       // c >= cmin_base - q0
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
+      // key rows past the batch's keys (the next batch's, when packed) see no query
+      const bool key_out = VL && wt.kv0 + rl >= wt.sq.nk;
       // this warpgroup's items of the tile: global parity w
       for (int it = ((gi & 1) == w ? 0 : 1); it < wt.n_items; it += 2) {
         const int g = gi + it;
@@ -407,8 +413,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         tmem_ld64(tS, st);
         tmem_ld64(tS + 64, dpt);
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
-        int cmin = 0;
-        if (shp.causal) {
+        int cmin = key_out ? BQ : 0;
+        if (shp.causal && !key_out) {
           const long long x = cmin_base - q0;
           cmin = x <= 0 ? 0 : (x > BQ ? BQ : int(x));
         }
@@ -449,12 +455,13 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         tc_fence_after();
       }
       const int kr = wt.kv0 + rl;
-      const bool row_ok = kr < shp.Nk;
+      const bool row_ok = kr < wt.sq.nk;
       const float sc = w == 0 ? 1.f : shp.scale;
       const uint32_t tAcc = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(w == 0 ? C::DV_COL : C::DK_COL));
       void* out = w == 0 ? dv_out : dk_out;
-      const long long off0 = w == 0 ? ((long long)wt.b * dv_sb + (long long)wt.kvh * dv_sh + (long long)kr * dv_sn)
-                                    : ((long long)wt.b * dk_sb + (long long)wt.kvh * dk_sh + (long long)kr * dk_sn);
+      const long long krow = (long long)wt.sq.k0 + kr;
+      const long long off0 = w == 0 ? ((long long)wt.sq.tb * dv_sb + (long long)wt.kvh * dv_sh + krow * dv_sn)
+                                    : ((long long)wt.sq.tb * dk_sb + (long long)wt.kvh * dk_sh + krow * dk_sn);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float gv[32];
@@ -569,7 +576,9 @@ struct Cfg {
 // head of the group x 128-row query tile) that see them.
 struct Tile {
   int kv0, b, kvh, i_start, per_head, n_items;
+  Seq sq;
 };
+template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   const int BHkv = shp.B * shp.Hkv;
   const int kv_tile = t / BHkv;
@@ -578,7 +587,8 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.b = bhk / shp.Hkv;
   w.kvh = bhk % shp.Hkv;
   w.kv0 = kv_tile * BM;
-  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  w.sq = seq_of_v<VL>(shp, w.b);
+  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
   int i_start = 0;
   if (shp.causal) {
     const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
@@ -592,7 +602,7 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 }  // namespace bkvw
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     fa_bwd_dkdv_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                             const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -689,7 +699,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     constexpr int PF = 2;
     float lv[PF + 1][4], dv[PF + 1][4];
     int pf_k = 0, pf_it = 0;  // prefetch cursor: tile round k, item it
-    Tile pf_w = tile_of(shp, snake_unit(cta, 0, n_cta, n_tiles) < n_tiles ? snake_unit(cta, 0, n_cta, n_tiles) : 0);
+    Tile pf_w = tile_of<VL>(shp, snake_unit(cta, 0, n_cta, n_tiles) < n_tiles ? snake_unit(cta, 0, n_cta, n_tiles) : 0);
     bool pf_live = snake_unit(cta, 0, n_cta, n_tiles) < n_tiles;
     auto pf_skip_empty = [&]() {
       while (pf_live && pf_it >= pf_w.n_items) {
@@ -697,7 +707,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         ++pf_k;
         const int t = snake_unit(cta, pf_k, n_cta, n_tiles);
         pf_live = t < n_tiles;
-        if (pf_live) pf_w = tile_of(shp, t);
+        if (pf_live) pf_w = tile_of<VL>(shp, t);
       }
     };
     auto fetch = [&](float (&l)[4], float (&d)[4]) {
@@ -710,11 +720,11 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
       if (!pf_live || !is_q) return;
       const int h = pf_w.kvh * group + pf_it / pf_w.per_head;
       const int q0 = (pf_w.i_start + pf_it % pf_w.per_head) * BQ;
-      const long long rowbase = ((long long)pf_w.b * shp.Hq + h) * shp.Nq;
+      const long long rowbase = row_stat_index_v<VL>(shp, pf_w.sq, pf_w.b, h, 0);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int qi = q0 + e * 32 + lane;
-        if (qi < shp.Nq) {
+        if (qi < pf_w.sq.nq) {
           l[e] = lse[rowbase + qi];
           d[e] = delta[rowbase + qi];
         }
@@ -728,7 +738,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
-      const Tile w = tile_of(shp, t);
+      const Tile w = tile_of<VL>(shp, t);
       if (w.n_items == 0) continue;
       const int kb = tcn & 1;
       if (tcn >= 2 && !mbar_wait_warp(kv_empty + kb, uint32_t((tcn >> 1) - 1) & 1, ctl, 160)) { ok = false; break; }
@@ -736,7 +746,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         mbar_arrive_expect_tx(kv_full + kb, C::KV_TILE_BYTES);
         for (int bx = 0; bx < G::NBOX; ++bx)
           tma_load_4d(smem + kv_off + kb * C::KV_TILE_BYTES + bx * BM * G::SW, tmap_kv, kv_full + kb, bx * G::BOX,
-                      w.kv0, w.kvh, w.b);
+                      w.sq.k0 + w.kv0, w.kvh, w.sq.tb);
       }
       ++tcn;
       for (int it = 0; it < w.n_items; ++it) {
@@ -749,8 +759,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         if (lane == 0) {
           mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
-            tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX, q0, h,
-                        w.b);
+            tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX,
+                        w.sq.q0 + q0, h, w.sq.tb);
         }
         if (is_q) {
 #pragma unroll
@@ -816,7 +826,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
       for (int k = 0; ok; ++k) {
         const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
-        const int n = tile_of(shp, t).n_items;
+        const int n = tile_of<VL>(shp, t).n_items;
         if (n == 0) continue;
         const int kb = tcn & 1;
         if (!mbar_wait(kv_full + kb, uint32_t(tcn >> 1) & 1, ctl, 170)) { ok = false; break; }
@@ -886,8 +896,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
-      const Tile wt = tile_of(shp, t);
+      const Tile wt = tile_of<VL>(shp, t);
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
+      // key rows past the batch's keys (the next batch's, when packed) see no query
+      const bool key_out = VL && wt.kv0 + rl >= wt.sq.nk;
       for (int it = 0; it < wt.n_items && ok; ++it) {
         const int g = gi + it;
         const int s = g % C::NST;
@@ -902,13 +914,14 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * hh);
             float st[64];
             tmem_ld64(tS, st);
-            if (shp.causal) {
+            int cmin = key_out ? 64 : 0;
+            if (shp.causal && !key_out) {
               const long long x = cmin_base - q0 - 64 * hh;
-              const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
-              if (cmin > 0) {
+              cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+            }
+            if (cmin > 0) {
 #pragma unroll
-                for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
-              }
+              for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];
@@ -967,12 +980,13 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         tc_fence_after();
       }
       const int kr = wt.kv0 + rl;
-      const bool row_ok = kr < shp.Nk;
+      const bool row_ok = kr < wt.sq.nk;
       const float sc = w == 0 ? 1.f : shp.scale;
       const uint32_t tAcc = lane_base + uint32_t(w == 0 ? C::DV_COL : C::DK_COL);
       void* out = w == 0 ? dv_out : dk_out;
-      const long long off0 = w == 0 ? ((long long)wt.b * dv_sb + (long long)wt.kvh * dv_sh + (long long)kr * dv_sn)
-                                    : ((long long)wt.b * dk_sb + (long long)wt.kvh * dk_sh + (long long)kr * dk_sn);
+      const long long krow = (long long)wt.sq.k0 + kr;
+      const long long off0 = w == 0 ? ((long long)wt.sq.tb * dv_sb + (long long)wt.kvh * dv_sh + krow * dv_sn)
+                                    : ((long long)wt.sq.tb * dk_sb + (long long)wt.kvh * dk_sh + krow * dk_sn);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float gv[32];
@@ -1024,10 +1038,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   using C = bkvw::Cfg<D>;
-  auto kern = fa_bwd_dkdv_wide_kernel<D, DT>;
+  auto kern = fa_bwd_dkdv_wide_kernel<D, DT, VL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkvw::BM - 1) / bkvw::BM;
@@ -1040,10 +1054,10 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
-  auto kern = fa_bwd_dkdv_kernel<D, DT>;
+  auto kern = fa_bwd_dkdv_kernel<D, DT, VL>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -1065,11 +1079,22 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+// Dense and packed (varlen) layouts are separate instantiations, so the
+// dense kernels carry no per-batch offset arithmetic.
+template <int D, int DT>
+int launch_bwd_dkdv_l(const BwdArgs& a) {
+  if constexpr (D == 128) {
+    return a.shape.cu_q ? launch_bwd_dkdv_t<D, DT, true>(a) : launch_bwd_dkdv_t<D, DT, false>(a);
+  } else {
+    return a.shape.cu_q ? launch_bwd_dkdv_wide_t<D, DT, true>(a) : launch_bwd_dkdv_wide_t<D, DT, false>(a);
+  }
+}
+
 int launch_bwd_dkdv(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return a.dtype == DT_BF16 ? launch_bwd_dkdv_wide_t<32, DT_BF16>(a) : launch_bwd_dkdv_wide_t<32, DT_F16>(a);
-    case 64: return a.dtype == DT_BF16 ? launch_bwd_dkdv_wide_t<64, DT_BF16>(a) : launch_bwd_dkdv_wide_t<64, DT_F16>(a);
-    case 128: return a.dtype == DT_BF16 ? launch_bwd_dkdv_t<128, DT_BF16>(a) : launch_bwd_dkdv_t<128, DT_F16>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_bwd_dkdv_l<32, DT_BF16>(a) : launch_bwd_dkdv_l<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_bwd_dkdv_l<64, DT_BF16>(a) : launch_bwd_dkdv_l<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_bwd_dkdv_l<128, DT_BF16>(a) : launch_bwd_dkdv_l<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

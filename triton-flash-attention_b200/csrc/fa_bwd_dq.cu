@@ -68,6 +68,7 @@ struct Cfg {
 // a causal mask).
 struct Tile {
   int b, h, kvh, row0, n_kv;
+  Seq sq;
 };
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   const int BH = shp.B * shp.Hq;
@@ -78,7 +79,8 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.h = bh % shp.Hq;
   w.kvh = w.h / (shp.Hq / shp.Hkv);
   w.row0 = (n_qt - 1 - t / BH) * BM;
-  w.n_kv = kv_tiles_for_rows(shp, w.row0, BM, BN);
+  w.sq = seq_of(shp, w.b);
+  w.n_kv = kv_tiles_for_rows(shp, w.sq, w.row0, BM, BN);
   return w;
 }
 }  // namespace bdqw
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         mbar_arrive_expect_tx(q_full + tb, C::Q_TILE_BYTES);
         for (int bx = 0; bx < G::NBOX; ++bx)
           tma_load_4d(smem + qd_off + tb * C::Q_TILE_BYTES + bx * BM * G::SW, tmap_qd, q_full + tb, bx * G::BOX,
-                      w.row0, w.h, w.b);
+                      w.sq.q0 + w.row0, w.h, w.sq.tb);
         ++tcn;
         for (int j = 0; j < w.n_kv; ++j, ++gj) {
           const int s = gj % C::NST;
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
             tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                        j * BN, w.kvh, w.b);
+                        w.sq.k0 + j * BN, w.kvh, w.sq.tb);
         }
       }
       for (int i = (tcn > C::QB ? tcn - C::QB : 0); i < tcn; ++i)
@@ -281,11 +283,11 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       const int r = wt.row0 + wq * 32 + lane;
       l = INFINITY;
       d = 0.f;
-      if (r < shp.Nq && wt.n_kv > 0) {
-        const long long bh = (long long)wt.b * shp.Hq + wt.h;
-        const float x = lse[bh * shp.Nq + r];
+      if (r < wt.sq.nq && wt.n_kv > 0) {
+        const long long i = row_stat_index(shp, wt.sq, wt.b, wt.h, r);
+        const float x = lse[i];
         l = x == -INFINITY ? INFINITY : x;
-        d = delta[bh * shp.Nq + r];
+        d = delta[i];
       }
     };
     int t_cur = snake_unit(cta, 0, n_cta, n_tiles);
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         row_vals(wt, lse_n, delta_n);
       }
       const int r = cur.row0 + wq * 32 + lane;
-      int lim = shp.Nk - 1;
+      int lim = cur.sq.nk - 1;
       if (shp.causal) {
         const long long c = (long long)r + shp.q_off - shp.k_off;
         lim = c < lim ? int(c) : lim;
@@ -365,8 +367,9 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < HALF; ++i) gv[i] = 0.f;
       }
-      if (r < shp.Nq) {
-        const long long off = (long long)cur.b * dq_sb + (long long)cur.h * dq_sh + (long long)r * dq_sn + w * HALF;
+      if (r < cur.sq.nq) {
+        const long long off =
+            (long long)cur.sq.tb * dq_sb + (long long)cur.h * dq_sh + (long long)(cur.sq.q0 + r) * dq_sn + w * HALF;
         if (accumulate_fp32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
 #pragma unroll

@@ -92,7 +92,9 @@ struct Cfg {
 // head of the group x 128-row query tile) that see them.
 struct Tile {
   int kv0, b, kvh, i_start, per_head, n_items;
+  Seq sq;
 };
+template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   const int BHkv = shp.B * shp.Hkv;
   const int kv_tile = t / BHkv;
@@ -101,7 +103,8 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.b = bhk / shp.Hkv;
   w.kvh = bhk % shp.Hkv;
   w.kv0 = kv_tile * BM;
-  const int n_qt = (shp.Nq + BQ - 1) / BQ;
+  w.sq = seq_of_v<VL>(shp, w.b);
+  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
   int i_start = 0;
   if (shp.causal) {
     // first query tile holding a row at or after this tile's first key
@@ -116,6 +119,7 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 
 // Walks the items of a CTA's non-empty tiles in issue order.
+template <bool VL>
 struct ItemCursor {
   int k, it;
   Tile w;
@@ -124,7 +128,7 @@ struct ItemCursor {
     for (;; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) return false;
-      w = tile_of(shp, t);
+      w = tile_of<VL>(shp, t);
       if (w.n_items > 0) {
         it = 0;
         return true;
@@ -139,7 +143,7 @@ struct ItemCursor {
 };
 }  // namespace bfz
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     fa_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                         const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       // rows that see no key, get lse2 = +inf so that their P is 0.
       constexpr int PF = 2;
       float lv[PF + 1][4], dvv[PF + 1][4];
-      ItemCursor ahead{0, 0, {}};
+      ItemCursor<VL> ahead{0, 0, {}};
       bool ahead_ok = is_q && ahead.seek(shp, cta, n_cta, n_tiles);
       auto fetch = [&](float (&l)[4], float (&d)[4]) {
 #pragma unroll
@@ -256,11 +260,11 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         if (!ahead_ok) return;
         const int h = ahead.w.kvh * group + ahead.it / ahead.w.per_head;
         const int q0 = (ahead.w.i_start + ahead.it % ahead.w.per_head) * BQ;
-        const long long rowbase = ((long long)ahead.w.b * shp.Hq + h) * shp.Nq;
+        const long long rowbase = row_stat_index_v<VL>(shp, ahead.w.sq, ahead.w.b, h, 0);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int qi = q0 + e * 32 + lane;
-          if (qi < shp.Nq) {
+          if (qi < ahead.w.sq.nq) {
             l[e] = lse[rowbase + qi];
             d[e] = delta[rowbase + qi];
           }
@@ -274,7 +278,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       for (int k = 0; ok; ++k) {
         const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
-        const Tile w = tile_of(shp, t);
+        const Tile w = tile_of<VL>(shp, t);
         if (w.n_items == 0) continue;
         const int kb = tcn & 1;
         if (tcn >= 2 && !mbar_wait_warp(kv_empty + kb, uint32_t((tcn >> 1) - 1) & 1, ctl, 200)) {
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
           mbar_arrive_expect_tx(kv_full + kb, C::KV_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
             tma_load_4d(smem + kv_off + kb * C::KV_TILE_BYTES + bx * BM * G::SW, tmap_kv, kv_full + kb,
-                        bx * G::BOX, w.kv0, w.kvh, w.b);
+                        bx * G::BOX, w.sq.k0 + w.kv0, w.kvh, w.sq.tb);
         }
         ++tcn;
         for (int it = 0; it < w.n_items; ++it) {
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
             mbar_arrive_expect_tx(full + s, C::Q_TILE_BYTES);
             for (int bx = 0; bx < G::NBOX; ++bx)
               tma_load_4d(smem + qd_off + s * C::Q_TILE_BYTES + bx * BQ * G::SW, tmap_qd, full + s, bx * G::BOX,
-                          q0, h, w.b);
+                          w.sq.q0 + q0, h, w.sq.tb);
           }
           if (is_q) {
 #pragma unroll
@@ -377,7 +381,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int t = snake_unit(cta, k, n_cta, n_tiles);
           if (t >= n_tiles) break;
-          const int n = tile_of(shp, t).n_items;
+          const int n = tile_of<VL>(shp, t).n_items;
           if (n == 0) continue;
           const int kb = tcn & 1;
           if (!mbar_wait(kv_full + kb, uint32_t(tcn >> 1) & 1, ctl, 211)) { ok = false; break; }
@@ -452,8 +456,10 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
-      const Tile wt = tile_of(shp, t);
+      const Tile wt = tile_of<VL>(shp, t);
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
+      // key rows past the batch's keys (the next batch's, when packed) see no query
+      const bool key_out = VL && wt.kv0 + rl >= wt.sq.nk;
       for (int it = 0; it < wt.n_items && ok; ++it) {
         const int g = gi + it;
         const int s = g % C::NST;
@@ -468,13 +474,14 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
             const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * hh);
             float st[64];
             tmem_ld64(tS, st);
-            if (shp.causal) {
+            int cmin = key_out ? 64 : 0;
+            if (shp.causal && !key_out) {
               const long long x = cmin_base - q0 - 64 * hh;
-              const int cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
-              if (cmin > 0) {
+              cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+            }
+            if (cmin > 0) {
 #pragma unroll
-                for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
-              }
+              for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];
@@ -548,12 +555,13 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         tc_fence_after();
       }
       const int kr = wt.kv0 + rl;
-      const bool row_ok = kr < shp.Nk;
+      const bool row_ok = kr < wt.sq.nk;
       const float sc = w == 0 ? 1.f : shp.scale;
       const uint32_t tAcc = lane_base + uint32_t(w == 0 ? C::DV_COL : C::DK_COL);
       void* out = w == 0 ? dv_out : dk_out;
-      const long long off0 = w == 0 ? ((long long)wt.b * dv_sb + (long long)wt.kvh * dv_sh + (long long)kr * dv_sn)
-                                    : ((long long)wt.b * dk_sb + (long long)wt.kvh * dk_sh + (long long)kr * dk_sn);
+      const long long krow = (long long)wt.sq.k0 + kr;
+      const long long off0 = w == 0 ? ((long long)wt.sq.tb * dv_sb + (long long)wt.kvh * dv_sh + krow * dv_sn)
+                                    : ((long long)wt.sq.tb * dk_sb + (long long)wt.kvh * dk_sh + krow * dk_sn);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float gv[32];
@@ -611,7 +619,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
       if (t >= n_tiles) break;
-      const Tile wt = tile_of(shp, t);
+      const Tile wt = tile_of<VL>(shp, t);
       for (int it = 0; it < wt.n_items; ++it) {
         const int g = gi + it;
         const int h = wt.kvh * group + it / wt.per_head;
@@ -637,7 +645,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
           mbar_arrive(stage_full);
           if (leader) {
             if (!mbar_wait(stage_full, pieces & 1, ctl, 232)) { ok = false; break; }
-            tma_reduce_add_4d(&tmap_dq, smem + C::OFF_DQS, j * 32, q0, h, wt.b);
+            tma_reduce_add_4d(&tmap_dq, smem + C::OFF_DQS, j * 32, wt.sq.q0 + q0, h, wt.sq.tb);
             bulk_commit_group();
             bulk_wait_read_all();
             mbar_arrive(stage_free);
@@ -660,10 +668,10 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT>
+template <int D, int DT, bool VL>
 int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
   using C = bfz::Cfg<D>;
-  auto kern = fa_bwd_fused_kernel<D, DT>;
+  auto kern = fa_bwd_fused_kernel<D, DT, VL>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -685,12 +693,19 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+// Dense and packed (varlen) layouts are separate instantiations, so the
+// dense kernels carry no per-batch offset arithmetic.
+template <int D, int DT>
+int launch_bwd_fused_l(const BwdArgs& a, const CUtensorMap& tmap_dq) {
+  return a.shape.cu_q ? launch_bwd_fused_t<D, DT, true>(a, tmap_dq) : launch_bwd_fused_t<D, DT, false>(a, tmap_dq);
+}
+
 int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D) {
   switch (D) {
     case 32:
-      return a.dtype == DT_BF16 ? launch_bwd_fused_t<32, DT_BF16>(a, tmap_dq) : launch_bwd_fused_t<32, DT_F16>(a, tmap_dq);
+      return a.dtype == DT_BF16 ? launch_bwd_fused_l<32, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<32, DT_F16>(a, tmap_dq);
     case 64:
-      return a.dtype == DT_BF16 ? launch_bwd_fused_t<64, DT_BF16>(a, tmap_dq) : launch_bwd_fused_t<64, DT_F16>(a, tmap_dq);
+      return a.dtype == DT_BF16 ? launch_bwd_fused_l<64, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<64, DT_F16>(a, tmap_dq);
     default:
       return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }

@@ -101,6 +101,10 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.scale = scale;
   s.scale_log2 = float(double(scale) * 1.4426950408889634);
   s.status = status_ptr();
+  s.cu_q = nullptr;
+  s.cu_k = nullptr;
+  s.total_q = 0;
+  s.total_k = 0;
   return s;
 }
 
@@ -293,6 +297,130 @@ int merge_impl(float* o_acc, float* lse_acc, const void* o_part, const float* ls
                               static_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------------------
+// Packed variable-length batches (no counterpart in the reference): q, o,
+// dO, dq are contiguous (total_q, Hq, D), k, v, dk, dv contiguous
+// (total_k, Hkv, D); batch b owns rows [cu_q[b], cu_q[b+1]) and
+// [cu_k[b], cu_k[b+1]).  The kernels are the dense ones, reading the packed
+// tensors through (1, H, total, D) tensor maps at the batch's row offset.
+
+// Element strides {batch, head, row} of a contiguous (total, H, D) tensor
+// seen as (1, H, total, D).
+struct PackedStrides {
+  int64_t v[3];
+  PackedStrides(int total, int H, int D) {
+    v[0] = int64_t(total > 0 ? total : 1) * H * D;
+    v[1] = D;
+    v[2] = int64_t(H) * D;
+  }
+};
+
+int check_varlen(const int* cu_q, const int* cu_k, int B, int Hq, int Hkv, int max_q, int max_k, int total_q,
+                 int total_k, int D) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) return FA_ERR_BAD_SHAPE;
+  if (max_q <= 0 || max_k <= 0 || total_q <= 0 || total_k <= 0) return FA_ERR_BAD_SHAPE;
+  if (!cu_q || !cu_k) return FA_ERR_BAD_SHAPE;
+  return FA_OK;
+}
+
+AttnShape varlen_shape(const int* cu_q, const int* cu_k, int B, int Hq, int Hkv, int max_q, int max_k, int total_q,
+                       int total_k, float scale, int causal) {
+  AttnShape sh = make_shape(B, Hq, Hkv, max_q, max_k, scale, causal, 0, 0);
+  sh.cu_q = cu_q;
+  sh.cu_k = cu_k;
+  sh.total_q = total_q;
+  sh.total_k = total_k;
+  return sh;
+}
+
+int fwd_varlen_impl(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_q,
+                    const int* cu_k, int B, int Hq, int Hkv, int max_q, int max_k, int total_q, int total_k, int D,
+                    float softmax_scale, int causal, void* stream, int dtype) {
+  int rc = check_varlen(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !lse || !std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const PackedStrides sq(total_q, Hq, D), sk(total_k, Hkv, D);
+  if (!out_strides_ok(o, sq.v, 2)) return FA_ERR_MISALIGNED;
+  FwdArgs a;
+  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, 128, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, 128, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, 128, dtype))) return rc;
+  a.shape = varlen_shape(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, softmax_scale, causal);
+  a.dtype = dtype;
+  a.o = o;
+  a.o_sb = 0;
+  a.o_sh = sq.v[1];
+  a.o_sn = sq.v[2];
+  a.lse = lse;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_fwd(a, D);
+}
+
+int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
+                    void* dq, void* dk, void* dv, float* delta, float* dq_accum, const int* cu_q, const int* cu_k,
+                    int B, int Hq, int Hkv, int max_q, int max_k, int total_q, int total_k, int D,
+                    float softmax_scale, int causal, int deterministic, void* stream, int dtype) {
+  int rc = check_varlen(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv || !delta) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const bool fused = D <= 64 && !deterministic;
+  if (fused && !dq_accum) return FA_ERR_BAD_SHAPE;
+  const PackedStrides sq(total_q, Hq, D), sk(total_k, Hkv, D);
+  if (!out_strides_ok(o, sq.v, 2) || !out_strides_ok(dO, sq.v, 2) || !out_strides_ok(dq, sq.v, 2) ||
+      !out_strides_ok(dk, sk.v, 2) || !out_strides_ok(dv, sk.v, 2) || !aligned16(delta) ||
+      (fused && !aligned16(dq_accum)))
+    return FA_ERR_MISALIGNED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Delta (Hq, total_q) and, for the fused pass, the zeroed (Hq, total_q, D) accumulator
+  if ((rc = launch_bwd_delta(o, sq.v[0], sq.v[1], sq.v[2], dO, sq.v[0], sq.v[1], sq.v[2], delta,
+                             fused ? dq_accum : nullptr, 1, Hq, total_q, D, dtype, st)))
+    return rc;
+  BwdArgs a;
+  a.dtype = dtype;
+  a.shape = varlen_shape(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, softmax_scale, causal);
+  a.lse = lse;
+  a.delta = delta;
+  a.dk = dk;
+  a.dv = dv;
+  a.dk_sb = a.dv_sb = 0;
+  a.dk_sh = a.dv_sh = sk.v[1];
+  a.dk_sn = a.dv_sn = sk.v[2];
+  a.accumulate_fp32 = 0;
+  a.stream = st;
+  if (fused) {
+    if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dkdv_cfg::BQ_WIDE, dtype))) return rc;
+    if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, dkdv_cfg::BQ_WIDE, dtype))) return rc;
+    if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
+    if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
+    CUtensorMap tmap_dq;
+    if ((rc = make_acc_map(&tmap_dq, dq_accum, 1, Hq, total_q, D))) return rc;
+    a.dq = dq_accum;
+    a.dq_sb = a.dq_sh = a.dq_sn = 0;
+    if ((rc = launch_bwd_fused(a, tmap_dq, D))) return rc;
+    return launch_dq_convert(dq_accum, dq, sq.v[0], sq.v[1], sq.v[2], 1, Hq, total_q, D, dtype, st);
+  }
+  // split path: dQ kernel, then dK/dV kernel
+  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dq_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, dq_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, dq_cfg::BN, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, dq_cfg::BN, dtype))) return rc;
+  a.dq = dq;
+  a.dq_sb = 0;
+  a.dq_sh = sq.v[1];
+  a.dq_sn = sq.v[2];
+  if ((rc = launch_bwd_dq(a, D))) return rc;
+  const int bq = D <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
+  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, bq, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
+  a.dq = nullptr;
+  a.dq_sb = a.dq_sh = a.dq_sn = 0;
+  return launch_bwd_dkdv(a, D);
+}
+
 }  // namespace
 }  // namespace fa
 
@@ -410,6 +538,39 @@ extern "C" int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, in
   return convert_impl(dq_accum, dq, B, H, N, D, dq_strides, stream, DT_BF16);
 }
 
+extern "C" int fa_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
+                             const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                             int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D, float softmax_scale,
+                             int causal, void* stream) {
+  return fwd_varlen_impl(q, k, v, o, lse, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv, max_seqlen_q, max_seqlen_k,
+                         total_q, total_k, D, softmax_scale, causal, stream, DT_F16);
+}
+extern "C" int fa_fwd_varlen_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                                  int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                                  float softmax_scale, int causal, void* stream) {
+  return fwd_varlen_impl(q, k, v, o, lse, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv, max_seqlen_q, max_seqlen_k,
+                         total_q, total_k, D, softmax_scale, causal, stream, DT_BF16);
+}
+extern "C" int fa_bwd_varlen(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                             const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                             const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                             int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D, float softmax_scale,
+                             int causal, int deterministic, void* stream) {
+  return bwd_varlen_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv,
+                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, deterministic, stream,
+                         DT_F16);
+}
+extern "C" int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                  const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                                  int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
+                                  float softmax_scale, int causal, int deterministic, void* stream) {
+  return bwd_varlen_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv,
+                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, deterministic, stream,
+                         DT_BF16);
+}
+
 extern "C" int fa_device_status(int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return FA_ERR_LAUNCH;
   int v = 0;
@@ -437,4 +598,4 @@ extern "C" const char* fa_status_string(int code) {
   }
 }
 
-extern "C" int fa_version(void) { return 10200; }
+extern "C" int fa_version(void) { return 10300; }

@@ -49,15 +49,75 @@ struct AttnShape {
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
   int* status;       // device status word (see CtaCtl)
+  // Packed variable-length batches: when cu_q is not null, batch b owns
+  // query rows [cu_q[b], cu_q[b+1]) and key rows [cu_k[b], cu_k[b+1]) of
+  // tensors packed as (total, heads, D); Nq / Nk are then the longest
+  // sequence lengths, and lse / Delta are laid out (Hq, total_q).
+  const int* cu_q;
+  const int* cu_k;
+  int total_q, total_k;
 };
 
-// Number of K/V tiles of width BN a block of query rows [r0, r0 + rows)
-// touches; 0 when every key is masked for all of them.
-__device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, int r0, int rows, int BN) {
-  if (r0 >= s.Nq) return 0;
-  int last = s.Nk - 1;
+// Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of
+// the tensors, and tb, b's coordinate in the 4-D tensor maps (0 when packed).
+struct Seq {
+  int q0, nq, k0, nk, tb;
+};
+__device__ __forceinline__ Seq seq_of(const AttnShape& s, int b) {
+  Seq r;
+  if (s.cu_q) {
+    r.q0 = __ldg(s.cu_q + b);
+    r.nq = __ldg(s.cu_q + b + 1) - r.q0;
+    r.k0 = __ldg(s.cu_k + b);
+    r.nk = __ldg(s.cu_k + b + 1) - r.k0;
+    r.tb = 0;
+  } else {
+    r.q0 = 0;
+    r.nq = s.Nq;
+    r.k0 = 0;
+    r.nk = s.Nk;
+    r.tb = b;
+  }
+  return r;
+}
+// Compile-time variants for kernels instantiated per layout: VL = packed.
+template <bool VL>
+__device__ __forceinline__ Seq seq_of_v(const AttnShape& s, int b) {
+  if constexpr (VL) {
+    Seq r;
+    r.q0 = __ldg(s.cu_q + b);
+    r.nq = __ldg(s.cu_q + b + 1) - r.q0;
+    r.k0 = __ldg(s.cu_k + b);
+    r.nk = __ldg(s.cu_k + b + 1) - r.k0;
+    r.tb = 0;
+    return r;
+  } else {
+    Seq r;
+    r.q0 = 0;
+    r.nq = s.Nq;
+    r.k0 = 0;
+    r.nk = s.Nk;
+    r.tb = b;
+    return r;
+  }
+}
+template <bool VL>
+__device__ __forceinline__ long long row_stat_index_v(const AttnShape& s, const Seq& q, int b, int h, int r) {
+  if constexpr (VL) return (long long)h * s.total_q + q.q0 + r;
+  else return ((long long)b * s.Hq + h) * s.Nq + r;
+}
+// Index of query row r (local to batch b) of head h in lse / Delta.
+__device__ __forceinline__ long long row_stat_index(const AttnShape& s, const Seq& q, int b, int h, int r) {
+  return s.cu_q ? (long long)h * s.total_q + q.q0 + r : ((long long)b * s.Hq + h) * s.Nq + r;
+}
+
+// Number of K/V tiles of width BN a block of query rows [r0, r0 + rows) of
+// a batch touches; 0 when every key is masked for all of them.
+__device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, const Seq& q, int r0, int rows, int BN) {
+  if (r0 >= q.nq || q.nk <= 0) return 0;
+  int last = q.nk - 1;
   if (s.causal) {
-    const int last_row = (r0 + rows < s.Nq ? r0 + rows : s.Nq) - 1;
+    const int last_row = (r0 + rows < q.nq ? r0 + rows : q.nq) - 1;
     const long long lim = (long long)last_row + s.q_off - s.k_off;
     if (lim < 0) return 0;
     if (lim < last) last = int(lim);

@@ -98,6 +98,7 @@ struct Cfg {
 // mask).
 struct Unit {
   int b, h, kvh, row0, n_kv[QT], n_max;
+  Seq sq;
 };
 __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   const int BH = shp.B * shp.Hq;
@@ -108,10 +109,11 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   w.h = bh % shp.Hq;
   w.kvh = w.h / (shp.Hq / shp.Hkv);
   w.row0 = (n_qblk - 1 - u / BH) * QT * BM;
+  w.sq = seq_of(shp, w.b);
   w.n_max = 0;
 #pragma unroll
   for (int t = 0; t < QT; ++t) {
-    w.n_kv[t] = kv_tiles_for_rows(shp, w.row0 + t * BM, BM, BN);
+    w.n_kv[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * BM, BM, BN);
     w.n_max = w.n_kv[t] > w.n_max ? w.n_kv[t] : w.n_max;
   }
   return w;
@@ -230,7 +232,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
               if (w.n_kv[t] == 0) continue;
               for (int bx = 0; bx < G::NBOX; ++bx)
                 tma_load_4d(smem + C::OFF_Q + qb * C::Q_UNIT_BYTES + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q,
-                            q_full + qb, bx * G::BOX, w.row0 + t * BM, w.h, w.b);
+                            q_full + qb, bx * G::BOX, w.sq.q0 + w.row0 + t * BM, w.h, w.sq.tb);
             }
           }
           ++uc;
@@ -241,7 +243,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
             for (int bx = 0; bx < G::NBOX; ++bx)
               tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                          j * BN, w.kvh, w.b);
+                          w.sq.k0 + j * BN, w.kvh, w.sq.tb);
           }
         }
         // Drain: every load this thread issued must land before the CTA exits.
@@ -403,7 +405,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       const int r = w.row0 + t * BM + row_local;  // query row
       const int nt = w.n_kv[t];
       // last visible key column of this row (local key index)
-      int lim = shp.Nk - 1;
+      int lim = w.sq.nk - 1;
       if (shp.causal) {
         const long long c = (long long)r + shp.q_off - shp.k_off;
         lim = c < lim ? int(c) : lim;  // may be negative: no visible key
@@ -528,9 +530,9 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         if (!mbar_wait_warp(o_full + t, uint32_t(oc) & 1, ctl, 22 + t)) { ok = false; break; }
         tc_fence_after();
       }
-      const bool row_ok = r < shp.Nq;
+      const bool row_ok = r < w.sq.nq;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* orow = o_ptr + (long long)w.b * o_sb + (long long)w.h * o_sh + (long long)r * o_sn;
+      uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)w.h * o_sh + (long long)(w.sq.q0 + r) * o_sn;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
@@ -559,7 +561,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       if (nt > 0) ++oc;
       if (row_ok) {
-        lse_ptr[((long long)w.b * shp.Hq + w.h) * shp.Nq + r] = l > 0.f ? m + lg2(l) : -INFINITY;
+        lse_ptr[row_stat_index(shp, w.sq, w.b, w.h, r)] = l > 0.f ? m + lg2(l) : -INFINITY;
       }
     }
   }

@@ -1,0 +1,163 @@
+"""Packed variable-length attention on the B200 kernels.
+
+No counterpart in the reference: its API takes ``(batch, heads, sequence,
+head_dim)`` tensors whose sequences all have one length
+(triton_flash_attention/attention.py:584-626).  Serving and packed-sequence
+training hold a batch of sequences of different lengths back to back
+instead: ``query`` is ``(total_q, Hq, D)``, ``key`` / ``value`` are
+``(total_k, Hkv, D)``, and int32 prefix sums ``cu_seqlens_q`` /
+``cu_seqlens_k`` (length ``B + 1``, starting at 0) say which rows belong to
+which sequence.  Each sequence attends only to its own keys; the causal mask
+is applied per sequence and top-left aligned (query ``i`` of a sequence sees
+its keys ``j <= i``), like the dense call.
+
+The same sm_100a kernels serve both layouts (the C ABI's ``fa_fwd_varlen`` /
+``fa_bwd_varlen``); the saved log-sum-exp is ``(Hq, total_q)`` fp32.
+"""
+
+from __future__ import annotations
+
+import math
+from numbers import Real
+
+import torch
+
+from . import _abi
+from .attention import SUPPORTED_DTYPES, SUPPORTED_HEAD_DIMS, _stream_handle, fused_backward_enabled
+
+
+def _validate_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, *,
+                     enable_gqa: bool) -> None:
+    tensors = {"query": query, "key": key, "value": value}
+    for name, tensor in tensors.items():
+        if not isinstance(tensor, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if tensor.ndim != 3:
+            raise ValueError(f"{name} must have shape (total, heads, head_dim); got {tuple(tensor.shape)}")
+        if tensor.shape[0] == 0 or tensor.shape[1] == 0 or tensor.shape[2] == 0:
+            raise ValueError(f"{name} dimensions must all be greater than zero")
+    for name, cu in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        if not isinstance(cu, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if cu.ndim != 1 or cu.numel() < 2 or cu.dtype != torch.int32:
+            raise ValueError(f"{name} must be a 1-D int32 tensor of batch + 1 prefix sums")
+        if cu.device != query.device:
+            raise ValueError(f"{name} must be on the same device as query")
+    if cu_seqlens_q.numel() != cu_seqlens_k.numel():
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must describe the same number of sequences")
+    for name, m in (("max_seqlen_q", max_seqlen_q), ("max_seqlen_k", max_seqlen_k)):
+        if isinstance(m, bool) or not isinstance(m, int) or m <= 0:
+            raise ValueError(f"{name} must be a positive int")
+    if query.device != key.device or query.device != value.device:
+        raise ValueError("query, key, and value must be on the same device")
+    if query.dtype != key.dtype or query.dtype != value.dtype:
+        raise ValueError("query, key, and value must have the same dtype")
+    if key.shape != value.shape:
+        raise ValueError("key and value must have the same shape")
+    if query.shape[2] != key.shape[2]:
+        raise ValueError("query and key head dimensions must match")
+    q_heads, kv_heads = query.shape[1], key.shape[1]
+    if q_heads != kv_heads and not enable_gqa:
+        raise ValueError(
+            "query has a different number of heads from key/value; pass "
+            "enable_gqa=True to use grouped-query attention")
+    if q_heads % kv_heads != 0:
+        raise ValueError("the number of query heads must be divisible by the number of key/value heads")
+    if query.device.type != "cuda":
+        raise RuntimeError("B200 CUDA backend is unavailable: the B200 kernel requires a CUDA tensor")
+    if query.dtype not in SUPPORTED_DTYPES:
+        raise RuntimeError("B200 CUDA backend is unavailable: the custom mixed-precision path currently "
+                           "supports float16 and bfloat16")
+    if query.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        supported = ", ".join(str(dim) for dim in SUPPORTED_HEAD_DIMS)
+        raise RuntimeError(f"B200 CUDA backend is unavailable: head_dim must be one of ({supported}) "
+                           "for the B200 path")
+    if torch.cuda.get_device_capability(query.device) != (10, 0):
+        raise RuntimeError("B200 CUDA backend is unavailable: the kernels are built for sm_100a (B200) GPUs only")
+
+
+def varlen_attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, max_seqlen_k: int,
+                             causal: bool, softmax_scale: float):
+    """Forward over packed sequences: returns ``(o, lse2)`` with ``o`` like
+    ``q`` and ``lse2`` the ``(Hq, total_q)`` base-2 log-sum-exp per row."""
+    total_q, hq, d = q.shape
+    total_k, hkv = k.shape[0], k.shape[1]
+    batch = cu_seqlens_q.numel() - 1
+    o = torch.empty_like(q)
+    lse = torch.empty((hq, total_q), device=q.device, dtype=torch.float32)
+    rc = _abi.entry("fa_fwd_varlen", q.dtype)(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+        cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, hq, hkv, int(max_seqlen_q), int(max_seqlen_k),
+        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, _stream_handle(q.device))
+    _abi.check(rc, "fa_fwd_varlen")
+    return o, lse
+
+
+def varlen_attention_backward(q, k, v, o, do, lse, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
+                              max_seqlen_k: int, causal: bool, softmax_scale: float):
+    """dQ, dK, dV over packed sequences.  Head dims 32 and 64 run the fused
+    pass (fp32 dQ accumulator in caller scratch) unless
+    ``torch.use_deterministic_algorithms(True)`` asks for the separate,
+    bitwise-reproducible dQ and dK/dV kernels."""
+    total_q, hq, d = q.shape
+    total_k, hkv = k.shape[0], k.shape[1]
+    batch = cu_seqlens_q.numel() - 1
+    fused = fused_backward_enabled(d)
+    delta = torch.empty((hq, total_q), device=q.device, dtype=torch.float32)
+    acc = torch.empty((hq, total_q, d), device=q.device, dtype=torch.float32) if fused else None
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    rc = _abi.entry("fa_bwd_varlen", q.dtype)(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+        dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr(), acc.data_ptr() if fused else None,
+        cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, hq, hkv, int(max_seqlen_q), int(max_seqlen_k),
+        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, 0 if fused else 1, _stream_handle(q.device))
+    _abi.check(rc, "fa_bwd_varlen")
+    return dq, dk, dv
+
+
+class B200VarlenAttention(torch.autograd.Function):
+    """Autograd bridge for packed variable-length attention; saves
+    (q, k, v, O, LSE) like the dense Function, plus the sequence offsets."""
+
+    @staticmethod
+    def forward(ctx, query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
+                softmax_scale):
+        output, lse = varlen_attention_forward(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                               max_seqlen_k, bool(causal), float(softmax_scale))
+        ctx.save_for_backward(query, key, value, output, lse, cu_seqlens_q, cu_seqlens_k)
+        ctx.max_seqlen = (int(max_seqlen_q), int(max_seqlen_k))
+        ctx.causal = bool(causal)
+        ctx.softmax_scale = float(softmax_scale)
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        query, key, value, output, lse, cu_q, cu_k = ctx.saved_tensors
+        dq, dk, dv = varlen_attention_backward(query, key, value, output, grad_output.contiguous(), lse, cu_q, cu_k,
+                                               *ctx.max_seqlen, ctx.causal, ctx.softmax_scale)
+        return dq, dk, dv, None, None, None, None, None, None
+
+
+def scaled_dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
+                                        max_seqlen_k: int, *, is_causal: bool = False, scale: float | None = None,
+                                        enable_gqa: bool = False) -> torch.Tensor:
+    """Attention over a batch of packed sequences of different lengths.
+
+    ``query``: ``(total_q, Hq, D)``; ``key``, ``value``: ``(total_k, Hkv, D)``;
+    ``cu_seqlens_q`` / ``cu_seqlens_k``: int32 prefix sums of the sequence
+    lengths on the same device (``[0, n_0, n_0 + n_1, ...]``, ending at the
+    totals); ``max_seqlen_q`` / ``max_seqlen_k``: at least the longest
+    sequence's lengths.  Sequences may be empty.  Returns ``(total_q, Hq, D)``
+    and supports autograd.  The default ``scale`` is ``D ** -0.5``."""
+    if not isinstance(is_causal, bool):
+        raise TypeError("is_causal must be a bool")
+    if not isinstance(enable_gqa, bool):
+        raise TypeError("enable_gqa must be a bool")
+    if scale is not None and (not isinstance(scale, Real) or not math.isfinite(float(scale))):
+        raise ValueError("scale must be a finite real number or None")
+    _validate_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                     enable_gqa=enable_gqa)
+    softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
+    return B200VarlenAttention.apply(query.contiguous(), key.contiguous(), value.contiguous(),
+                                     cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous(), max_seqlen_q,
+                                     max_seqlen_k, is_causal, softmax_scale)
