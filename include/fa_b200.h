@@ -228,6 +228,30 @@ FA_API int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const
                        int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
                        float softmax_scale, int causal, int deterministic, void* stream);
 
+/* Forward over a paged K/V cache.  No counterpart in the reference (it has
+ * no cache); this is the layout serving engines keep keys and values in.
+ * Queries, o and lse as in fa_fwd_varlen (packed (total_q, Hq, D), cu_seqlens_q,
+ * lse (Hq, total_q)).  k_cache / v_cache are contiguous
+ * (num_pages, page_size, Hkv, D); batch b has seqlens_k[b] keys (device int32
+ * array of B), and its key j is row j % page_size of page
+ * block_table[b * max_pages_per_seq + j / page_size] (device int32 array of
+ * B * max_pages_per_seq).  page_size is a power of two, at least 16.  The
+ * causal mask is bottom-right aligned, the KV-cache convention: query i of a
+ * batch with nq queries and nk keys sees keys j <= i + nk - nq.  Cache rows
+ * past a batch's length (in its last page) must hold finite values: their
+ * keys are masked, but their values still meet a zero weight in the P V
+ * product.  Forward only. */
+FA_API int fa_fwd_paged(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                 const int* cu_seqlens_q, const int* seqlens_k, const int* block_table,
+                 int B, int Hq, int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q,
+                 int num_pages, int page_size, int max_pages_per_seq, int D,
+                 float softmax_scale, int causal, void* stream);
+FA_API int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                      const int* cu_seqlens_q, const int* seqlens_k, const int* block_table,
+                      int B, int Hq, int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q,
+                      int num_pages, int page_size, int max_pages_per_seq, int D,
+                      float softmax_scale, int causal, void* stream);
+
 /* Size of the scratch array fa_bwd_fused_noalloc uses: 32 MiB per device. */
 #define FA_NOALLOC_SCRATCH_BYTES (32u << 20)
 
@@ -267,7 +291,8 @@ FA_API int fa_device_status(int reset);
 FA_API const char* fa_status_string(int code);
 
 /* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
- * 1.2.0 the fused backward, 1.3.0 packed variable-length batches). */
+ * 1.2.0 the fused backward, 1.3.0 packed variable-length batches and the
+ * paged K/V forward). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

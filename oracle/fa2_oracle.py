@@ -143,6 +143,36 @@ def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | N
     return out
 
 
+def sdpa_paged_reference(q, k_cache, v_cache, block_table, cu_q, seqlens_k, *, causal: bool,
+                         scale: float | None = None):
+    """Forward over a paged K/V cache in float64: sequence b's keys are rows
+    0..seqlens_k[b]-1 of its pages block_table[b, :] laid end to end; its
+    queries are the last nq positions (causal bottom-right aligned:
+    sdpa_reference with q_offset = nk - nq).  Returns packed ``o`` and
+    ``lse2`` (Hq, total_q).  No counterpart in the reference (no cache)."""
+    q = np.asarray(q, dtype=np.float64)
+    k_cache = np.asarray(k_cache, dtype=np.float64)
+    v_cache = np.asarray(v_cache, dtype=np.float64)
+    total_q, hq, d = q.shape
+    page = k_cache.shape[1]
+    if scale is None:
+        scale = d ** -0.5
+    out = {"o": np.zeros_like(q), "lse2": np.full((hq, total_q), -np.inf)}
+    for b in range(len(cu_q) - 1):
+        q0, q1, nk = int(cu_q[b]), int(cu_q[b + 1]), int(seqlens_k[b])
+        nq = q1 - q0
+        if nq == 0 or nk == 0:
+            continue
+        pages = np.asarray(block_table[b][: (nk + page - 1) // page])
+        k = k_cache[pages].reshape(-1, *k_cache.shape[2:])[:nk]
+        v = v_cache[pages].reshape(-1, *v_cache.shape[2:])[:nk]
+        to4 = lambda x: x.transpose(1, 0, 2)[None]
+        r = sdpa_reference(to4(q[q0:q1]), to4(k), to4(v), causal=causal, scale=scale, q_offset=nk - nq)
+        out["o"][q0:q1] = r["o"][0].transpose(1, 0, 2)
+        out["lse2"][:, q0:q1] = r["lse2"][0]
+    return out
+
+
 def _f16(x):
     return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
 

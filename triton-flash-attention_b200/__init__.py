@@ -24,6 +24,8 @@ from .attention import (
 from .flops import attention_flops, delta_bytes, memory_model
 from .varlen import (
     B200VarlenAttention,
+    paged_attention_forward,
+    scaled_dot_product_attention_paged,
     scaled_dot_product_attention_varlen,
     varlen_attention_backward,
     varlen_attention_forward,
@@ -46,7 +48,9 @@ __all__ = [
     "explain_dispatch",
     "fused_backward_enabled",
     "memory_model",
+    "paged_attention_forward",
     "scaled_dot_product_attention",
+    "scaled_dot_product_attention_paged",
     "scaled_dot_product_attention_varlen",
     "varlen_attention_backward",
     "varlen_attention_forward",

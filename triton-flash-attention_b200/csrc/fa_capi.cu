@@ -105,6 +105,10 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.cu_k = nullptr;
   s.total_q = 0;
   s.total_k = 0;
+  s.seqlen_k = nullptr;
+  s.block_table = nullptr;
+  s.bt_stride = 0;
+  s.page_size = 0;
   return s;
 }
 
@@ -421,6 +425,49 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
   return launch_bwd_dkdv(a, D);
 }
 
+// ---------------------------------------------------------------------------
+// Paged K/V forward (no counterpart in the reference): packed queries as in
+// the varlen calls, keys and values in (num_pages * page_size, Hkv, D)
+// caches addressed through a (B, bt_stride) block table.
+int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse, const int* cu_q,
+                   const int* seqlens_k, const int* block_table, int B, int Hq, int Hkv, int max_q, int max_k,
+                   int total_q, int num_pages, int page_size, int bt_stride, int D, float softmax_scale, int causal,
+                   void* stream, int dtype) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || max_q <= 0 || max_k <= 0 || total_q <= 0 ||
+      num_pages <= 0 || bt_stride <= 0)
+    return FA_ERR_BAD_SHAPE;
+  // a power of two of at least 16 rows: a key tile of 128 is whole pieces of
+  // pages, each starting on a swizzle-atom boundary of the shared tile
+  if (page_size < 16 || (page_size & (page_size - 1)) != 0) return FA_ERR_BAD_SHAPE;
+  if ((long long)num_pages * page_size > 0x7fffffffLL) return FA_ERR_BAD_SHAPE;
+  if (!q || !k_cache || !v_cache || !o || !lse || !cu_q || !seqlens_k || !block_table) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const PackedStrides sq(total_q, Hq, D), sk(num_pages * page_size, Hkv, D);
+  if (!out_strides_ok(o, sq.v, 2)) return FA_ERR_MISALIGNED;
+  int rc;
+  FwdArgs a;
+  const int pr = page_size < 128 ? page_size : 128;
+  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, 128, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_k, k_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
+  if ((rc = make_map(&a.tmap_v, v_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, max_q, max_k, softmax_scale, causal, 0, 0);
+  a.shape.cu_q = cu_q;
+  a.shape.total_q = total_q;
+  a.shape.seqlen_k = seqlens_k;
+  a.shape.block_table = block_table;
+  a.shape.bt_stride = bt_stride;
+  a.shape.page_size = page_size;
+  a.dtype = dtype;
+  a.o = o;
+  a.o_sb = 0;
+  a.o_sh = sq.v[1];
+  a.o_sn = sq.v[2];
+  a.lse = lse;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_fwd(a, D);
+}
+
 }  // namespace
 }  // namespace fa
 
@@ -569,6 +616,24 @@ extern "C" int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, c
   return bwd_varlen_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv,
                          max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, deterministic, stream,
                          DT_BF16);
+}
+
+extern "C" int fa_fwd_paged(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                            const int* cu_seqlens_q, const int* seqlens_k, const int* block_table, int B, int Hq,
+                            int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q, int num_pages, int page_size,
+                            int max_pages_per_seq, int D, float softmax_scale, int causal, void* stream) {
+  return fwd_paged_impl(q, k_cache, v_cache, o, lse, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv, max_seqlen_q,
+                        max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D, softmax_scale, causal,
+                        stream, DT_F16);
+}
+extern "C" int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
+                                 const int* cu_seqlens_q, const int* seqlens_k, const int* block_table, int B, int Hq,
+                                 int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q, int num_pages,
+                                 int page_size, int max_pages_per_seq, int D, float softmax_scale, int causal,
+                                 void* stream) {
+  return fwd_paged_impl(q, k_cache, v_cache, o, lse, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv, max_seqlen_q,
+                        max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D, softmax_scale, causal,
+                        stream, DT_BF16);
 }
 
 extern "C" int fa_device_status(int reset) {

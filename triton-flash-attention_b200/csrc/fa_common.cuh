@@ -56,20 +56,36 @@ struct AttnShape {
   const int* cu_q;
   const int* cu_k;
   int total_q, total_k;
+  // Paged K/V (forward only): when block_table is not null, batch b has
+  // seqlen_k[b] keys, and key row j lives at row j % page_size of page
+  // block_table[b * bt_stride + j / page_size] of the (pages * page_size,
+  // Hkv, D) caches; the causal mask is then bottom-right aligned (query i of
+  // nq sees keys j <= i + nk - nq), the convention of a KV cache.
+  const int* seqlen_k;
+  const int* block_table;
+  int bt_stride, page_size;
 };
 
 // Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of
 // the tensors, and tb, b's coordinate in the 4-D tensor maps (0 when packed).
 struct Seq {
   int q0, nq, k0, nk, tb;
+  int diag;  // added to a query's position for the causal limit (bottom-right alignment)
 };
 __device__ __forceinline__ Seq seq_of(const AttnShape& s, int b) {
   Seq r;
+  r.diag = 0;
   if (s.cu_q) {
     r.q0 = __ldg(s.cu_q + b);
     r.nq = __ldg(s.cu_q + b + 1) - r.q0;
-    r.k0 = __ldg(s.cu_k + b);
-    r.nk = __ldg(s.cu_k + b + 1) - r.k0;
+    if (s.block_table) {
+      r.k0 = 0;
+      r.nk = __ldg(s.seqlen_k + b);
+      r.diag = r.nk - r.nq;
+    } else {
+      r.k0 = __ldg(s.cu_k + b);
+      r.nk = __ldg(s.cu_k + b + 1) - r.k0;
+    }
     r.tb = 0;
   } else {
     r.q0 = 0;
@@ -85,6 +101,7 @@ template <bool VL>
 __device__ __forceinline__ Seq seq_of_v(const AttnShape& s, int b) {
   if constexpr (VL) {
     Seq r;
+    r.diag = 0;
     r.q0 = __ldg(s.cu_q + b);
     r.nq = __ldg(s.cu_q + b + 1) - r.q0;
     r.k0 = __ldg(s.cu_k + b);
@@ -98,6 +115,7 @@ __device__ __forceinline__ Seq seq_of_v(const AttnShape& s, int b) {
     r.k0 = 0;
     r.nk = s.Nk;
     r.tb = b;
+    r.diag = 0;
     return r;
   }
 }
@@ -118,7 +136,7 @@ __device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, const Seq& 
   int last = q.nk - 1;
   if (s.causal) {
     const int last_row = (r0 + rows < q.nq ? r0 + rows : q.nq) - 1;
-    const long long lim = (long long)last_row + s.q_off - s.k_off;
+    const long long lim = (long long)last_row + s.q_off - s.k_off + q.diag;
     if (lim < 0) return 0;
     if (lim < last) last = int(lim);
   }

@@ -241,9 +241,27 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             const uint32_t u = uint32_t(gj / C::NST);
             if (u > 0 && !mbar_wait(kv_empty + s, (u - 1) & 1, ctl, is_k ? 1 : 2)) { ok = false; break; }
             mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
-            for (int bx = 0; bx < G::NBOX; ++bx)
-              tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                          w.sq.k0 + j * BN, w.kvh, w.sq.tb);
+            if (shp.block_table) {
+              // paged K/V: the tile's 128 keys in pieces of min(page, 128)
+              // rows, one load per page; pieces past the batch's last page
+              // repeat it (finite data; their keys are masked)
+              const int P = shp.page_size;
+              const int PR = P < BN ? P : BN;
+              const int last_page = (w.sq.nk - 1) / P;
+              const int* bt = shp.block_table + (long long)w.b * shp.bt_stride;
+              for (int i = 0; i < BN / PR; ++i) {
+                const int kr = j * BN + i * PR;
+                const int pidx = kr / P < last_page ? kr / P : last_page;
+                const int row = __ldg(bt + pidx) * P + kr % P;
+                for (int bx = 0; bx < G::NBOX; ++bx)
+                  tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW + i * PR * G::SW, tmap_kv,
+                              kv_full + s, bx * G::BOX, row, w.kvh, 0);
+              }
+            } else {
+              for (int bx = 0; bx < G::NBOX; ++bx)
+                tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s,
+                            bx * G::BOX, w.sq.k0 + j * BN, w.kvh, w.sq.tb);
+            }
           }
         }
         // Drain: every load this thread issued must land before the CTA exits.
@@ -407,7 +425,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       // last visible key column of this row (local key index)
       int lim = w.sq.nk - 1;
       if (shp.causal) {
-        const long long c = (long long)r + shp.q_off - shp.k_off;
+        const long long c = (long long)r + shp.q_off - shp.k_off + w.sq.diag;
         lim = c < lim ? int(c) : lim;  // may be negative: no visible key
       }
       float m = -INFINITY;  // running exponent base (scaled log2 units)

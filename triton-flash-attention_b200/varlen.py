@@ -13,6 +13,12 @@ its keys ``j <= i``), like the dense call.
 
 The same sm_100a kernels serve both layouts (the C ABI's ``fa_fwd_varlen`` /
 ``fa_bwd_varlen``); the saved log-sum-exp is ``(Hq, total_q)`` fp32.
+
+``scaled_dot_product_attention_paged`` is the forward over a paged K/V cache
+(``fa_fwd_paged``): packed queries as above, keys and values in
+``(num_pages, page_size, Hkv, D)`` caches addressed by a block table, with
+the KV-cache convention for the causal mask (bottom-right aligned: query
+``i`` of ``nq`` sees keys ``j <= i + nk - nq``).
 """
 
 from __future__ import annotations
@@ -161,3 +167,71 @@ def scaled_dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seql
     return B200VarlenAttention.apply(query.contiguous(), key.contiguous(), value.contiguous(),
                                      cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous(), max_seqlen_q,
                                      max_seqlen_k, is_causal, softmax_scale)
+
+
+def paged_attention_forward(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k, max_seqlen_q: int,
+                            max_seqlen_k: int, causal: bool, softmax_scale: float):
+    """Forward over a paged K/V cache: returns ``(o, lse2)`` like
+    ``varlen_attention_forward``."""
+    total_q, hq, d = q.shape
+    num_pages, page_size, hkv = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+    batch = cu_seqlens_q.numel() - 1
+    o = torch.empty_like(q)
+    lse = torch.empty((hq, total_q), device=q.device, dtype=torch.float32)
+    rc = _abi.entry("fa_fwd_paged", q.dtype)(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), lse.data_ptr(),
+        cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), block_table.data_ptr(), batch, hq, hkv,
+        int(max_seqlen_q), int(max_seqlen_k), total_q, num_pages, page_size, block_table.shape[1], d,
+        float(softmax_scale), 1 if causal else 0, _stream_handle(q.device))
+    _abi.check(rc, "fa_fwd_paged")
+    return o, lse
+
+
+def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k,
+                                       max_seqlen_q: int, max_seqlen_k: int, *, is_causal: bool = False,
+                                       scale: float | None = None, enable_gqa: bool = False) -> torch.Tensor:
+    """Attention of packed queries over a paged K/V cache (forward only).
+
+    ``query``: ``(total_q, Hq, D)`` with ``cu_seqlens_q`` int32 prefix sums;
+    ``k_cache``, ``v_cache``: ``(num_pages, page_size, Hkv, D)``, page_size a
+    power of two >= 16; ``block_table``: int32 ``(B, max_pages_per_seq)``,
+    the pages of each sequence in order; ``seqlens_k``: int32 ``(B,)`` key
+    counts.  Cache rows past a sequence's length must be finite (a zeroed
+    cache is).  ``is_causal`` aligns the mask bottom-right, so a sequence's
+    queries are its last ``nq`` positions (decode: one query sees every
+    key)."""
+    if not isinstance(is_causal, bool):
+        raise TypeError("is_causal must be a bool")
+    if not isinstance(enable_gqa, bool):
+        raise TypeError("enable_gqa must be a bool")
+    if scale is not None and (not isinstance(scale, Real) or not math.isfinite(float(scale))):
+        raise ValueError("scale must be a finite real number or None")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.ndim != 4:
+            raise ValueError(f"{name} must have shape (num_pages, page_size, heads, head_dim); got {tuple(t.shape)}")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must have the same shape")
+    page_size = k_cache.shape[1]
+    if page_size < 16 or page_size & (page_size - 1):
+        raise ValueError("page_size must be a power of two of at least 16")
+    for name, t, nd in (("block_table", block_table, 2), ("seqlens_k", seqlens_k, 1)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.ndim != nd or t.dtype != torch.int32 or t.device != query.device:
+            raise ValueError(f"{name} must be a {nd}-D int32 tensor on the query's device")
+    batch = cu_seqlens_q.numel() - 1 if isinstance(cu_seqlens_q, torch.Tensor) else -1
+    if block_table.shape[0] != batch or seqlens_k.numel() != batch:
+        raise ValueError("block_table and seqlens_k must have one row per sequence of cu_seqlens_q")
+    if any(t.requires_grad for t in (query, k_cache, v_cache)) and torch.is_grad_enabled():
+        raise RuntimeError("the paged K/V path is forward only; run it under torch.no_grad()")
+    # the varlen checks on (query, one page of the cache seen as keys)
+    kv_view = k_cache[0]
+    _validate_varlen(query, kv_view, kv_view, cu_seqlens_q, cu_seqlens_q, max_seqlen_q, max_seqlen_k,
+                     enable_gqa=enable_gqa)
+    softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
+    o, _ = paged_attention_forward(query.contiguous(), k_cache.contiguous(), v_cache.contiguous(),
+                                   block_table.contiguous(), cu_seqlens_q.contiguous(), seqlens_k.contiguous(),
+                                   max_seqlen_q, max_seqlen_k, is_causal, softmax_scale)
+    return o
