@@ -22,6 +22,9 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 * ``roofline``: the dominant kernel (the fused backward; dK/dV under
   ``--deterministic``) -- its GEMM FLOPs per launch over its CUDA-event
   duration against the measured dense bf16/fp16 peak.
+* ``graph``: the same step captured once in a CUDA graph (torch.cuda.graph)
+  and replayed -- the launch gaps between the four kernels removed; an extra
+  key, the metric stays the eager ``value``.
 * ``cpu_baseline``: the oracle's float32 restatement of the reference's CPU
   path timed on the host cores on a bounded sample (whole heads of C2).
 * Multi-GPU (torchrun): weak scaling -- every rank runs its own C2-sized
@@ -223,7 +226,7 @@ def run_ours(args) -> None:
     def step(record: bool):
         o, lse = fa.attention_forward(q, k, v, CAUSAL, scale)
         if fused:
-            sh = stream.cuda_stream
+            sh = torch.cuda.current_stream(dev).cuda_stream  # the capture stream under torch.cuda.graph
             _abi.check(_abi.lib().fa_bwd_preprocess(o.data_ptr(), do.data_ptr(), delta_buf.data_ptr(),
                                                     dq_acc.data_ptr(), B, H, N, D, _abi.strides3(o),
                                                     _abi.strides3(do), sh), "fa_bwd_preprocess")
@@ -285,6 +288,31 @@ def run_ours(args) -> None:
     kv_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_kv)
     value = world * fl / (ms * 1e-3) / 1e12
     status = fa._abi.device_status()
+
+    # ---------------- the same step captured once in a CUDA graph and replayed
+    # (launch gaps removed; the kernels and their work are the same)
+    graph_info = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(False)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = barrier_max(world, g0.elapsed_time(g1) / args.steps)
+        graph_info = {"ms_per_step": round(gms, 4), "value": round(world * fl / (gms * 1e-3) / 1e12, 2),
+                      "note": "the same step captured in one CUDA graph (torch.cuda.graph) and replayed"}
+        del graph
+    except Exception as exc:  # reported, not fatal: the eager number above is the metric
+        graph_info = {"error": f"{type(exc).__name__}: {exc}"[:200]}
 
     # ---------------- end to end through the public API, host buffers
     # Every step copies its q, k, v, dO from pinned host memory and its O,
@@ -387,6 +415,7 @@ def run_ours(args) -> None:
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
                          "peak_source": peaks["source"], "launch_ms": round(kv_ms, 4)},
+            "graph": graph_info,
             "cpu_baseline": cpu,
             "gpu_launches": 4 * args.steps,
             "clocks": clk.summary(),
