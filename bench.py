@@ -40,6 +40,8 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 * ``--workload varlen``: a packed batch of 16 causal sequences of ragged
   lengths through ``scaled_dot_product_attention_varlen``, beside the same
   sequences padded and run dense.  Informational.
+* ``--workload decode``: one query per sequence over a paged K/V cache
+  (``scaled_dot_product_attention_paged``), HBM roofline.  Informational.
 """
 
 from __future__ import annotations
@@ -740,6 +742,65 @@ def run_varlen(args) -> None:
     }), flush=True)
 
 
+DECODE_B, DECODE_HQ, DECODE_HKV, DECODE_D, DECODE_CTX, DECODE_PAGE = 16, 32, 8, 128, 8192, 64
+
+
+def run_decode(args) -> None:
+    """Decode over a paged K/V cache (no counterpart in the reference): 16
+    sequences of 8,192 cached tokens, one new query each, GQA 32/8, D128,
+    page 64, fp16, through ``scaled_dot_product_attention_paged`` (the GQA
+    group's 4 query heads share a query tile, so each K/V page is read once
+    per group).  Decode is bound by reading the cache: the line reports the
+    achieved HBM bandwidth (unique K/V bytes / time) against the measured
+    copy peak.  Informational, one JSON line."""
+    import numpy as np
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    dev = torch.device("cuda", 0)
+    pages_per = DECODE_CTX // DECODE_PAGE
+    n_pages = DECODE_B * pages_per
+    rng = np.random.default_rng(5)
+    table = torch.tensor(rng.permutation(n_pages).reshape(DECODE_B, pages_per), dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(6)
+    kc, vc = (torch.randn(n_pages, DECODE_PAGE, DECODE_HKV, DECODE_D, device=dev, dtype=torch.float16, generator=g)
+              for _ in range(2))
+    q = torch.randn(DECODE_B, DECODE_HQ, DECODE_D, device=dev, dtype=torch.float16, generator=g)
+    cu = torch.arange(DECODE_B + 1, dtype=torch.int32, device=dev)
+    sk = torch.full((DECODE_B,), DECODE_CTX, dtype=torch.int32, device=dev)
+    steps = max(1, min(args.steps, 50))
+
+    def step():
+        fa.scaled_dot_product_attention_paged(q, kc, vc, table, cu, sk, 1, DECODE_CTX, is_causal=True,
+                                              enable_gqa=True)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    kv_bytes = 2 * DECODE_B * DECODE_CTX * DECODE_HKV * DECODE_D * 2
+    peaks = read_peaks()
+    gbs = kv_bytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "workload": "decode", "sequences": DECODE_B, "context": DECODE_CTX, "query_heads": DECODE_HQ,
+        "kv_heads": DECODE_HKV, "head_dim": DECODE_D, "page_size": DECODE_PAGE, "dtype": "fp16",
+        "data": "synthetic: seeded N(0,1) cache and queries, shuffled page table",
+        "ms_per_step": round(ms, 4), "kv_bytes_per_step": kv_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"]},
+        "note": "L2 (126 MB) is smaller than the 512 MiB cache; no flush needed",
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -749,10 +810,11 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--deterministic", action="store_true",
                     help="time the bitwise-reproducible backward (separate dQ and dK/dV kernels)")
-    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen", "decode"], default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
                          "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel; "
-                         "varlen: a packed batch of ragged sequences beside its padded dense equivalent")
+                         "varlen: a packed batch of ragged sequences beside its padded dense equivalent; "
+                         "decode: one query per sequence over a paged K/V cache")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -767,6 +829,8 @@ def main() -> None:
         run_sweep(args)
     elif args.workload == "varlen":
         run_varlen(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -179,3 +179,25 @@ def test_paged_matches_varlen_when_pages_are_contiguous():
     o_v, lse_v = fa.varlen_attention_forward(q, k, v, cu, cu, 300, 300, True, d ** -0.5)
     assert torch.equal(o_p, o_v)
     assert torch.equal(lse_p, lse_v)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hq,hkv,nq", [(16, 2, 17), (32, 1, 5), (64, 1, 1), (8, 4, 100)])
+def test_gqa_packed_forward_dense(hq, hkv, nq):
+    """Short query sides with GQA run the packed forward (a query tile holds
+    the group's heads); causal with Nq != Nk (top-left, the dense
+    convention) and non-causal, against float64."""
+    g = torch.Generator(device="cpu").manual_seed(hq + nq)
+    d, nk = 64, 700
+    q = torch.randn(2, hq, nq, d, generator=g).half()
+    k = torch.randn(2, hkv, nk, d, generator=g).half()
+    v = torch.randn(2, hkv, nk, d, generator=g).half()
+    for causal in (False, True):
+        o, lse = fa.attention_forward(q.cuda(), k.cuda(), v.cuda(), causal, d ** -0.5)
+        ref = orc.sdpa_reference(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal,
+                                 scale=d ** -0.5)
+        assert _maxabs(o.float().cpu(), ref["o"]) <= 2e-3
+        finite = np.isfinite(ref["lse2"])
+        lse = lse.cpu().numpy()
+        assert np.array_equal(np.isfinite(lse), finite)
+        assert _maxabs(lse[finite], ref["lse2"][finite]) <= 1e-3

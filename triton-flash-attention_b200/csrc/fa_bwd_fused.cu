@@ -44,6 +44,9 @@ constexpr int BM = 128;  // keys per tile
 constexpr int BQ = 128;  // query rows per item
 constexpr int NUM_THREADS = 512;
 constexpr int POLY_MASK = 0;  // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2 (none: measured fastest)
+constexpr int POLY_MASK_D32 = 0;  // the same at D = 32
+template <int D>
+constexpr int poly_mask() { return D == 32 ? POLY_MASK_D32 : POLY_MASK; }
 // Registers per thread: launched at 128 (512 threads); warps 0-3 drop to
 // CTRL_REGS and the dQ warpgroup to DQ_REGS, and the two elementwise
 // warpgroups rise to SOFT_REGS (ptxas -v shows no spills at this split).
@@ -491,8 +494,8 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
               const int c = c4 * 4;
               const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
               const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
-              const uint64_t e01 = ((2 * c4) & 7) < POLY_MASK ? exp2_poly2(x01) : exp2_mufu2(x01);
-              const uint64_t e23 = ((2 * c4 + 1) & 7) < POLY_MASK ? exp2_poly2(x23) : exp2_mufu2(x23);
+              const uint64_t e01 = ((2 * c4) & 7) < poly_mask<D>() ? exp2_poly2(x01) : exp2_mufu2(x01);
+              const uint64_t e23 = ((2 * c4 + 1) & 7) < poly_mask<D>() ? exp2_poly2(x23) : exp2_mufu2(x23);
               pk_p[c4 * 2] = pack2_f2<DT>(e01);
               pk_p[c4 * 2 + 1] = pack2_f2<DT>(e23);
             }

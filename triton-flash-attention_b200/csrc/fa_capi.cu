@@ -55,7 +55,7 @@ bool supported_d(int D) { return D == 32 || D == 64 || D == 128; }
 // swizzle the kernels' shared memory descriptors assume (128 B for D >= 64,
 // 64 B for D = 32).
 int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, const int64_t* strides, int rows,
-             int dtype) {
+             int dtype, int heads_per_box = 1) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DRIVER;
   if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
@@ -64,7 +64,7 @@ int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, cons
   const int box_d = D >= 64 ? 64 : 32;
   cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
   cuuint64_t gstr[3] = {cuuint64_t(strides[2]) * 2, cuuint64_t(strides[1]) * 2, cuuint64_t(strides[0]) * 2};
-  cuuint32_t box[4] = {cuuint32_t(box_d), cuuint32_t(rows), 1, 1};
+  cuuint32_t box[4] = {cuuint32_t(box_d), cuuint32_t(rows), cuuint32_t(heads_per_box), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType ty = dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = enc(map, ty, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
@@ -109,7 +109,27 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.block_table = nullptr;
   s.bt_stride = 0;
   s.page_size = 0;
+  s.pack_g = 0;
   return s;
+}
+
+// GQA packing of the forward (AttnShape::pack_g): a query tile holds the G
+// query heads of a K/V head x 128 / G rows, so K/V is read once per group.
+// Worth it when the query side is short -- decode and short chunks, where
+// one unit then covers all of a sequence's queries -- and not for long
+// causal queries, whose diagonal tiles it would make mostly masked.
+int gqa_pack(int Hq, int Hkv, int max_q) {
+  const int G = Hq / Hkv;
+  if (G < 2 || G > 64 || (G & (G - 1)) != 0) return 0;
+  return max_q * G <= 256 ? G : 0;
+}
+
+// The forward's query tensor map: a 128-row box of one head, or with GQA
+// packing 128 / G rows of G consecutive heads.
+int make_q_map(CUtensorMap* map, const void* q, int B, int H, int N, int D, const int64_t* strides, int dtype,
+               int pack) {
+  return pack > 1 ? make_map(map, q, B, H, N, D, strides, 128 / pack, dtype, pack)
+                  : make_map(map, q, B, H, N, D, strides, 128, dtype);
 }
 
 int fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
@@ -122,10 +142,12 @@ int fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse, i
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
   FwdArgs a;
-  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, 128, dtype))) return rc;
+  const int pack = gqa_pack(Hq, Hkv, Nq);
+  if ((rc = make_q_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, dtype, pack))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, 128, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, 128, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
+  a.shape.pack_g = pack;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = o_strides[0];
@@ -347,10 +369,12 @@ int fwd_varlen_impl(const void* q, const void* k, const void* v, void* o, float*
   const PackedStrides sq(total_q, Hq, D), sk(total_k, Hkv, D);
   if (!out_strides_ok(o, sq.v, 2)) return FA_ERR_MISALIGNED;
   FwdArgs a;
-  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, 128, dtype))) return rc;
+  const int pack = gqa_pack(Hq, Hkv, max_q);
+  if ((rc = make_q_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dtype, pack))) return rc;
   if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, 128, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, 128, dtype))) return rc;
   a.shape = varlen_shape(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, softmax_scale, causal);
+  a.shape.pack_g = pack;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = 0;
@@ -448,7 +472,8 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   int rc;
   FwdArgs a;
   const int pr = page_size < 128 ? page_size : 128;
-  if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, 128, dtype))) return rc;
+  const int pack = gqa_pack(Hq, Hkv, max_q);
+  if ((rc = make_q_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dtype, pack))) return rc;
   if ((rc = make_map(&a.tmap_k, k_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
   a.shape = make_shape(B, Hq, Hkv, max_q, max_k, softmax_scale, causal, 0, 0);
@@ -458,6 +483,7 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   a.shape.block_table = block_table;
   a.shape.bt_stride = bt_stride;
   a.shape.page_size = page_size;
+  a.shape.pack_g = pack;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = 0;

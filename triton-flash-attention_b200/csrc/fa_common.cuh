@@ -64,6 +64,10 @@ struct AttnShape {
   const int* seqlen_k;
   const int* block_table;
   int bt_stride, page_size;
+  // Forward only: when pack_g > 1, a 128-row query tile holds pack_g query
+  // heads of one K/V head (a GQA group) x 128 / pack_g query rows, so each
+  // K/V tile is read once for the whole group (decode, short queries).
+  int pack_g;
 };
 
 // Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of

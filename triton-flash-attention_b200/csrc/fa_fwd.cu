@@ -47,6 +47,9 @@ constexpr int NUM_THREADS = 384;
 constexpr bool TURNS = true;  // separate-P layout: the softmax warpgroups take turns at their exponentials
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
 constexpr int POLY_MASK = 0;               // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
+constexpr int POLY_MASK_D32 = 0;           // the same at D = 32 (half the MMA work per exponential)
+template <int D>
+constexpr int poly_mask() { return D == 32 ? POLY_MASK_D32 : POLY_MASK; }
 // Registers per thread: launched at 168 (384 threads); the control
 // warpgroup (warps 0-3) drops to CTRL_REGS and the two softmax warpgroups
 // rise to SOFT_REGS.  128 * CTRL_REGS + 256 * SOFT_REGS must not exceed
@@ -95,25 +98,38 @@ struct Cfg {
 
 // A work unit: QT query tiles of one (batch, head); n_kv[t] key tiles each.
 // Units are numbered late query blocks first (the heavy ones under a causal
-// mask).
+// mask).  With GQA packing (shp.pack_g = G > 1) a unit is one (batch, K/V
+// head) instead: its tiles hold the G query heads of the group x R = 128 / G
+// query rows (tile row = g * R + r), h is the group's first query head, and
+// row0 / rows count query rows per head.
 struct Unit {
-  int b, h, kvh, row0, n_kv[QT], n_max;
+  int b, h, kvh, row0, rows, n_kv[QT], n_max;
   Seq sq;
 };
+template <bool PACK>
 __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
-  const int BH = shp.B * shp.Hq;
-  const int n_qblk = (shp.Nq + QT * BM - 1) / (QT * BM);
+  const int G = PACK ? shp.pack_g : 1;
+  const int rows = BM / G;  // query rows per head in a tile
+  const int BH = shp.B * (G > 1 ? shp.Hkv : shp.Hq);
+  const int n_qblk = (shp.Nq + QT * rows - 1) / (QT * rows);
   Unit w;
   const int bh = u % BH;
-  w.b = bh / shp.Hq;
-  w.h = bh % shp.Hq;
-  w.kvh = w.h / (shp.Hq / shp.Hkv);
-  w.row0 = (n_qblk - 1 - u / BH) * QT * BM;
+  if (PACK) {
+    w.b = bh / shp.Hkv;
+    w.kvh = bh % shp.Hkv;
+    w.h = w.kvh * G;
+  } else {
+    w.b = bh / shp.Hq;
+    w.h = bh % shp.Hq;
+    w.kvh = w.h / (shp.Hq / shp.Hkv);
+  }
+  w.rows = rows;
+  w.row0 = (n_qblk - 1 - u / BH) * QT * rows;
   w.sq = seq_of(shp, w.b);
   w.n_max = 0;
 #pragma unroll
   for (int t = 0; t < QT; ++t) {
-    w.n_kv[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * BM, BM, BN);
+    w.n_kv[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * rows, rows, BN);
     w.n_max = w.n_kv[t] > w.n_max ? w.n_kv[t] : w.n_max;
   }
   return w;
@@ -121,7 +137,7 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
 
 }  // namespace fwd
 
-template <int D, int DT>
+template <int D, int DT, bool PACK>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
@@ -220,7 +236,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of(shp, ui);
+          const Unit w = unit_of<PACK>(shp, ui);
           if (w.n_max == 0) continue;
           if (is_k) {
             const int qb = uc % C::QB;
@@ -232,7 +248,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
               if (w.n_kv[t] == 0) continue;
               for (int bx = 0; bx < G::NBOX; ++bx)
                 tma_load_4d(smem + C::OFF_Q + qb * C::Q_UNIT_BYTES + t * C::Q_TILE_BYTES + bx * BM * G::SW, &tmap_q,
-                            q_full + qb, bx * G::BOX, w.sq.q0 + w.row0 + t * BM, w.h, w.sq.tb);
+                            q_full + qb, bx * G::BOX, w.sq.q0 + w.row0 + t * w.rows, w.h, w.sq.tb);
             }
           }
           ++uc;
@@ -286,7 +302,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of(shp, ui);
+          const Unit w = unit_of<PACK>(shp, ui);
           if (w.n_max == 0) continue;
           const int qb = uc % C::QB;
           if (!mbar_wait(q_full + qb, uint32_t(uc / C::QB) & 1, ctl, 10)) { ok = false; break; }
@@ -419,8 +435,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int ui = snake_unit(cta, k, n_cta, n_units);
       if (ui >= n_units) break;
-      const Unit w = unit_of(shp, ui);
-      const int r = w.row0 + t * BM + row_local;  // query row
+      const Unit w = unit_of<PACK>(shp, ui);
+      // query row (within the batch) and head of this thread's tile row
+      const int r = w.row0 + t * w.rows + (PACK ? row_local % w.rows : row_local);
+      const int hq = w.h + (PACK ? row_local / w.rows : 0);
       const int nt = w.n_kv[t];
       // last visible key column of this row (local key index)
       int lim = w.sq.nk - 1;
@@ -480,7 +498,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             const int c0 = cc * 32 + 2 * i;
             const uint64_t x = ffma2(f2pack(s[c0], s[c0 + 1]), c2x2, nb2);
             // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
-            const uint64_t e = (i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x);
+            const uint64_t e = (i & 7) < poly_mask<D>() ? exp2_poly2(x) : exp2_mufu2(x);
             packed[i] = pack2_f2<DT>(e);
             sum2[i & 3] = fadd2(sum2[i & 3], e);
           }
@@ -550,7 +568,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       const bool row_ok = r < w.sq.nq;
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)w.h * o_sh + (long long)(w.sq.q0 + r) * o_sn;
+      uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)hq * o_sh + (long long)(w.sq.q0 + r) * o_sn;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
@@ -579,7 +597,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       if (nt > 0) ++oc;
       if (row_ok) {
-        lse_ptr[row_stat_index(shp, w.sq, w.b, w.h, r)] = l > 0.f ? m + lg2(l) : -INFINITY;
+        lse_ptr[row_stat_index(shp, w.sq, w.b, hq, r)] = l > 0.f ? m + lg2(l) : -INFINITY;
       }
     }
   }
@@ -592,11 +610,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT>
+template <int D, int DT, bool PACK>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D, DT>;
+  auto kern = fa_fwd_kernel<D, DT, PACK>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -608,8 +626,10 @@ int launch_fwd_t(const FwdArgs& a) {
   if (!regs_ok) return FA_ERR_LAUNCH;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return FA_ERR_LAUNCH;
-  const int n_qblk = (a.shape.Nq + fwd::QT * fwd::BM - 1) / (fwd::QT * fwd::BM);
-  const int n_units = n_qblk * a.shape.B * a.shape.Hq;
+  const int G = a.shape.pack_g > 1 ? a.shape.pack_g : 1;
+  const int rows = fwd::QT * (fwd::BM / G);
+  const int n_qblk = (a.shape.Nq + rows - 1) / rows;
+  const int n_units = n_qblk * a.shape.B * (G > 1 ? a.shape.Hkv : a.shape.Hq);
   const int sms = device_sm_count();
   const int n_cta = n_units < sms ? n_units : sms;
   kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, static_cast<uint16_t*>(a.o),
@@ -617,11 +637,17 @@ int launch_fwd_t(const FwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+// GQA-packed and plain query tiles are separate instantiations.
+template <int D, int DT>
+int launch_fwd_l(const FwdArgs& a) {
+  return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true>(a) : launch_fwd_t<D, DT, false>(a);
+}
+
 int launch_fwd(const FwdArgs& a, int D) {
   switch (D) {
-    case 32: return a.dtype == DT_BF16 ? launch_fwd_t<32, DT_BF16>(a) : launch_fwd_t<32, DT_F16>(a);
-    case 64: return a.dtype == DT_BF16 ? launch_fwd_t<64, DT_BF16>(a) : launch_fwd_t<64, DT_F16>(a);
-    case 128: return a.dtype == DT_BF16 ? launch_fwd_t<128, DT_BF16>(a) : launch_fwd_t<128, DT_F16>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_fwd_l<32, DT_BF16>(a) : launch_fwd_l<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_fwd_l<64, DT_BF16>(a) : launch_fwd_l<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_fwd_l<128, DT_BF16>(a) : launch_fwd_l<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }
