@@ -44,7 +44,7 @@ constexpr int BM = 128;  // keys per tile
 constexpr int BQ = 128;  // query rows per item
 constexpr int NUM_THREADS = 512;
 constexpr int POLY_MASK = 0;  // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2 (none: measured fastest)
-constexpr int POLY_MASK_D32 = 0;  // the same at D = 32
+constexpr int POLY_MASK_D32 = 2;  // the same at D = 32 (measured)
 template <int D>
 constexpr int poly_mask() { return D == 32 ? POLY_MASK_D32 : POLY_MASK; }
 // Registers per thread: launched at 128 (512 threads); warps 0-3 drop to
