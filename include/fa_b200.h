@@ -203,11 +203,14 @@ FA_API int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, int H,
  * (Hq, total_q) fp32.  Causal masking is per batch and top-left aligned
  * (query i of a batch sees its keys j <= i), as in the dense calls.  A
  * batch may be empty; a query row with no visible key gets o = 0 and
- * lse = -inf.  total_q and total_k must be positive. */
+ * lse = -inf.  total_q and total_k must be positive.  window > 0 (causal
+ * only) is a sliding window: a query sees only the window keys ending at
+ * its own position (key j is visible iff pos - window < j <= pos); 0 means
+ * no window. */
 FA_API int fa_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
                   const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                   int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                  float softmax_scale, int causal, void* stream);
+                  float softmax_scale, int causal, int window, void* stream);
 /* The whole varlen backward: delta (caller's (Hq, total_q) fp32 buffer) and
  * dq, dk, dv.  D <= 64 with deterministic == 0 runs the fused pass and needs
  * dq_accum, a caller's (Hq, total_q, D) fp32 scratch buffer (zeroed here);
@@ -217,16 +220,16 @@ FA_API int fa_bwd_varlen(const void* q, const void* k, const void* v, const void
                   const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
                   const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                   int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                  float softmax_scale, int causal, int deterministic, void* stream);
+                  float softmax_scale, int causal, int window, int deterministic, void* stream);
 FA_API int fa_fwd_varlen_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
                        const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                        int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                       float softmax_scale, int causal, void* stream);
+                       float softmax_scale, int causal, int window, void* stream);
 FA_API int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
                        const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
                        const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                        int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                       float softmax_scale, int causal, int deterministic, void* stream);
+                       float softmax_scale, int causal, int window, int deterministic, void* stream);
 
 /* Forward over a paged K/V cache.  No counterpart in the reference (it has
  * no cache); this is the layout serving engines keep keys and values in.
@@ -240,17 +243,18 @@ FA_API int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const
  * batch with nq queries and nk keys sees keys j <= i + nk - nq.  Cache rows
  * past a batch's length (in its last page) must hold finite values: their
  * keys are masked, but their values still meet a zero weight in the P V
- * product.  Forward only. */
+ * product.  window as in fa_fwd_varlen (positions bottom-right aligned).
+ * Forward only. */
 FA_API int fa_fwd_paged(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                  const int* cu_seqlens_q, const int* seqlens_k, const int* block_table,
                  int B, int Hq, int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q,
                  int num_pages, int page_size, int max_pages_per_seq, int D,
-                 float softmax_scale, int causal, void* stream);
+                 float softmax_scale, int causal, int window, void* stream);
 FA_API int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                       const int* cu_seqlens_q, const int* seqlens_k, const int* block_table,
                       int B, int Hq, int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q,
                       int num_pages, int page_size, int max_pages_per_seq, int D,
-                      float softmax_scale, int causal, void* stream);
+                      float softmax_scale, int causal, int window, void* stream);
 
 /* Size of the scratch array fa_bwd_fused_noalloc uses: 32 MiB per device. */
 #define FA_NOALLOC_SCRATCH_BYTES (32u << 20)

@@ -55,19 +55,24 @@ def _reduce_kv(dx: np.ndarray, hkv: int) -> np.ndarray:
     return dx.reshape(b, hkv, g, n, d).sum(axis=2)
 
 
-def causal_mask(nq: int, nk: int, q_offset: int = 0, k_offset: int = 0) -> np.ndarray:
+def causal_mask(nq: int, nk: int, q_offset: int = 0, k_offset: int = 0, window: int = 0) -> np.ndarray:
     """True where a key is visible: key position <= query position.
 
     With zero offsets and nq == nk this is the reference's ``row >= col``
     (attention.py:65, 300, 343), the same as SDPA ``is_causal`` top-left
-    alignment.  The offsets give the global positions of a sequence chunk."""
+    alignment.  The offsets give the global positions of a sequence chunk.
+    ``window`` > 0 adds a sliding window (no counterpart in the reference):
+    only the ``window`` keys ending at the query's position are visible."""
     qi = np.arange(nq)[:, None] + q_offset
     kj = np.arange(nk)[None, :] + k_offset
-    return kj <= qi
+    m = kj <= qi
+    if window > 0:
+        m &= kj > qi - window
+    return m
 
 
 def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None,
-                   q_offset: int = 0, k_offset: int = 0):
+                   q_offset: int = 0, k_offset: int = 0, window: int = 0):
     """Dense attention in float64 (the math behind attention.py:774-786).
 
     Returns a dict with ``o``, ``lse`` (natural log), ``lse2`` (base-2 log of
@@ -86,7 +91,7 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
     ve = _expand_kv(v, hq)
     s = np.einsum("bhqd,bhkd->bhqk", q, ke) * scale
     if causal:
-        m = causal_mask(nq, nk, q_offset, k_offset)
+        m = causal_mask(nq, nk, q_offset, k_offset, window)
         s = np.where(m[None, None], s, -np.inf)
     mx = s.max(axis=-1, keepdims=True)
     mx_safe = np.where(np.isfinite(mx), mx, 0.0)
@@ -109,7 +114,8 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
     return out
 
 
-def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | None = None, do=None):
+def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | None = None, do=None,
+                          window: int = 0):
     """Packed variable-length attention in float64: ``q`` (total_q, Hq, D),
     ``k``/``v`` (total_k, Hkv, D), prefix sums ``cu_q``/``cu_k``; each
     sequence is dense attention over its own rows (``sdpa_reference``, causal
@@ -133,7 +139,7 @@ def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | N
             continue  # no query rows, or no keys: o = 0, lse = -inf, no gradient
         to4 = lambda x: x.transpose(1, 0, 2)[None]  # (n, H, D) -> (1, H, n, D)
         r = sdpa_reference(to4(q[q0:q1]), to4(k[k0:k1]), to4(v[k0:k1]), causal=causal, scale=scale,
-                           do=None if do is None else to4(do[q0:q1]))
+                           do=None if do is None else to4(do[q0:q1]), window=window)
         out["o"][q0:q1] = r["o"][0].transpose(1, 0, 2)
         out["lse2"][:, q0:q1] = r["lse2"][0]
         if do is not None:
@@ -144,7 +150,7 @@ def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | N
 
 
 def sdpa_paged_reference(q, k_cache, v_cache, block_table, cu_q, seqlens_k, *, causal: bool,
-                         scale: float | None = None):
+                         scale: float | None = None, window: int = 0):
     """Forward over a paged K/V cache in float64: sequence b's keys are rows
     0..seqlens_k[b]-1 of its pages block_table[b, :] laid end to end; its
     queries are the last nq positions (causal bottom-right aligned:
@@ -167,7 +173,8 @@ def sdpa_paged_reference(q, k_cache, v_cache, block_table, cu_q, seqlens_k, *, c
         k = k_cache[pages].reshape(-1, *k_cache.shape[2:])[:nk]
         v = v_cache[pages].reshape(-1, *v_cache.shape[2:])[:nk]
         to4 = lambda x: x.transpose(1, 0, 2)[None]
-        r = sdpa_reference(to4(q[q0:q1]), to4(k), to4(v), causal=causal, scale=scale, q_offset=nk - nq)
+        r = sdpa_reference(to4(q[q0:q1]), to4(k), to4(v), causal=causal, scale=scale, q_offset=nk - nq,
+                           window=window)
         out["o"][q0:q1] = r["o"][0].transpose(1, 0, 2)
         out["lse2"][:, q0:q1] = r["lse2"][0]
     return out

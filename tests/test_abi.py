@@ -87,21 +87,28 @@ def test_fused_backward_validation_without_cuda():
 def test_varlen_and_paged_entry_points_reject_before_any_cuda_call():
     lib = _abi.lib()
     p = 16  # a non-null, 16-byte aligned stand-in pointer; nothing is dereferenced on these paths
-    # fa_fwd_varlen(q, k, v, o, lse, cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D, scale, causal, stream)
-    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 2, 64, 64, 100, 100, 48, 0.1, 1, None) \
+    # fa_fwd_varlen(q, k, v, o, lse, cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D, scale, causal,
+    #               window, stream)
+    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 2, 64, 64, 100, 100, 48, 0.1, 1, 0, None) \
         == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
-    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 0, 4, 2, 64, 64, 100, 100, 64, 0.1, 1, None) == _abi.FA_ERR_BAD_SHAPE
-    assert lib.fa_fwd_varlen(p, p, p, p, p, None, p, 2, 4, 2, 64, 64, 100, 100, 64, 0.1, 1, None) \
+    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 0, 4, 2, 64, 64, 100, 100, 64, 0.1, 1, 0, None) \
         == _abi.FA_ERR_BAD_SHAPE
-    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 3, 64, 64, 100, 100, 64, 0.1, 1, None) \
+    assert lib.fa_fwd_varlen(p, p, p, p, p, None, p, 2, 4, 2, 64, 64, 100, 100, 64, 0.1, 1, 0, None) \
+        == _abi.FA_ERR_BAD_SHAPE
+    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 3, 64, 64, 100, 100, 64, 0.1, 1, 0, None) \
+        == _abi.FA_ERR_BAD_SHAPE
+    # a sliding window needs the causal mask and a non-negative size
+    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 2, 64, 64, 100, 100, 64, 0.1, 0, 16, None) \
+        == _abi.FA_ERR_BAD_SHAPE
+    assert lib.fa_fwd_varlen(p, p, p, p, p, p, p, 2, 4, 2, 64, 64, 100, 100, 64, 0.1, 1, -1, None) \
         == _abi.FA_ERR_BAD_SHAPE
     # fa_bwd_varlen: the fused pass (D = 64, deterministic = 0) needs the dQ accumulator
     assert lib.fa_bwd_varlen(p, p, p, p, p, p, p, p, p, p, None, p, p, 2, 4, 2, 64, 64, 100, 100, 64,
-                             0.1, 1, 0, None) == _abi.FA_ERR_BAD_SHAPE
+                             0.1, 1, 0, 0, None) == _abi.FA_ERR_BAD_SHAPE
     # fa_fwd_paged(q, kc, vc, o, lse, cu_q, seqlens_k, table, B, Hq, Hkv, max_q, max_k, total_q,
-    #              num_pages, page_size, max_pages_per_seq, D, scale, causal, stream)
+    #              num_pages, page_size, max_pages_per_seq, D, scale, causal, window, stream)
     for page in (12, 8, 0, 48):
-        assert lib.fa_fwd_paged(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, page, 5, 64, 0.1, 1, None) \
+        assert lib.fa_fwd_paged(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, page, 5, 64, 0.1, 1, 0, None) \
             == _abi.FA_ERR_BAD_SHAPE, page
-    assert lib.fa_fwd_paged(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, 64, 5, 96, 0.1, 1, None) \
+    assert lib.fa_fwd_paged(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, 64, 5, 96, 0.1, 1, 0, None) \
         == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM

@@ -201,3 +201,20 @@ def test_gqa_packed_forward_dense(hq, hkv, nq):
         lse = lse.cpu().numpy()
         assert np.array_equal(np.isfinite(lse), finite)
         assert _maxabs(lse[finite], ref["lse2"][finite]) <= 1e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("lens_q,window", [([1, 1, 1], 100), ([200, 37], 64)])
+def test_paged_sliding_window(lens_q, window):
+    """Sliding window over a paged cache (bottom-right positions): decode and
+    a prefill chunk, against float64."""
+    lens_k = [1000, 300, 77][: len(lens_q)]
+    q, kc, vc, table, cu_q, seqlens_k = _case(lens_q, lens_k, 64, 4, 2, 64, seed=window)
+    with torch.no_grad():
+        o, lse = fa.paged_attention_forward(
+            q.cuda(), kc.cuda(), vc.cuda(), torch.from_numpy(table).cuda(), torch.from_numpy(cu_q).cuda(),
+            torch.from_numpy(seqlens_k).cuda(), max(lens_q), max(lens_k), True, 64 ** -0.5, window)
+    ref = orc.sdpa_paged_reference(q.float().numpy(), kc.float().numpy(), vc.float().numpy(), table, cu_q,
+                                   seqlens_k, causal=True, window=window)
+    assert _maxabs(o.float().cpu(), ref["o"]) <= 2e-3
+    assert _maxabs(lse.cpu().numpy(), ref["lse2"]) <= 1e-3

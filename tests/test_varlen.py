@@ -183,3 +183,60 @@ def test_varlen_equal_lengths_match_dense_forward():
     o_var, lse_var = fa.varlen_attention_forward(pack(q), pack(k), pack(v), cu, cu, n, n, True, d ** -0.5)
     assert torch.equal(o_var, pack(o_dense))
     assert torch.equal(lse_var, lse_dense.transpose(0, 1).reshape(h, b * n))
+
+
+# ---------------------------------------------------------------- sliding window
+def test_oracle_window_mask():
+    m = orc.causal_mask(5, 5, window=2)
+    assert m.tolist() == [[i - 2 < j <= i for j in range(5)] for i in range(5)]
+
+
+def test_window_validation():
+    q = torch.zeros(4, 2, 64, dtype=torch.float16)
+    cu = torch.tensor([0, 4], dtype=torch.int32)
+    with pytest.raises(ValueError, match="is_causal"):
+        fa.scaled_dot_product_attention_varlen(q, q, q, cu, cu, 4, 4, window_size=2)
+    with pytest.raises(ValueError, match="positive int"):
+        fa.scaled_dot_product_attention_varlen(q, q, q, cu, cu, 4, 4, is_causal=True, window_size=0)
+
+
+WINDOW_CASES = [
+    # lens, hq, hkv, d, window
+    ([1, 17, 300, 129, 600], 2, 2, 64, 100),
+    ([1, 17, 300, 129, 600], 2, 2, 64, 128),
+    ([257, 1000], 4, 2, 32, 1),
+    ([700, 64], 2, 1, 128, 200),
+    ([1000, 513], 2, 2, 64, 333),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", WINDOW_CASES)
+def test_varlen_sliding_window_against_float64(case):
+    """Causal sliding window: forward (O, lse2) and both backward paths
+    (fused at D <= 64 and the deterministic split) against float64."""
+    lens, hq, hkv, d, window = case
+    cu = _cu(lens)
+    q, k, v, do = _inputs(lens, lens, hq, hkv, d, seed=window + d)
+    ref = orc.sdpa_varlen_reference(q.float().numpy(), k.float().numpy(), v.float().numpy(), cu, cu,
+                                    causal=True, do=do.float().numpy(), window=window)
+    cq = torch.from_numpy(cu).cuda()
+    for det in (False, True):
+        prev = torch.are_deterministic_algorithms_enabled()
+        torch.use_deterministic_algorithms(det)
+        try:
+            qc, kc, vc = (t.cuda().requires_grad_() for t in (q, k, v))
+            o = fa.scaled_dot_product_attention_varlen(qc, kc, vc, cq, cq, max(lens), max(lens), is_causal=True,
+                                                       enable_gqa=hq != hkv, window_size=window)
+            grads = torch.autograd.grad(o, (qc, kc, vc), do.cuda())
+            torch.cuda.synchronize()
+        finally:
+            torch.use_deterministic_algorithms(prev)
+        assert _maxabs(o.detach().float().cpu(), ref["o"]) <= 2e-3
+        for name, t in zip(("dq", "dk", "dv"), grads):
+            err = _maxabs(t.float().cpu(), ref[name])
+            assert err <= 1e-2, (name, det, err)
+    _, lse = fa.varlen_attention_forward(q.cuda(), k.cuda(), v.cuda(), cq, cq, max(lens), max(lens), True,
+                                         d ** -0.5, window)
+    assert _maxabs(lse.cpu().numpy(), ref["lse2"]) <= 1e-3
+    assert fa._abi.device_status() == 0

@@ -48,10 +48,10 @@ SIGNATURES = {
 # the bf16 twins take the same arguments
 SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in list(SIGNATURES)})
 SIGNATURES.update({
-    "fa_fwd_varlen": (_i, [_p] * 7 + [_i] * 8 + [_f, _i, _p]),
-    "fa_bwd_varlen": (_i, [_p] * 13 + [_i] * 8 + [_f, _i, _i, _p]),
+    "fa_fwd_varlen": (_i, [_p] * 7 + [_i] * 8 + [_f, _i, _i, _p]),
+    "fa_bwd_varlen": (_i, [_p] * 13 + [_i] * 8 + [_f, _i, _i, _i, _p]),
 })
-SIGNATURES["fa_fwd_paged"] = (_i, [_p] * 8 + [_i] * 10 + [_f, _i, _p])
+SIGNATURES["fa_fwd_paged"] = (_i, [_p] * 8 + [_i] * 10 + [_f, _i, _i, _p])
 SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in ("fa_fwd_varlen", "fa_bwd_varlen", "fa_fwd_paged")})
 SIGNATURES.update({
     "fa_bwd_fused_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,

@@ -67,9 +67,10 @@ struct Cfg {
 // they see.  Tiles are numbered late query tiles first (the heavy ones under
 // a causal mask).
 struct Tile {
-  int b, h, kvh, row0, n_kv;
+  int b, h, kvh, row0, kt0, n_kv;  // key tiles kt0 .. kt0 + n_kv - 1
   Seq sq;
 };
+template <bool WIN>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   const int BH = shp.B * shp.Hq;
   const int n_qt = (shp.Nq + BM - 1) / BM;
@@ -80,12 +81,15 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
   w.kvh = w.h / (shp.Hq / shp.Hkv);
   w.row0 = (n_qt - 1 - t / BH) * BM;
   w.sq = seq_of(shp, w.b);
-  w.n_kv = kv_tiles_for_rows(shp, w.sq, w.row0, BM, BN);
+  const int end = kv_tiles_for_rows(shp, w.sq, w.row0, BM, BN);
+  const int first = WIN ? kv_first_tile(shp, w.sq, w.row0, BN) : 0;  // > 0 only under a sliding window
+  w.kt0 = first < end ? first : 0;
+  w.n_kv = first < end ? end - first : 0;
   return w;
 }
 }  // namespace bdqw
 
-template <int D, int DT>
+template <int D, int DT, bool WIN>
 __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     fa_bwd_dq_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       for (int k = 0; ok; ++k) {
         const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
-        const Tile w = tile_of(shp, t);
+        const Tile w = tile_of<WIN>(shp, t);
         if (w.n_kv == 0) continue;
         const int tb = tcn % C::QB;
         if (tcn >= C::QB && !mbar_wait(q_empty + tb, uint32_t(tcn / C::QB - 1) & 1, ctl, 130)) break;
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           mbar_arrive_expect_tx(kv_full + s, C::KV_TILE_BYTES);
           for (int bx = 0; bx < G::NBOX; ++bx)
             tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s, bx * G::BOX,
-                        w.sq.k0 + j * BN, w.kvh, w.sq.tb);
+                        w.sq.k0 + (w.kt0 + j) * BN, w.kvh, w.sq.tb);
         }
       }
       for (int i = (tcn > C::QB ? tcn - C::QB : 0); i < tcn; ++i)
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       for (int k = 0; ok; ++k) {
         const int t = snake_unit(cta, k, n_cta, n_tiles);
         if (t >= n_tiles) break;
-        const int n_kv = tile_of(shp, t).n_kv;
+        const int n_kv = tile_of<WIN>(shp, t).n_kv;
         if (n_kv == 0) continue;
         const int tb = tcn % C::QB;
         if (!mbar_wait(q_full + tb, uint32_t(tcn / C::QB) & 1, ctl, 140)) { ok = false; break; }
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       }
     };
     int t_cur = snake_unit(cta, 0, n_cta, n_tiles);
-    Tile wt = tile_of(shp, t_cur < n_tiles ? t_cur : 0);
+    Tile wt = tile_of<WIN>(shp, t_cur < n_tiles ? t_cur : 0);
     float lse_n = INFINITY, delta_n = 0.f;
     if (t_cur < n_tiles) row_vals(wt, lse_n, delta_n);
     int gj = 0, tcn = 0;
@@ -301,14 +305,16 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       const float lse_r = lse_n, delta_r = delta_n;
       t_cur = snake_unit(cta, k + 1, n_cta, n_tiles);
       if (t_cur < n_tiles) {
-        wt = tile_of(shp, t_cur);
+        wt = tile_of<WIN>(shp, t_cur);
         row_vals(wt, lse_n, delta_n);
       }
       const int r = cur.row0 + wq * 32 + lane;
       int lim = cur.sq.nk - 1;
+      long long lo = 0;  // first visible key under a sliding window
       if (shp.causal) {
         const long long c = (long long)r + shp.q_off - shp.k_off;
         lim = c < lim ? int(c) : lim;
+        if (WIN) lo = c - shp.window + 1;
       }
       const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
       const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
@@ -319,10 +325,16 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * w);
         float sv[64];
         tmem_ld64(tS, sv);
-        const int lim_j = lim - j * BN - 64 * w;  // last visible column of this half
+        const int key0 = (cur.kt0 + j) * BN + 64 * w;  // key index of this half's column 0
+        const int lim_j = lim - key0;                   // last visible column of this half
         if (lim_j < 63) {
 #pragma unroll
           for (int c = 0; c < 64; ++c) sv[c] = c <= lim_j ? sv[c] : -INFINITY;
+        }
+        if (WIN && lo > key0) {
+          const long long lo_j = lo - key0;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) sv[c] = c >= lo_j ? sv[c] : -INFINITY;
         }
         uint32_t pk_p[32];
 #pragma unroll
@@ -409,10 +421,10 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT>
+template <int D, int DT, bool WIN>
 int launch_bwd_dq_wide_t(const BwdArgs& a) {
   using C = bdqw::Cfg<D>;
-  auto kern = fa_bwd_dq_wide_kernel<D, DT>;
+  auto kern = fa_bwd_dq_wide_kernel<D, DT, WIN>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
@@ -425,11 +437,17 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+// Sliding-window and plain masks are separate instantiations.
+template <int D, int DT>
+int launch_bwd_dq_l(const BwdArgs& a) {
+  return a.shape.window > 0 ? launch_bwd_dq_wide_t<D, DT, true>(a) : launch_bwd_dq_wide_t<D, DT, false>(a);
+}
+
 int launch_bwd_dq(const BwdArgs& a, int D) {
   switch (D) {
-    case 32: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<32, DT_BF16>(a) : launch_bwd_dq_wide_t<32, DT_F16>(a);
-    case 64: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<64, DT_BF16>(a) : launch_bwd_dq_wide_t<64, DT_F16>(a);
-    case 128: return a.dtype == DT_BF16 ? launch_bwd_dq_wide_t<128, DT_BF16>(a) : launch_bwd_dq_wide_t<128, DT_F16>(a);
+    case 32: return a.dtype == DT_BF16 ? launch_bwd_dq_l<32, DT_BF16>(a) : launch_bwd_dq_l<32, DT_F16>(a);
+    case 64: return a.dtype == DT_BF16 ? launch_bwd_dq_l<64, DT_BF16>(a) : launch_bwd_dq_l<64, DT_F16>(a);
+    case 128: return a.dtype == DT_BF16 ? launch_bwd_dq_l<128, DT_BF16>(a) : launch_bwd_dq_l<128, DT_F16>(a);
     default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }
 }

@@ -115,8 +115,15 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
     i_start = first_row <= 0 ? 0 : int(first_row / BQ);
     if (i_start > n_qt) i_start = n_qt;
   }
+  int n_qt_w = n_qt;
+  if (VL && shp.causal && shp.window > 0) {  // windows come with the packed layout only
+    // sliding window: the last query that sees this tile's last key
+    const long long last_row = (long long)w.kv0 + BM - 1 + shp.window - 1 + shp.k_off - shp.q_off;
+    const long long i_end = last_row < 0 ? 0 : last_row / BQ + 1;
+    if (i_end < n_qt_w) n_qt_w = int(i_end);
+  }
   w.i_start = i_start;
-  w.per_head = n_qt - i_start;
+  w.per_head = n_qt_w > i_start ? n_qt_w - i_start : 0;
   w.n_items = w.per_head * (shp.Hq / shp.Hkv);
   return w;
 }
@@ -485,6 +492,14 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
             if (cmin > 0) {
 #pragma unroll
               for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+            }
+            if (VL && shp.window > 0 && !key_out) {
+              // sliding window: queries past this key's window do not see it
+              const long long xm = cmin_base + shp.window - 1 - q0 - 64 * hh;  // last visible column
+              if (xm < 63) {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
+              }
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];

@@ -110,6 +110,7 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.bt_stride = 0;
   s.page_size = 0;
   s.pack_g = 0;
+  s.window = 0;
   return s;
 }
 
@@ -362,10 +363,11 @@ AttnShape varlen_shape(const int* cu_q, const int* cu_k, int B, int Hq, int Hkv,
 
 int fwd_varlen_impl(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_q,
                     const int* cu_k, int B, int Hq, int Hkv, int max_q, int max_k, int total_q, int total_k, int D,
-                    float softmax_scale, int causal, void* stream, int dtype) {
+                    float softmax_scale, int causal, int window, void* stream, int dtype) {
   int rc = check_varlen(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D);
   if (rc) return rc;
   if (!q || !k || !v || !o || !lse || !std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  if (window < 0 || (window > 0 && !causal)) return FA_ERR_BAD_SHAPE;
   const PackedStrides sq(total_q, Hq, D), sk(total_k, Hkv, D);
   if (!out_strides_ok(o, sq.v, 2)) return FA_ERR_MISALIGNED;
   FwdArgs a;
@@ -375,6 +377,7 @@ int fwd_varlen_impl(const void* q, const void* k, const void* v, void* o, float*
   if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, 128, dtype))) return rc;
   a.shape = varlen_shape(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, softmax_scale, causal);
   a.shape.pack_g = pack;
+  a.shape.window = window;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = 0;
@@ -388,9 +391,10 @@ int fwd_varlen_impl(const void* q, const void* k, const void* v, void* o, float*
 int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
                     void* dq, void* dk, void* dv, float* delta, float* dq_accum, const int* cu_q, const int* cu_k,
                     int B, int Hq, int Hkv, int max_q, int max_k, int total_q, int total_k, int D,
-                    float softmax_scale, int causal, int deterministic, void* stream, int dtype) {
+                    float softmax_scale, int causal, int window, int deterministic, void* stream, int dtype) {
   int rc = check_varlen(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, D);
   if (rc) return rc;
+  if (window < 0 || (window > 0 && !causal)) return FA_ERR_BAD_SHAPE;
   if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv || !delta) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
   const bool fused = D <= 64 && !deterministic;
@@ -408,6 +412,7 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
   BwdArgs a;
   a.dtype = dtype;
   a.shape = varlen_shape(cu_q, cu_k, B, Hq, Hkv, max_q, max_k, total_q, total_k, softmax_scale, causal);
+  a.shape.window = window;
   a.lse = lse;
   a.delta = delta;
   a.dk = dk;
@@ -456,7 +461,7 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
 int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse, const int* cu_q,
                    const int* seqlens_k, const int* block_table, int B, int Hq, int Hkv, int max_q, int max_k,
                    int total_q, int num_pages, int page_size, int bt_stride, int D, float softmax_scale, int causal,
-                   void* stream, int dtype) {
+                   int window, void* stream, int dtype) {
   if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || max_q <= 0 || max_k <= 0 || total_q <= 0 ||
       num_pages <= 0 || bt_stride <= 0)
@@ -467,6 +472,7 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   if ((long long)num_pages * page_size > 0x7fffffffLL) return FA_ERR_BAD_SHAPE;
   if (!q || !k_cache || !v_cache || !o || !lse || !cu_q || !seqlens_k || !block_table) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  if (window < 0 || (window > 0 && !causal)) return FA_ERR_BAD_SHAPE;
   const PackedStrides sq(total_q, Hq, D), sk(num_pages * page_size, Hkv, D);
   if (!out_strides_ok(o, sq.v, 2)) return FA_ERR_MISALIGNED;
   int rc;
@@ -484,6 +490,7 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   a.shape.bt_stride = bt_stride;
   a.shape.page_size = page_size;
   a.shape.pack_g = pack;
+  a.shape.window = window;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = 0;
@@ -614,52 +621,52 @@ extern "C" int fa_bwd_dq_convert_bf16(const float* dq_accum, void* dq, int B, in
 extern "C" int fa_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
                              const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                              int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D, float softmax_scale,
-                             int causal, void* stream) {
+                             int causal, int window, void* stream) {
   return fwd_varlen_impl(q, k, v, o, lse, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv, max_seqlen_q, max_seqlen_k,
-                         total_q, total_k, D, softmax_scale, causal, stream, DT_F16);
+                         total_q, total_k, D, softmax_scale, causal, window, stream, DT_F16);
 }
 extern "C" int fa_fwd_varlen_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
                                   const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                                   int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                                  float softmax_scale, int causal, void* stream) {
+                                  float softmax_scale, int causal, int window, void* stream) {
   return fwd_varlen_impl(q, k, v, o, lse, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv, max_seqlen_q, max_seqlen_k,
-                         total_q, total_k, D, softmax_scale, causal, stream, DT_BF16);
+                         total_q, total_k, D, softmax_scale, causal, window, stream, DT_BF16);
 }
 extern "C" int fa_bwd_varlen(const void* q, const void* k, const void* v, const void* o, const void* dO,
                              const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
                              const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                              int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D, float softmax_scale,
-                             int causal, int deterministic, void* stream) {
+                             int causal, int window, int deterministic, void* stream) {
   return bwd_varlen_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv,
-                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, deterministic, stream,
+                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, window, deterministic, stream,
                          DT_F16);
 }
 extern "C" int fa_bwd_varlen_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
                                   const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
                                   const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
                                   int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int D,
-                                  float softmax_scale, int causal, int deterministic, void* stream) {
+                                  float softmax_scale, int causal, int window, int deterministic, void* stream) {
   return bwd_varlen_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, cu_seqlens_q, cu_seqlens_k, B, Hq, Hkv,
-                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, deterministic, stream,
+                         max_seqlen_q, max_seqlen_k, total_q, total_k, D, softmax_scale, causal, window, deterministic, stream,
                          DT_BF16);
 }
 
 extern "C" int fa_fwd_paged(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                             const int* cu_seqlens_q, const int* seqlens_k, const int* block_table, int B, int Hq,
                             int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q, int num_pages, int page_size,
-                            int max_pages_per_seq, int D, float softmax_scale, int causal, void* stream) {
+                            int max_pages_per_seq, int D, float softmax_scale, int causal, int window, void* stream) {
   return fwd_paged_impl(q, k_cache, v_cache, o, lse, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv, max_seqlen_q,
                         max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D, softmax_scale, causal,
-                        stream, DT_F16);
+                        window, stream, DT_F16);
 }
 extern "C" int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse,
                                  const int* cu_seqlens_q, const int* seqlens_k, const int* block_table, int B, int Hq,
                                  int Hkv, int max_seqlen_q, int max_seqlen_k, int total_q, int num_pages,
                                  int page_size, int max_pages_per_seq, int D, float softmax_scale, int causal,
-                                 void* stream) {
+                                 int window, void* stream) {
   return fwd_paged_impl(q, k_cache, v_cache, o, lse, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv, max_seqlen_q,
                         max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D, softmax_scale, causal,
-                        stream, DT_BF16);
+                        window, stream, DT_BF16);
 }
 
 extern "C" int fa_device_status(int reset) {

@@ -68,6 +68,9 @@ struct AttnShape {
   // heads of one K/V head (a GQA group) x 128 / pack_g query rows, so each
   // K/V tile is read once for the whole group (decode, short queries).
   int pack_g;
+  // Sliding window (causal only): when window > 0, a query sees only the
+  // window keys ending at its own position, j > pos - window.
+  int window;
 };
 
 // Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of
@@ -145,6 +148,14 @@ __device__ __forceinline__ int kv_tiles_for_rows(const AttnShape& s, const Seq& 
     if (lim < last) last = int(lim);
   }
   return last / BN + 1;
+}
+
+// First K/V tile of width BN that a block of query rows starting at r0 of a
+// batch touches: 0 unless a sliding window hides the keys before it.
+__device__ __forceinline__ int kv_first_tile(const AttnShape& s, const Seq& q, int r0, int BN) {
+  if (s.window <= 0) return 0;
+  const long long lo = (long long)r0 + s.q_off - s.k_off + q.diag - s.window + 1;  // first visible key
+  return lo <= 0 ? 0 : int(lo / BN);
 }
 
 // Persistent kernels: the k-th work unit of CTA c when G CTAs share n units

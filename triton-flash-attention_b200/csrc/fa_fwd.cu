@@ -102,11 +102,14 @@ struct Cfg {
 // head) instead: its tiles hold the G query heads of the group x R = 128 / G
 // query rows (tile row = g * R + r), h is the group's first query head, and
 // row0 / rows count query rows per head.
+// Key tiles: the unit streams key tiles kt0 .. kt0 + n_max - 1 (local index
+// j = 0 .. n_max - 1); tile t is active for local j in [js[t], n_kv[t])
+// (js = 0 and kt0 = 0 unless a sliding window hides leading keys).
 struct Unit {
-  int b, h, kvh, row0, rows, n_kv[QT], n_max;
+  int b, h, kvh, row0, rows, kt0, js[QT], n_kv[QT], n_max;
   Seq sq;
 };
-template <bool PACK>
+template <bool PACK, bool WIN>
 __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   const int G = PACK ? shp.pack_g : 1;
   const int rows = BM / G;  // query rows per head in a tile
@@ -126,10 +129,22 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   w.rows = rows;
   w.row0 = (n_qblk - 1 - u / BH) * QT * rows;
   w.sq = seq_of(shp, w.b);
+  int first[QT], end[QT];
+  w.kt0 = 1 << 30;
+#pragma unroll
+  for (int t = 0; t < QT; ++t) {
+    end[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * rows, rows, BN);
+    first[t] = WIN ? kv_first_tile(shp, w.sq, w.row0 + t * rows, BN) : 0;
+    if (first[t] >= end[t]) first[t] = end[t] = 0;  // no visible key
+    else w.kt0 = first[t] < w.kt0 ? first[t] : w.kt0;
+  }
+  if (w.kt0 == (1 << 30)) w.kt0 = 0;
   w.n_max = 0;
 #pragma unroll
   for (int t = 0; t < QT; ++t) {
-    w.n_kv[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * rows, rows, BN);
+    const bool active = end[t] > first[t];
+    w.js[t] = active ? first[t] - w.kt0 : 0;
+    w.n_kv[t] = active ? end[t] - w.kt0 : 0;
     w.n_max = w.n_kv[t] > w.n_max ? w.n_kv[t] : w.n_max;
   }
   return w;
@@ -137,7 +152,7 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
 
 }  // namespace fwd
 
-template <int D, int DT, bool PACK>
+template <int D, int DT, bool PACK, bool WIN>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
@@ -236,7 +251,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of<PACK>(shp, ui);
+          const Unit w = unit_of<PACK, WIN>(shp, ui);
           if (w.n_max == 0) continue;
           if (is_k) {
             const int qb = uc % C::QB;
@@ -266,7 +281,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
               const int last_page = (w.sq.nk - 1) / P;
               const int* bt = shp.block_table + (long long)w.b * shp.bt_stride;
               for (int i = 0; i < BN / PR; ++i) {
-                const int kr = j * BN + i * PR;
+                const int kr = (w.kt0 + j) * BN + i * PR;
                 const int pidx = kr / P < last_page ? kr / P : last_page;
                 const int row = __ldg(bt + pidx) * P + kr % P;
                 for (int bx = 0; bx < G::NBOX; ++bx)
@@ -276,7 +291,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             } else {
               for (int bx = 0; bx < G::NBOX; ++bx)
                 tma_load_4d(smem + kv_off + s * C::KV_TILE_BYTES + bx * BN * G::SW, tmap_kv, kv_full + s,
-                            bx * G::BOX, w.sq.k0 + j * BN, w.kvh, w.sq.tb);
+                            bx * G::BOX, w.sq.k0 + (w.kt0 + j) * BN, w.kvh, w.sq.tb);
             }
           }
         }
@@ -302,7 +317,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of<PACK>(shp, ui);
+          const Unit w = unit_of<PACK, WIN>(shp, ui);
           if (w.n_max == 0) continue;
           const int qb = uc % C::QB;
           if (!mbar_wait(q_full + qb, uint32_t(uc / C::QB) & 1, ctl, 10)) { ok = false; break; }
@@ -332,7 +347,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           if (!mbar_wait(k_full + gj % C::NST, uint32_t(gj / C::NST) & 1, ctl, 11)) { ok = false; break; }
           tc_fence_after();
           for (int t = 0; t < QT; ++t)
-            if (w.n_kv[t] > 0) issue_s(t, gj);
+            if (w.n_kv[t] > 0 && w.js[t] == 0) issue_s(t, gj);
           umma_commit(k_empty + gj % C::NST);
           if constexpr (C::SEP_P) {
             // S_t(j+1) once the warpgroup read S_t(j); P_t(j) V once it wrote P_t(j)
@@ -343,8 +358,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
               if (more) {
                 if (!mbar_wait(k_full + (g + 1) % C::NST, uint32_t((g + 1) / C::NST) & 1, ctl, 13)) { ok = false; break; }
                 for (int t = 0; t < QT && ok; ++t) {
-                  if (j + 1 >= w.n_kv[t]) continue;
-                  if (!mbar_wait(s_read + t, uint32_t(cnt[t]) & 1, ctl, 17)) { ok = false; break; }
+                  if (j + 1 >= w.n_kv[t] || j + 1 < w.js[t]) continue;
+                  // a tile's first S in the unit finds its buffer free; later
+                  // ones wait until the warpgroup read the previous S
+                  if (j + 1 > w.js[t] && !mbar_wait(s_read + t, uint32_t(cnt[t]) & 1, ctl, 17)) { ok = false; break; }
                   tc_fence_after();
                   issue_s(t, g + 1);
                 }
@@ -353,11 +370,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
               }
               if (!mbar_wait(v_full + s, uint32_t(g / C::NST) & 1, ctl, 12)) { ok = false; break; }
               for (int t = 0; t < QT && ok; ++t) {
-                if (j >= w.n_kv[t]) continue;
+                if (j >= w.n_kv[t] || j < w.js[t]) continue;
                 if (!mbar_wait(p_ready + t, uint32_t(cnt[t]) & 1, ctl, 14)) { ok = false; break; }
-                if (j == 0 && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
+                if (j == w.js[t] && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
                 tc_fence_after();
-                issue_pv(t, g, j > 0);
+                issue_pv(t, g, j > w.js[t]);
                 umma_commit(pv_done + t);
                 ++cnt[t];
               }
@@ -376,12 +393,13 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             }
             tc_fence_after();
             for (int t = 0; t < QT && ok; ++t) {
-              if (j >= w.n_kv[t]) continue;
+              if (j + 1 == w.js[t] && j + 1 < w.n_kv[t]) issue_s(t, g + 1);  // the tile's first S
+              if (j >= w.n_kv[t] || j < w.js[t]) continue;
               if (!mbar_wait(p_ready + t, uint32_t(cnt[t]) & 1, ctl, 14)) { ok = false; break; }
               // O_t of the previous unit was read by its epilogue
-              if (j == 0 && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
+              if (j == w.js[t] && oc[t] > 0 && !mbar_wait(o_empty + t, uint32_t(oc[t] - 1) & 1, ctl, 16)) { ok = false; break; }
               tc_fence_after();
-              issue_pv(t, g, j > 0);
+              issue_pv(t, g, j > w.js[t]);
               ++cnt[t];
               if (j + 1 < w.n_kv[t]) issue_s(t, g + 1);
             }
@@ -435,20 +453,32 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int ui = snake_unit(cta, k, n_cta, n_units);
       if (ui >= n_units) break;
-      const Unit w = unit_of<PACK>(shp, ui);
+      const Unit w = unit_of<PACK, WIN>(shp, ui);
       // query row (within the batch) and head of this thread's tile row
       const int r = w.row0 + t * w.rows + (PACK ? row_local % w.rows : row_local);
       const int hq = w.h + (PACK ? row_local / w.rows : 0);
-      const int nt = w.n_kv[t];
-      // last visible key column of this row (local key index)
+      const int nt = w.n_kv[t];  // this tile's steps are local key tiles js .. nt - 1
+      const int js = w.js[t];
+      // last visible key column of this row (key index in the batch), and
+      // with a sliding window the first one
       int lim = w.sq.nk - 1;
+      long long lo = 0;
       if (shp.causal) {
         const long long c = (long long)r + shp.q_off - shp.k_off + w.sq.diag;
         lim = c < lim ? int(c) : lim;  // may be negative: no visible key
+        if (WIN) lo = c - shp.window + 1;
+      }
+      if constexpr (C::SEP_P && TURNS) {
+        // empty turns for the leading key tiles the other query tile has and this one lacks
+        for (int j = 0; j < js && ok; ++j) {
+          if (!take_turn()) { ok = false; break; }
+          pass_turn();
+        }
+        if (!ok) break;
       }
       float m = -INFINITY;  // running exponent base (scaled log2 units)
       float l = 0.f;        // running row sum of exp2(s * c2 - m)
-      for (int j = 0; j < nt; ++j) {
+      for (int j = js; j < nt; ++j) {
         if (!mbar_wait_warp(s_full + t, uint32_t(cnt) & 1, ctl, 20 + t)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
@@ -459,10 +489,16 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           tc_fence_before();
           mbar_arrive(s_read + t);
         }
-        const int lim_j = lim - j * BN;  // last visible local column in this tile
+        const int key0 = (w.kt0 + j) * BN;  // key index of this tile's column 0
+        const int lim_j = lim - key0;      // last visible column in this tile
         if (lim_j < BN - 1) {
 #pragma unroll
           for (int c = 0; c < BN; ++c) s[c] = c <= lim_j ? s[c] : -INFINITY;
+        }
+        if (WIN && lo > key0) {  // sliding window: columns before lo are hidden
+          const long long lo_j = lo - key0;
+#pragma unroll
+          for (int c = 0; c < BN; ++c) s[c] = c >= lo_j ? s[c] : -INFINITY;
         }
         // row max: 8 independent 3-input max chains, then a short tree
         float a8[8];
@@ -517,7 +553,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         }
         if constexpr (C::SEP_P) {
           // P_t(j-1) V has read the P buffer and finished accumulating O_t
-          if (j > 0 && !mbar_wait_warp(pv_done + t, uint32_t(cnt - 1) & 1, ctl, 24 + t)) { ok = false; break; }
+          if (j > js && !mbar_wait_warp(pv_done + t, uint32_t(cnt - 1) & 1, ctl, 24 + t)) { ok = false; break; }
           tc_fence_after();
         }
         {
@@ -533,7 +569,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
 #pragma unroll
           for (int cc = 0; cc < BN / 32; ++cc) tmem_st16(tP + cc * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc * 16]));
         }
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        if (j > js && __any_sync(0xffffffffu, rescale)) {
           // O *= alpha
 #pragma unroll 1
           for (int cc = 0; cc < C::OW / 16; ++cc) {
@@ -610,11 +646,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool PACK>
+template <int D, int DT, bool PACK, bool WIN>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D, DT, PACK>;
+  auto kern = fa_fwd_kernel<D, DT, PACK, WIN>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -637,10 +673,13 @@ int launch_fwd_t(const FwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-// GQA-packed and plain query tiles are separate instantiations.
+// GQA-packed and plain query tiles, and sliding-window and plain masks, are
+// separate instantiations.
 template <int D, int DT>
 int launch_fwd_l(const FwdArgs& a) {
-  return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true>(a) : launch_fwd_t<D, DT, false>(a);
+  if (a.shape.window > 0)
+    return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, true>(a) : launch_fwd_t<D, DT, false, true>(a);
+  return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, false>(a) : launch_fwd_t<D, DT, false, false>(a);
 }
 
 int launch_fwd(const FwdArgs& a, int D) {

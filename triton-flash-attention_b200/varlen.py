@@ -83,7 +83,7 @@ def _validate_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q
 
 
 def varlen_attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, max_seqlen_k: int,
-                             causal: bool, softmax_scale: float):
+                             causal: bool, softmax_scale: float, window: int = 0):
     """Forward over packed sequences: returns ``(o, lse2)`` with ``o`` like
     ``q`` and ``lse2`` the ``(Hq, total_q)`` base-2 log-sum-exp per row."""
     total_q, hq, d = q.shape
@@ -94,13 +94,13 @@ def varlen_attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: 
     rc = _abi.entry("fa_fwd_varlen", q.dtype)(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
         cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, hq, hkv, int(max_seqlen_q), int(max_seqlen_k),
-        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, _stream_handle(q.device))
+        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, int(window), _stream_handle(q.device))
     _abi.check(rc, "fa_fwd_varlen")
     return o, lse
 
 
 def varlen_attention_backward(q, k, v, o, do, lse, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
-                              max_seqlen_k: int, causal: bool, softmax_scale: float):
+                              max_seqlen_k: int, causal: bool, softmax_scale: float, window: int = 0):
     """dQ, dK, dV over packed sequences.  Head dims 32 and 64 run the fused
     pass (fp32 dQ accumulator in caller scratch) unless
     ``torch.use_deterministic_algorithms(True)`` asks for the separate,
@@ -116,7 +116,8 @@ def varlen_attention_backward(q, k, v, o, do, lse, cu_seqlens_q, cu_seqlens_k, m
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr(), acc.data_ptr() if fused else None,
         cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, hq, hkv, int(max_seqlen_q), int(max_seqlen_k),
-        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, 0 if fused else 1, _stream_handle(q.device))
+        total_q, total_k, d, float(softmax_scale), 1 if causal else 0, int(window), 0 if fused else 1,
+        _stream_handle(q.device))
     _abi.check(rc, "fa_bwd_varlen")
     return dq, dk, dv
 
@@ -127,26 +128,37 @@ class B200VarlenAttention(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
-                softmax_scale):
+                softmax_scale, window=0):
         output, lse = varlen_attention_forward(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
-                                               max_seqlen_k, bool(causal), float(softmax_scale))
+                                               max_seqlen_k, bool(causal), float(softmax_scale), int(window))
         ctx.save_for_backward(query, key, value, output, lse, cu_seqlens_q, cu_seqlens_k)
         ctx.max_seqlen = (int(max_seqlen_q), int(max_seqlen_k))
         ctx.causal = bool(causal)
         ctx.softmax_scale = float(softmax_scale)
+        ctx.window = int(window)
         return output
 
     @staticmethod
     def backward(ctx, grad_output):
         query, key, value, output, lse, cu_q, cu_k = ctx.saved_tensors
         dq, dk, dv = varlen_attention_backward(query, key, value, output, grad_output.contiguous(), lse, cu_q, cu_k,
-                                               *ctx.max_seqlen, ctx.causal, ctx.softmax_scale)
-        return dq, dk, dv, None, None, None, None, None, None
+                                               *ctx.max_seqlen, ctx.causal, ctx.softmax_scale, ctx.window)
+        return dq, dk, dv, None, None, None, None, None, None, None
+
+
+def _window_arg(window_size, is_causal: bool) -> int:
+    if window_size is None:
+        return 0
+    if isinstance(window_size, bool) or not isinstance(window_size, int) or window_size < 1:
+        raise ValueError("window_size must be a positive int or None")
+    if not is_causal:
+        raise ValueError("window_size (a sliding window) requires is_causal=True")
+    return window_size
 
 
 def scaled_dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
                                         max_seqlen_k: int, *, is_causal: bool = False, scale: float | None = None,
-                                        enable_gqa: bool = False) -> torch.Tensor:
+                                        enable_gqa: bool = False, window_size: int | None = None) -> torch.Tensor:
     """Attention over a batch of packed sequences of different lengths.
 
     ``query``: ``(total_q, Hq, D)``; ``key``, ``value``: ``(total_k, Hkv, D)``;
@@ -154,23 +166,26 @@ def scaled_dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seql
     lengths on the same device (``[0, n_0, n_0 + n_1, ...]``, ending at the
     totals); ``max_seqlen_q`` / ``max_seqlen_k``: at least the longest
     sequence's lengths.  Sequences may be empty.  Returns ``(total_q, Hq, D)``
-    and supports autograd.  The default ``scale`` is ``D ** -0.5``."""
+    and supports autograd.  The default ``scale`` is ``D ** -0.5``.
+    ``window_size`` (with ``is_causal``) is a sliding window: each query sees
+    only the ``window_size`` keys ending at its own position."""
     if not isinstance(is_causal, bool):
         raise TypeError("is_causal must be a bool")
     if not isinstance(enable_gqa, bool):
         raise TypeError("enable_gqa must be a bool")
     if scale is not None and (not isinstance(scale, Real) or not math.isfinite(float(scale))):
         raise ValueError("scale must be a finite real number or None")
+    window = _window_arg(window_size, is_causal)
     _validate_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
                      enable_gqa=enable_gqa)
     softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
     return B200VarlenAttention.apply(query.contiguous(), key.contiguous(), value.contiguous(),
                                      cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous(), max_seqlen_q,
-                                     max_seqlen_k, is_causal, softmax_scale)
+                                     max_seqlen_k, is_causal, softmax_scale, window)
 
 
 def paged_attention_forward(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k, max_seqlen_q: int,
-                            max_seqlen_k: int, causal: bool, softmax_scale: float):
+                            max_seqlen_k: int, causal: bool, softmax_scale: float, window: int = 0):
     """Forward over a paged K/V cache: returns ``(o, lse2)`` like
     ``varlen_attention_forward``."""
     total_q, hq, d = q.shape
@@ -182,14 +197,15 @@ def paged_attention_forward(q, k_cache, v_cache, block_table, cu_seqlens_q, seql
         q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), lse.data_ptr(),
         cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), block_table.data_ptr(), batch, hq, hkv,
         int(max_seqlen_q), int(max_seqlen_k), total_q, num_pages, page_size, block_table.shape[1], d,
-        float(softmax_scale), 1 if causal else 0, _stream_handle(q.device))
+        float(softmax_scale), 1 if causal else 0, int(window), _stream_handle(q.device))
     _abi.check(rc, "fa_fwd_paged")
     return o, lse
 
 
 def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k,
                                        max_seqlen_q: int, max_seqlen_k: int, *, is_causal: bool = False,
-                                       scale: float | None = None, enable_gqa: bool = False) -> torch.Tensor:
+                                       scale: float | None = None, enable_gqa: bool = False,
+                                       window_size: int | None = None) -> torch.Tensor:
     """Attention of packed queries over a paged K/V cache (forward only).
 
     ``query``: ``(total_q, Hq, D)`` with ``cu_seqlens_q`` int32 prefix sums;
@@ -228,10 +244,11 @@ def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_
         raise RuntimeError("the paged K/V path is forward only; run it under torch.no_grad()")
     # the varlen checks on (query, one page of the cache seen as keys)
     kv_view = k_cache[0]
+    window = _window_arg(window_size, is_causal)
     _validate_varlen(query, kv_view, kv_view, cu_seqlens_q, cu_seqlens_q, max_seqlen_q, max_seqlen_k,
                      enable_gqa=enable_gqa)
     softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
     o, _ = paged_attention_forward(query.contiguous(), k_cache.contiguous(), v_cache.contiguous(),
                                    block_table.contiguous(), cu_seqlens_q.contiguous(), seqlens_k.contiguous(),
-                                   max_seqlen_q, max_seqlen_k, is_causal, softmax_scale)
+                                   max_seqlen_q, max_seqlen_k, is_causal, softmax_scale, window)
     return o
