@@ -286,6 +286,47 @@ FA_API int fa_bwd_fused_noalloc(const void* q, const void* k, const void* v, con
                                 const int64_t* dk_strides, const int64_t* dv_strides,
                                 float softmax_scale, int causal, void* stream);
 
+/* Attention whose value head size Dv differs from the query/key head size D
+ * (dense (B, H, N, D) layout, as fa_fwd).  Replaces the reference's
+ * dispatch of such inputs to PyTorch's SDPA (attention.py:639-646: the
+ * Triton kernel takes one head size).  D and Dv are each 32, 64 or 128; q, k
+ * are D wide, v, o, dO Dv wide; lse as in fa_fwd.  The kernels run at width
+ * max(D, Dv), with the narrower operands' missing columns read as zeros, so
+ * a call costs what an equal-width call of max(D, Dv) costs.  Zero position
+ * offsets (no ring step).  fa_fwd_vdim also serves D == Dv. */
+FA_API int fa_fwd_vdim(const void* q, const void* k, const void* v, void* o, float* lse,
+                       int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                       const int64_t* q_strides, const int64_t* k_strides,
+                       const int64_t* v_strides, const int64_t* o_strides,
+                       float softmax_scale, int causal, void* stream);
+/* The whole backward for fa_fwd_vdim: delta (caller's (B, Hq, Nq) fp32
+ * buffer), dq and dk (D wide), dv (Dv wide).  With max(D, Dv) <= 64 and
+ * deterministic == 0 it runs the fused pass and needs dq_accum, a caller's
+ * contiguous (B, Hq, Nq, max(D, Dv)) fp32 scratch buffer (zeroed here);
+ * otherwise the separate dQ and dK/dV kernels run (bitwise reproducible)
+ * and dq_accum may be NULL. */
+FA_API int fa_bwd_vdim(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                       const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                       int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                       const int64_t* q_strides, const int64_t* k_strides,
+                       const int64_t* v_strides, const int64_t* o_strides,
+                       const int64_t* do_strides, const int64_t* dq_strides,
+                       const int64_t* dk_strides, const int64_t* dv_strides,
+                       float softmax_scale, int causal, int deterministic, void* stream);
+FA_API int fa_fwd_vdim_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                            int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                            const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, const int64_t* o_strides,
+                            float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_vdim_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                            int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                            const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, const int64_t* o_strides,
+                            const int64_t* do_strides, const int64_t* dq_strides,
+                            const int64_t* dk_strides, const int64_t* dv_strides,
+                            float softmax_scale, int causal, int deterministic, void* stream);
+
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
  * low byte and the barrier site in bits 8..15.  Synchronises the device. */
@@ -296,7 +337,7 @@ FA_API const char* fa_status_string(int code);
 
 /* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
  * 1.2.0 the fused backward, 1.3.0 packed variable-length batches and the
- * paged K/V forward). */
+ * paged K/V forward, 1.4.0 value head sizes different from D). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

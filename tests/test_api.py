@@ -86,16 +86,24 @@ def test_type_errors():
         scaled_dot_product_attention(t, t, t, scale=float("nan"))
 
 
-def test_cross_attention_requires_equal_value_head_size():
-    """Cross-attention itself is served; Dv != Dqk is not (attention.py:643-646)."""
-    query = torch.randn(1, 2, 3, 32)
-    key = torch.randn(1, 2, 5, 32)
-    value = torch.randn(1, 2, 5, 16)
-    decision = explain_dispatch(query, key, value)
+def test_value_head_size_reasons(monkeypatch):
+    """A value head size different from the query/key one is served (the
+    reference sends it to PyTorch, attention.py:639-646) when both are 32, 64
+    or 128; other value head sizes get their own reason.  Checked with the
+    device test bypassed (no GPU here)."""
+    class FakeDevice:
+        type = "cuda"
+
+    query = torch.randn(1, 2, 3, 32).half()
+    key = torch.randn(1, 2, 5, 32).half()
+    fake = FakeDevice()
+    monkeypatch.setattr(torch.Tensor, "device", property(lambda self: fake), raising=False)
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
+    decision = explain_dispatch(query, key, torch.randn(1, 2, 5, 16).half())
     assert decision.backend == "unsupported"
-    assert "value head sizes" in decision.reason
-    with pytest.raises(RuntimeError, match="value head sizes"):
-        scaled_dot_product_attention(query, key, value)
+    assert "value head_dim must be one of (32, 64, 128)" in decision.reason
+    decision = explain_dispatch(query, key, torch.randn(1, 2, 5, 128).half())
+    assert decision.backend == "cuda"
 
 
 def test_dtype_and_head_dim_reasons(monkeypatch):

@@ -15,8 +15,10 @@ from .attention import (
     attention_backward_dkdv,
     attention_backward_dq,
     attention_backward_fused,
+    attention_backward_vdim,
     attention_delta,
     attention_forward,
+    attention_forward_vdim,
     explain_dispatch,
     fused_backward_enabled,
     scaled_dot_product_attention,
@@ -41,9 +43,11 @@ __all__ = [
     "attention_backward_dkdv",
     "attention_backward_dq",
     "attention_backward_fused",
+    "attention_backward_vdim",
     "attention_delta",
     "attention_flops",
     "attention_forward",
+    "attention_forward_vdim",
     "delta_bytes",
     "explain_dispatch",
     "fused_backward_enabled",

@@ -54,6 +54,11 @@ SIGNATURES.update({
 SIGNATURES["fa_fwd_paged"] = (_i, [_p] * 8 + [_i] * 10 + [_f, _i, _i, _p])
 SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in ("fa_fwd_varlen", "fa_bwd_varlen", "fa_fwd_paged")})
 SIGNATURES.update({
+    "fa_fwd_vdim": (_i, [_p] * 5 + [_i] * 7 + [_s] * 4 + [_f, _i, _p]),
+    "fa_bwd_vdim": (_i, [_p] * 11 + [_i] * 7 + [_s] * 8 + [_f, _i, _i, _p]),
+})
+SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in ("fa_fwd_vdim", "fa_bwd_vdim")})
+SIGNATURES.update({
     "fa_bwd_fused_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
                                   _s, _s, _s, _s, _s, _s, _s, _s, _f, _i, _p]),
     "fa_device_status": (_i, [_i]),

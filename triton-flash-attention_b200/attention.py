@@ -75,11 +75,10 @@ def _validate_inputs(query, key, value, *, enable_gqa: bool) -> None:
 def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> DispatchDecision:
     """Explain whether the B200 kernels can serve these inputs
     (attention.py:629-670).  Query and key lengths may differ (the causal
-    mask is then top-left aligned, as in PyTorch's SDPA)."""
+    mask is then top-left aligned, as in PyTorch's SDPA), and so may the
+    query/key and value head sizes (the reference sends both to PyTorch,
+    attention.py:639-646); each head size must be 32, 64 or 128."""
     _validate_inputs(query, key, value, enable_gqa=enable_gqa)
-    if value.shape[3] != query.shape[3]:
-        return DispatchDecision(
-            "unsupported", "the custom kernel requires equal query/key and value head sizes")
     if query.device.type != "cuda":
         return DispatchDecision("unsupported", "the B200 kernel requires a CUDA tensor")
     if torch.version.hip is not None:
@@ -87,10 +86,13 @@ def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> Dispatch
     if query.dtype not in SUPPORTED_DTYPES:
         return DispatchDecision(
             "unsupported", "the custom mixed-precision path currently supports float16 and bfloat16")
+    supported = ", ".join(str(dim) for dim in SUPPORTED_HEAD_DIMS)
     if query.shape[-1] not in SUPPORTED_HEAD_DIMS:
-        supported = ", ".join(str(dim) for dim in SUPPORTED_HEAD_DIMS)
         return DispatchDecision(
             "unsupported", f"head_dim must be one of ({supported}) for the B200 path")
+    if value.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        return DispatchDecision(
+            "unsupported", f"the value head_dim must be one of ({supported}) for the B200 path")
     major, minor = torch.cuda.get_device_capability(query.device)
     if (major, minor) != (10, 0):
         return DispatchDecision(
@@ -108,6 +110,10 @@ def attention_forward(q, k, v, causal: bool, softmax_scale: float, *, q_offset: 
     log-sum-exp per query row in the scaled domain (attention.py:230)."""
     b, hq, nq, d = q.shape
     hkv, nk = k.shape[1], k.shape[2]
+    if v.shape[-1] != d:
+        if q_offset or k_offset:
+            raise ValueError("position offsets need equal query/key and value head sizes")
+        return attention_forward_vdim(q, k, v, causal, softmax_scale)
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)  # contiguous even for strided q
     lse = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
     rc = _abi.entry("fa_fwd", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
@@ -117,6 +123,49 @@ def attention_forward(q, k, v, causal: bool, softmax_scale: float, *, q_offset: 
                     _stream_handle(q.device))
     _abi.check(rc, "fa_fwd")
     return o, lse
+
+
+def attention_forward_vdim(q, k, v, causal: bool, softmax_scale: float):
+    """Forward with a value head size Dv different from the query/key head
+    size D: returns o (B, Hq, Nq, Dv) and lse2 as attention_forward does.
+    The kernels run at width max(D, Dv) with the narrower operands' missing
+    columns read as zeros."""
+    b, hq, nq, d = q.shape
+    hkv, nk, dv = k.shape[1], k.shape[2], v.shape[3]
+    o = torch.empty((b, hq, nq, dv), device=q.device, dtype=q.dtype)
+    lse = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
+    rc = _abi.entry("fa_fwd_vdim", q.dtype)(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                            b, hq, hkv, nq, nk, d, dv,
+                                            _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(o),
+                                            float(softmax_scale), 1 if causal else 0, _stream_handle(q.device))
+    _abi.check(rc, "fa_fwd_vdim")
+    return o, lse
+
+
+def attention_backward_vdim(q, k, v, o, do, lse, causal: bool, softmax_scale: float):
+    """dQ, dK (D wide) and dV (Dv wide) for attention_forward_vdim: the fused
+    pass when max(D, Dv) <= 64 and deterministic algorithms are off, else the
+    separate dQ and dK/dV kernels."""
+    b, hq, nq, d = q.shape
+    hkv, nk, dv_dim = k.shape[1], k.shape[2], v.shape[3]
+    width = max(d, dv_dim)
+    deterministic = torch.are_deterministic_algorithms_enabled()
+    delta = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
+    acc = None
+    if width <= 64 and not deterministic:
+        acc = torch.empty((b, hq, nq, width), device=q.device, dtype=torch.float32)
+    dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+    dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
+    rc = _abi.entry("fa_bwd_vdim", q.dtype)(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+        dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), delta.data_ptr(), acc.data_ptr() if acc is not None else None,
+        b, hq, hkv, nq, nk, d, dv_dim,
+        _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(o), _abi.strides3(do),
+        _abi.strides3(dq), _abi.strides3(dk), _abi.strides3(dv),
+        float(softmax_scale), 1 if causal else 0, 1 if deterministic else 0, _stream_handle(q.device))
+    _abi.check(rc, "fa_bwd_vdim")
+    return dq, dk, dv
 
 
 def attention_delta(o, do):
@@ -239,6 +288,10 @@ class B200Attention(torch.autograd.Function):
     def backward(ctx, grad_output):
         query, key, value, output, lse = ctx.saved_tensors
         grad_output = grad_output.contiguous()
+        if value.shape[-1] != query.shape[-1]:
+            grad_query, grad_key, grad_value = attention_backward_vdim(
+                query, key, value, output, grad_output, lse, ctx.causal, ctx.softmax_scale)
+            return grad_query, grad_key, grad_value, None, None
         if fused_backward_enabled(query.shape[-1]):
             grad_query, grad_key, grad_value = attention_backward_fused(
                 query, key, value, output, grad_output, lse, ctx.causal, ctx.softmax_scale)

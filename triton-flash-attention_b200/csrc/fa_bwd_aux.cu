@@ -115,12 +115,13 @@ int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_
                                                        zero_acc, B, H, N, D, stream);
 }
 
-// dq (operand type, element strides {sb, sh, sn, 1}) <- acc (contiguous
-// [B, H, N, D] fp32), eight elements per thread.
+// dq (operand type, element strides {sb, sh, sn, 1}) <- the first D columns
+// of acc (contiguous [B, H, N, acc_w] fp32, acc_w >= D), eight elements per
+// thread.
 template <int DT>
 __global__ void __launch_bounds__(256) fa_dq_convert_kernel(const float* __restrict__ acc, uint16_t* __restrict__ dq,
                                                             long long sb, long long sh, long long sn, int H, int N,
-                                                            int D, long long rows) {
+                                                            int D, int acc_w, long long rows) {
   const int vec_per_row = D / 8;
   const long long total = rows * vec_per_row;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) fa_dq_convert_kernel(const float* __restr
     const long long bh = row / N;
     const int h = int(bh % H);
     const long long b = bh / H;
-    const float4* src = reinterpret_cast<const float4*>(acc + row * D + part * 8);
+    const float4* src = reinterpret_cast<const float4*>(acc + row * acc_w + part * 8);
     const float4 x = src[0];
     const float4 y = src[1];
     uint4 pk;
@@ -144,7 +145,8 @@ __global__ void __launch_bounds__(256) fa_dq_convert_kernel(const float* __restr
 }
 
 int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
-                      int dtype, cudaStream_t stream) {
+                      int dtype, cudaStream_t stream, int acc_w) {
+  if (acc_w <= 0) acc_w = D;
   const long long rows = (long long)B * H * N;
   const long long work = rows * (D / 8);
   long long blocks = (work + 255) / 256;
@@ -153,9 +155,9 @@ int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, lo
   if (blocks < 1) blocks = 1;
   uint16_t* d16 = static_cast<uint16_t*>(dq);
   if (dtype == DT_BF16)
-    fa_dq_convert_kernel<DT_BF16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, rows);
+    fa_dq_convert_kernel<DT_BF16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, acc_w, rows);
   else
-    fa_dq_convert_kernel<DT_F16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, rows);
+    fa_dq_convert_kernel<DT_F16><<<unsigned(blocks), 256, 0, stream>>>(acc, d16, sb, sh, sn, H, N, D, acc_w, rows);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 

@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) gv[i] = 0.f;
         }
-        if (!row_ok) continue;
+        if (!row_ok || cc * 32 >= (w == 0 ? shp.v_cols : shp.qk_cols)) continue;
         if (accumulate_fp32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + off0 + cc * 32);
 #pragma unroll
@@ -1026,7 +1026,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) gv[i] = 0.f;
         }
-        if (!row_ok) continue;
+        if (!row_ok || cc * 32 >= (w == 0 ? shp.v_cols : shp.qk_cols)) continue;
         if (accumulate_fp32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + off0 + cc * 32);
 #pragma unroll

@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dq_out) + off);
 #pragma unroll
           for (int v4 = 0; v4 < HALF / 4; ++v4) {
+            if (w * HALF + v4 * 4 >= shp.qk_cols) break;
             float4 x = dst[v4];
             x.x += gv[v4 * 4 + 0] * sc;
             x.y += gv[v4 * 4 + 1] * sc;
@@ -397,6 +398,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dq_out) + off);
 #pragma unroll
           for (int v8 = 0; v8 < HALF / 8; ++v8) {
+            if (w * HALF + v8 * 8 >= shp.qk_cols) break;
             uint4 pk;
             pk.x = pack2<DT>(gv[v8 * 8 + 0] * sc, gv[v8 * 8 + 1] * sc);
             pk.y = pack2<DT>(gv[v8 * 8 + 2] * sc, gv[v8 * 8 + 3] * sc);

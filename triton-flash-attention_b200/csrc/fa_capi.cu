@@ -53,16 +53,17 @@ bool supported_d(int D) { return D == 32 || D == 64 || D == 128; }
 // 4-D tensor map (fp16 or bf16 elements) over (B, H, N, D) with element
 // strides {sb, sh, sn, 1}.  The box is {min(D, 64), rows, 1, 1} with the
 // swizzle the kernels' shared memory descriptors assume (128 B for D >= 64,
-// 64 B for D = 32).
+// 64 B for D = 32).  extent > 0 (< D) declares a tensor only extent columns
+// wide read by a width-D kernel: the TMA fills columns extent..D-1 with zeros.
 int make_map(CUtensorMap* map, const void* ptr, int B, int H, int N, int D, const int64_t* strides, int rows,
-             int dtype, int heads_per_box = 1) {
+             int dtype, int heads_per_box = 1, int extent = 0) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DRIVER;
   if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
   for (int i = 0; i < 3; ++i)
     if (strides[i] <= 0 || (strides[i] * 2) % 16 != 0) return FA_ERR_MISALIGNED;
   const int box_d = D >= 64 ? 64 : 32;
-  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t dims[4] = {cuuint64_t(extent > 0 ? extent : D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
   cuuint64_t gstr[3] = {cuuint64_t(strides[2]) * 2, cuuint64_t(strides[1]) * 2, cuuint64_t(strides[0]) * 2};
   cuuint32_t box[4] = {cuuint32_t(box_d), cuuint32_t(rows), cuuint32_t(heads_per_box), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -111,6 +112,8 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.page_size = 0;
   s.pack_g = 0;
   s.window = 0;
+  s.qk_cols = 1 << 20;  // no narrower tensor: every column is stored
+  s.v_cols = 1 << 20;
   return s;
 }
 
@@ -128,9 +131,9 @@ int gqa_pack(int Hq, int Hkv, int max_q) {
 // The forward's query tensor map: a 128-row box of one head, or with GQA
 // packing 128 / G rows of G consecutive heads.
 int make_q_map(CUtensorMap* map, const void* q, int B, int H, int N, int D, const int64_t* strides, int dtype,
-               int pack) {
-  return pack > 1 ? make_map(map, q, B, H, N, D, strides, 128 / pack, dtype, pack)
-                  : make_map(map, q, B, H, N, D, strides, 128, dtype);
+               int pack, int extent = 0) {
+  return pack > 1 ? make_map(map, q, B, H, N, D, strides, 128 / pack, dtype, pack, extent)
+                  : make_map(map, q, B, H, N, D, strides, 128, dtype, 1, extent);
 }
 
 int fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
@@ -501,6 +504,125 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   return launch_fwd(a, D);
 }
 
+// ---------------------------------------------------------------------------
+// Value head size Dv different from the query/key head size D (the
+// reference hands these inputs to PyTorch, attention.py:639-646).  The
+// kernels run at width W = max(D, Dv): the narrower operands are read
+// through tensor maps whose extent is their own width, so the TMA fills
+// the missing columns with zeros -- zero columns of Q and K leave Q K^T
+// unchanged, zero columns of V and dO give zero columns of O, dP's
+// reduction is unchanged and the padded gradient columns are zero -- and
+// the kernels store only the first D columns of dQ / dK and the first Dv of
+// O / dV (AttnShape::qk_cols, v_cols).  The MMAs on the padded columns are
+// wasted work: W = max(D, Dv) sets the cost.
+int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
+                  int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                  const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal, void* stream,
+                  int dtype) {
+  if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  const int W = D > Dv ? D : Dv;
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides || !o_strides) return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
+  FwdArgs a;
+  const int pack = gqa_pack(Hq, Hkv, Nq);
+  if ((rc = make_q_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, dtype, pack, D))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, 128, dtype, 1, D))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, 128, dtype, 1, Dv))) return rc;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, 0, 0);
+  a.shape.pack_g = pack;
+  a.shape.qk_cols = D;
+  a.shape.v_cols = Dv;
+  a.dtype = dtype;
+  a.o = o;
+  a.o_sb = o_strides[0];
+  a.o_sh = o_strides[1];
+  a.o_sn = o_strides[2];
+  a.lse = lse;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_fwd(a, W);
+}
+
+int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
+                  void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B, int Hq, int Hkv, int Nq, int Nk,
+                  int D, int Dv, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                  const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+                  const int64_t* dk_strides, const int64_t* dv_strides, float softmax_scale, int causal,
+                  int deterministic, void* stream, int dtype) {
+  if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  const int W = D > Dv ? D : Dv;
+  int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv || !delta) return FA_ERR_BAD_SHAPE;
+  if (!q_strides || !k_strides || !v_strides || !o_strides || !do_strides || !dq_strides || !dk_strides ||
+      !dv_strides)
+    return FA_ERR_BAD_SHAPE;
+  if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
+  const bool fused = W <= 64 && !deterministic;
+  if (fused && !dq_accum) return FA_ERR_BAD_SHAPE;
+  if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2) || !out_strides_ok(dq, dq_strides, 2) ||
+      !out_strides_ok(dk, dk_strides, 2) || !out_strides_ok(dv, dv_strides, 2) || !aligned16(delta) ||
+      (fused && !aligned16(dq_accum)))
+    return FA_ERR_MISALIGNED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Delta = rowsum(O * dO) over the Dv columns
+  if ((rc = launch_bwd_delta(o, o_strides[0], o_strides[1], o_strides[2], dO, do_strides[0], do_strides[1],
+                             do_strides[2], delta, nullptr, B, Hq, Nq, Dv, dtype, st)))
+    return rc;
+  BwdArgs a;
+  a.dtype = dtype;
+  a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, 0, 0);
+  a.shape.qk_cols = D;
+  a.shape.v_cols = Dv;
+  a.lse = lse;
+  a.delta = delta;
+  a.dk = dk;
+  a.dv = dv;
+  a.dk_sb = dk_strides[0];
+  a.dk_sh = dk_strides[1];
+  a.dk_sn = dk_strides[2];
+  a.dv_sb = dv_strides[0];
+  a.dv_sh = dv_strides[1];
+  a.dv_sn = dv_strides[2];
+  a.accumulate_fp32 = 0;
+  a.stream = st;
+  if (fused) {
+    // the (B, Hq, Nq, W) fp32 dQ accumulator starts at zero
+    if (cudaMemsetAsync(dq_accum, 0, sizeof(float) * size_t(B) * Hq * Nq * W, st) != cudaSuccess)
+      return FA_ERR_LAUNCH;
+    if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, dkdv_cfg::BQ_WIDE, dtype, 1, D))) return rc;
+    if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, W, do_strides, dkdv_cfg::BQ_WIDE, dtype, 1, Dv))) return rc;
+    if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, dkdv_cfg::BM, dtype, 1, D))) return rc;
+    if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, dkdv_cfg::BM, dtype, 1, Dv))) return rc;
+    CUtensorMap tmap_dq;
+    if ((rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, W))) return rc;
+    a.dq = dq_accum;
+    a.dq_sb = a.dq_sh = a.dq_sn = 0;
+    if ((rc = launch_bwd_fused(a, tmap_dq, W))) return rc;
+    return launch_dq_convert(dq_accum, dq, dq_strides[0], dq_strides[1], dq_strides[2], B, Hq, Nq, D, dtype, st, W);
+  }
+  // split path: dQ kernel, then dK/dV kernel
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, dq_cfg::BM, dtype, 1, D))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, W, do_strides, dq_cfg::BM, dtype, 1, Dv))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, dq_cfg::BN, dtype, 1, D))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, dq_cfg::BN, dtype, 1, Dv))) return rc;
+  a.dq = dq;
+  a.dq_sb = dq_strides[0];
+  a.dq_sh = dq_strides[1];
+  a.dq_sn = dq_strides[2];
+  if ((rc = launch_bwd_dq(a, W))) return rc;
+  const int bq = W <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
+  if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, bq, dtype, 1, D))) return rc;
+  if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, W, do_strides, bq, dtype, 1, Dv))) return rc;
+  if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, dkdv_cfg::BM, dtype, 1, D))) return rc;
+  if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, dkdv_cfg::BM, dtype, 1, Dv))) return rc;
+  a.dq = nullptr;
+  a.dq_sb = a.dq_sh = a.dq_sn = 0;
+  return launch_bwd_dkdv(a, W);
+}
+
 }  // namespace
 }  // namespace fa
 
@@ -696,4 +818,42 @@ extern "C" const char* fa_status_string(int code) {
   }
 }
 
-extern "C" int fa_version(void) { return 10300; }
+// Value head size different from the query/key head size.
+extern "C" int fa_fwd_vdim(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                           int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                           const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
+                           void* stream) {
+  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                       softmax_scale, causal, stream, DT_F16);
+}
+extern "C" int fa_fwd_vdim_bf16(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                                int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                float softmax_scale, int causal, void* stream) {
+  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                       softmax_scale, causal, stream, DT_BF16);
+}
+extern "C" int fa_bwd_vdim(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                           const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B,
+                           int Hq, int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                           const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                           const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                           const int64_t* dv_strides, float softmax_scale, int causal, int deterministic,
+                           void* stream) {
+  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                       k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
+                       causal, deterministic, stream, DT_F16);
+}
+extern "C" int fa_bwd_vdim_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B,
+                                int Hq, int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                                const int64_t* dv_strides, float softmax_scale, int causal, int deterministic,
+                                void* stream) {
+  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                       k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
+                       causal, deterministic, stream, DT_BF16);
+}
+
+extern "C" int fa_version(void) { return 10400; }

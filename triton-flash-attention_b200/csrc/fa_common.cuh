@@ -71,6 +71,13 @@ struct AttnShape {
   // Sliding window (causal only): when window > 0, a query sees only the
   // window keys ending at its own position, j > pos - window.
   int window;
+  // Columns of the outputs the kernels store: qk_cols of dQ / dK, v_cols of
+  // O / dV.  The kernels compute at their template width D; a narrower
+  // tensor (value head size != query/key head size) is read through a tensor
+  // map whose extent is its own width, so the TMA fills the missing columns
+  // with zeros (they add nothing to Q K^T, P V or the gradients), and its
+  // output columns at or past the width are not stored.  Multiples of 32.
+  int qk_cols, v_cols;
 };
 
 // Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of

@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
-        if (row_ok) {
+        if (row_ok && cc * 32 < shp.v_cols) {
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 pk;

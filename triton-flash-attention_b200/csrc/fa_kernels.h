@@ -64,8 +64,9 @@ int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_
                      int N, int D, int dtype, cudaStream_t stream);
 // Fused dK/dV + dQ backward (D <= 64); tmap_dq maps the fp32 accumulator.
 int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D);
+// acc_w: the accumulator's row width (0: D); dq receives its first D columns.
 int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
-                      int dtype, cudaStream_t stream);
+                      int dtype, cudaStream_t stream, int acc_w = 0);
 int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
                          int D, int dtype, cudaStream_t stream);
 
