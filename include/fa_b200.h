@@ -327,6 +327,58 @@ FA_API int fa_bwd_vdim_bf16(const void* q, const void* k, const void* v, const v
                             const int64_t* dk_strides, const int64_t* dv_strides,
                             float softmax_scale, int causal, int deterministic, void* stream);
 
+/* Dense boolean attention masks.  No counterpart in the reference
+ * (README.md:93: "Dropout and arbitrary attention masks are not currently
+ * implemented").  fa_mask_pack turns a byte-per-position mask (a torch.bool
+ * tensor: nonzero = the key takes part) of Bm x Hm x Nq x Nk positions with
+ * element strides {batch, head, query, key} (0 broadcasts) into two
+ * contiguous uint32 bit matrices:
+ *   mask_bits   (Bm, Hm, Nq, roundup(Nk, 128) / 32): bit k & 31 of word k >> 5
+ *               of row q is position (q, k);
+ *   mask_bits_t (Bm, Hm, Nk, roundup(Nq, 128) / 32): the transpose.
+ * Bits past Nq / Nk are zero.  Both buffers 16-byte aligned. */
+FA_API int fa_mask_pack(const void* mask, int Bm, int Hm, int Nq, int Nk, const int64_t* mask_strides,
+                        uint32_t* mask_bits, uint32_t* mask_bits_t, void* stream);
+/* fa_fwd_vdim / fa_bwd_vdim with a packed mask: key k is visible to query q
+ * of head h, batch b only if its bit is set (and, with causal != 0, also
+ * k <= q).  mask_strides / mask_t_strides are word strides {batch, head,
+ * row} of mask_bits / mask_bits_t (0 broadcasts over batches or heads; rows
+ * at least the padded width; multiples of 4).  A query row that sees no key
+ * gets o = 0 and lse = -inf (PyTorch's SDPA gives NaN there) and zero
+ * gradients.  The forward reads mask_bits, the backward both. */
+FA_API int fa_fwd_masked(const void* q, const void* k, const void* v, void* o, float* lse,
+                         int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                         const int64_t* q_strides, const int64_t* k_strides,
+                         const int64_t* v_strides, const int64_t* o_strides,
+                         const uint32_t* mask_bits, const int64_t* mask_strides,
+                         float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_masked(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                         const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                         int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                         const int64_t* q_strides, const int64_t* k_strides,
+                         const int64_t* v_strides, const int64_t* o_strides,
+                         const int64_t* do_strides, const int64_t* dq_strides,
+                         const int64_t* dk_strides, const int64_t* dv_strides,
+                         const uint32_t* mask_bits, const int64_t* mask_strides,
+                         const uint32_t* mask_bits_t, const int64_t* mask_t_strides,
+                         float softmax_scale, int causal, int deterministic, void* stream);
+FA_API int fa_fwd_masked_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                              int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                              const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides,
+                              const uint32_t* mask_bits, const int64_t* mask_strides,
+                              float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_masked_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                              const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                              int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                              const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides,
+                              const int64_t* do_strides, const int64_t* dq_strides,
+                              const int64_t* dk_strides, const int64_t* dv_strides,
+                              const uint32_t* mask_bits, const int64_t* mask_strides,
+                              const uint32_t* mask_bits_t, const int64_t* mask_t_strides,
+                              float softmax_scale, int causal, int deterministic, void* stream);
+
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
  * low byte and the barrier site in bits 8..15.  Synchronises the device. */
@@ -337,7 +389,8 @@ FA_API const char* fa_status_string(int code);
 
 /* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
  * 1.2.0 the fused backward, 1.3.0 packed variable-length batches and the
- * paged K/V forward, 1.4.0 value head sizes different from D). */
+ * paged K/V forward, 1.4.0 value head sizes different from D, 1.5.0 dense
+ * boolean masks). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

@@ -72,8 +72,12 @@ def causal_mask(nq: int, nk: int, q_offset: int = 0, k_offset: int = 0, window: 
 
 
 def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None,
-                   q_offset: int = 0, k_offset: int = 0, window: int = 0):
+                   q_offset: int = 0, k_offset: int = 0, window: int = 0, mask=None):
     """Dense attention in float64 (the math behind attention.py:774-786).
+
+    ``mask`` (optional) is a bool array broadcastable to (B, Hq, Nq, Nk):
+    False hides the key, as ``attn_mask`` of PyTorch's SDPA (combined with
+    ``causal`` by AND).
 
     Returns a dict with ``o``, ``lse`` (natural log), ``lse2`` (base-2 log of
     the row sum of exp2(scale*log2(e)*s), the unit the reference saves,
@@ -93,6 +97,8 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
     if causal:
         m = causal_mask(nq, nk, q_offset, k_offset, window)
         s = np.where(m[None, None], s, -np.inf)
+    if mask is not None:
+        s = np.where(np.broadcast_to(np.asarray(mask, dtype=bool), s.shape), s, -np.inf)
     mx = s.max(axis=-1, keepdims=True)
     mx_safe = np.where(np.isfinite(mx), mx, 0.0)
     e = np.exp(s - mx_safe)
@@ -112,6 +118,25 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
         dve = np.einsum("bhqk,bhqd->bhkd", p, do)
         out.update(delta=delta, dq=dq, dk=_reduce_kv(dke, hkv), dv=_reduce_kv(dve, hkv))
     return out
+
+
+def mask_bits_reference(mask):
+    """The bit rows the library packs a bool mask (Bm, Hm, Nq, Nk) into
+    (fa_mask_pack): ``bits`` (Bm, Hm, Nq, Wk) with bit k & 31 of word k >> 5
+    of row q set iff mask[..., q, k], and ``bits_t`` (Bm, Hm, Nk, Wq) its
+    transpose; Wk = roundup(Nk, 128) / 32, Wq likewise, padding bits zero.
+    No counterpart in the reference (it has no masks, README.md:93)."""
+    m = np.asarray(mask, dtype=bool)
+    bm, hm, nq, nk = m.shape
+    weights = np.left_shift(np.uint64(1), np.arange(32, dtype=np.uint64))
+
+    def pack(rows, n_rows, n_cols):
+        words = (n_cols + 127) // 128 * 4
+        padded = np.zeros((bm, hm, n_rows, words * 32), dtype=np.uint64)
+        padded[..., :n_cols] = rows
+        return (padded.reshape(bm, hm, n_rows, words, 32) * weights).sum(axis=-1).astype(np.uint32)
+
+    return pack(m, nq, nk), pack(np.swapaxes(m, 2, 3), nk, nq)
 
 
 def sdpa_varlen_reference(q, k, v, cu_q, cu_k, *, causal: bool, scale: float | None = None, do=None,

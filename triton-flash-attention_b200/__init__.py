@@ -24,6 +24,12 @@ from .attention import (
     scaled_dot_product_attention,
 )
 from .flops import attention_flops, delta_bytes, memory_model
+from .masks import (
+    B200MaskedAttention,
+    attention_backward_masked,
+    attention_forward_masked,
+    pack_attention_mask,
+)
 from .varlen import (
     B200VarlenAttention,
     paged_attention_forward,
@@ -35,6 +41,7 @@ from .varlen import (
 
 __all__ = [
     "B200Attention",
+    "B200MaskedAttention",
     "B200VarlenAttention",
     "DispatchDecision",
     "SUPPORTED_HEAD_DIMS",
@@ -43,15 +50,18 @@ __all__ = [
     "attention_backward_dkdv",
     "attention_backward_dq",
     "attention_backward_fused",
+    "attention_backward_masked",
     "attention_backward_vdim",
     "attention_delta",
     "attention_flops",
     "attention_forward",
+    "attention_forward_masked",
     "attention_forward_vdim",
     "delta_bytes",
     "explain_dispatch",
     "fused_backward_enabled",
     "memory_model",
+    "pack_attention_mask",
     "paged_attention_forward",
     "scaled_dot_product_attention",
     "scaled_dot_product_attention_paged",

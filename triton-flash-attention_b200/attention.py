@@ -309,14 +309,21 @@ TritonAttention = B200Attention
 
 
 def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, scale: float | None = None,
-                                 enable_gqa: bool = False, backend: Backend = "auto") -> torch.Tensor:
+                                 enable_gqa: bool = False, backend: Backend = "auto",
+                                 attn_mask: torch.Tensor | None = None) -> torch.Tensor:
     """Scaled dot-product attention on the B200 kernels (attention.py:789-845).
 
     Forward and backward, causal and bidirectional attention, arbitrary
     positive sequence lengths, GQA.  ``backend`` is kept for drop-in
     compatibility: ``"auto"``, ``"triton"`` (the reference's name for its
     custom kernel) and ``"cuda"`` all select the B200 kernels.  Inputs they
-    cannot serve raise ``RuntimeError`` -- there is no PyTorch fallback."""
+    cannot serve raise ``RuntimeError`` -- there is no PyTorch fallback.
+
+    ``attn_mask`` (an addition; the reference has no masks, README.md:93) is
+    a bool tensor broadcastable to (batch, query heads, query length, key
+    length), ``True`` where the key takes part, as in PyTorch's SDPA; with
+    ``is_causal`` a key must pass both.  A query row that sees no key gets
+    zeros (PyTorch returns NaN)."""
     if backend == "torch":
         raise RuntimeError(
             "backend='torch' (the PyTorch SDPA fallback) is not part of this package; "
@@ -333,8 +340,14 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
     decision = explain_dispatch(query, key, value, enable_gqa=enable_gqa)
     if decision.backend != "cuda":
         raise RuntimeError(f"B200 CUDA backend is unavailable: {decision.reason}")
+    if attn_mask is not None:
+        from .masks import validate_attention_mask
+        validate_attention_mask(attn_mask, query, key)
     query_c = query.contiguous()
     key_c = key.contiguous()
     value_c = value.contiguous()
     softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
+    if attn_mask is not None:
+        from .masks import B200MaskedAttention
+        return B200MaskedAttention.apply(query_c, key_c, value_c, attn_mask, is_causal, softmax_scale)
     return B200Attention.apply(query_c, key_c, value_c, is_causal, softmax_scale)

@@ -133,7 +133,7 @@ struct ItemCursor {
 
 }  // namespace bkv
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS>
 __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -412,6 +412,16 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       for (int it = ((gi & 1) == w ? 0 : 1); it < wt.n_items; it += 2) {
         const int g = gi + it;
         const int s = g % C::NST;
+        // dense boolean mask: this key row's bits of the item's queries (a
+        // row past the keys reads the last one)
+        uint2 mw;
+        if constexpr (BITS) {
+          const int h = wt.kvh * group + it / wt.per_head;
+          const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
+          const int qm = (wt.i_start + it % wt.per_head) * BQ;
+          mw = __ldg(reinterpret_cast<const uint2*>(shp.mask_t + (long long)wt.b * shp.mt_sb +
+                                                    (long long)h * shp.mt_sh + (long long)kr * shp.mt_sn + (qm >> 5)));
+        }
         if (!mbar_wait_warp(st_full + w, uint32_t(g >> 1) & 1, ctl, 80 + w)) { ok = false; break; }
         // the stage's lse2/Delta values: their phase completed before st_full
         if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 82 + w)) { ok = false; break; }
@@ -436,6 +446,10 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
 #pragma unroll
             for (int c = 0; c < BQ; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
           }
+        }
+        if constexpr (BITS) {
+          const uint32_t words[2] = {mw.x, mw.y};
+          apply_mask_bits<BQ>(st, words);
         }
         // stage values are stored negated: -lse2 and -Delta
         const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ);
@@ -624,7 +638,7 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 }  // namespace bkvw
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS>
 __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
     fa_bwd_dkdv_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                             const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -927,6 +941,16 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         const int s = g % C::NST;
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
         if (w == 0) {
+          // dense boolean mask: this key row's bits of the item's 128 queries
+          // (a row past the keys reads the last one)
+          uint4 mw;
+          if constexpr (BITS) {
+            const int h = wt.kvh * group + it / wt.per_head;
+            const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
+            mw = __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb +
+                                                      (long long)h * shp.mt_sh + (long long)kr * shp.mt_sn +
+                                                      (q0 >> 5)));
+          }
           if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 180)) { ok = false; break; }
           // the stage's -lse2/-Delta: its phase completed before S^T was issued
           if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 182)) { ok = false; break; }
@@ -952,6 +976,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
 #pragma unroll
                 for (int c = 0; c < 64; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
               }
+            }
+            if constexpr (BITS) {
+              const uint32_t words[2] = {hh ? mw.z : mw.x, hh ? mw.w : mw.y};
+              apply_mask_bits<64>(st, words);
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];
@@ -1068,10 +1096,10 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS = false>
 int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   using C = bkvw::Cfg<D>;
-  auto kern = fa_bwd_dkdv_wide_kernel<D, DT, VL>;
+  auto kern = fa_bwd_dkdv_wide_kernel<D, DT, VL, BITS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_kt = (a.shape.Nk + bkvw::BM - 1) / bkvw::BM;
@@ -1084,10 +1112,10 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS = false>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
-  auto kern = fa_bwd_dkdv_kernel<D, DT, VL>;
+  auto kern = fa_bwd_dkdv_kernel<D, DT, VL, BITS>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -1114,8 +1142,10 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
 template <int D, int DT>
 int launch_bwd_dkdv_l(const BwdArgs& a) {
   if constexpr (D == 128) {
+    if (a.shape.mask) return launch_bwd_dkdv_t<D, DT, false, true>(a);  // dense layout only
     return a.shape.cu_q ? launch_bwd_dkdv_t<D, DT, true>(a) : launch_bwd_dkdv_t<D, DT, false>(a);
   } else {
+    if (a.shape.mask) return launch_bwd_dkdv_wide_t<D, DT, false, true>(a);
     return a.shape.cu_q ? launch_bwd_dkdv_wide_t<D, DT, true>(a) : launch_bwd_dkdv_wide_t<D, DT, false>(a);
   }
 }

@@ -89,7 +89,7 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 }  // namespace bdqw
 
-template <int D, int DT, bool WIN>
+template <int D, int DT, bool WIN, bool BITS>
 __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     fa_bwd_dq_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -316,10 +316,18 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         lim = c < lim ? int(c) : lim;
         if (WIN) lo = c - shp.window + 1;
       }
+      // dense boolean mask: this row's bit words (a row past the queries reads the last one)
+      const uint32_t* mrow = nullptr;
+      if constexpr (BITS) {
+        const int rr = r < cur.sq.nq ? r : cur.sq.nq - 1;
+        mrow = shp.mask + (long long)cur.b * shp.mask_sb + (long long)cur.h * shp.mask_sh + (long long)rr * shp.mask_sn;
+      }
       const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
       const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
       for (int j = 0; j < cur.n_kv; ++j) {
         const int g = gj + j;
+        uint2 mw;
+        if constexpr (BITS) mw = __ldg(reinterpret_cast<const uint2*>(mrow + (((cur.kt0 + j) * BN + 64 * w) >> 5)));
         if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 150 + w)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * w);
@@ -335,6 +343,10 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           const long long lo_j = lo - key0;
 #pragma unroll
           for (int c = 0; c < 64; ++c) sv[c] = c >= lo_j ? sv[c] : -INFINITY;
+        }
+        if constexpr (BITS) {
+          const uint32_t words[2] = {mw.x, mw.y};
+          apply_mask_bits<64>(sv, words);
         }
         uint32_t pk_p[32];
 #pragma unroll
@@ -423,10 +435,10 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool WIN>
+template <int D, int DT, bool WIN, bool BITS = false>
 int launch_bwd_dq_wide_t(const BwdArgs& a) {
   using C = bdqw::Cfg<D>;
-  auto kern = fa_bwd_dq_wide_kernel<D, DT, WIN>;
+  auto kern = fa_bwd_dq_wide_kernel<D, DT, WIN, BITS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
@@ -439,9 +451,10 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-// Sliding-window and plain masks are separate instantiations.
+// Sliding-window, boolean and plain masks are separate instantiations.
 template <int D, int DT>
 int launch_bwd_dq_l(const BwdArgs& a) {
+  if (a.shape.mask) return launch_bwd_dq_wide_t<D, DT, false, true>(a);  // dense, no window
   return a.shape.window > 0 ? launch_bwd_dq_wide_t<D, DT, true>(a) : launch_bwd_dq_wide_t<D, DT, false>(a);
 }
 

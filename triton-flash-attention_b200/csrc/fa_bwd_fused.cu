@@ -153,7 +153,7 @@ struct ItemCursor {
 };
 }  // namespace bfz
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS>
 __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     fa_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                         const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -475,6 +475,16 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         const int s = g % C::NST;
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
         if (w == 0) {
+          // dense boolean mask: this key row's bits of the item's 128 queries
+          // (a row past the keys reads the last one)
+          uint4 mw;
+          if constexpr (BITS) {
+            const int h = wt.kvh * group + it / wt.per_head;
+            const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
+            mw = __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb +
+                                                      (long long)h * shp.mt_sh + (long long)kr * shp.mt_sn +
+                                                      (q0 >> 5)));
+          }
           if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 220)) { ok = false; break; }
           // the stage's -lse2/-Delta: its phase completed before S^T was issued
           if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 221)) { ok = false; break; }
@@ -500,6 +510,10 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
 #pragma unroll
                 for (int c = 0; c < 64; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
               }
+            }
+            if constexpr (BITS) {
+              const uint32_t words[2] = {hh ? mw.z : mw.x, hh ? mw.w : mw.y};
+              apply_mask_bits<64>(st, words);
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];
@@ -686,10 +700,10 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool VL>
+template <int D, int DT, bool VL, bool BITS = false>
 int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
   using C = bfz::Cfg<D>;
-  auto kern = fa_bwd_fused_kernel<D, DT, VL>;
+  auto kern = fa_bwd_fused_kernel<D, DT, VL, BITS>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -715,6 +729,7 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
 // dense kernels carry no per-batch offset arithmetic.
 template <int D, int DT>
 int launch_bwd_fused_l(const BwdArgs& a, const CUtensorMap& tmap_dq) {
+  if (a.shape.mask) return launch_bwd_fused_t<D, DT, false, true>(a, tmap_dq);  // dense layout only
   return a.shape.cu_q ? launch_bwd_fused_t<D, DT, true>(a, tmap_dq) : launch_bwd_fused_t<D, DT, false>(a, tmap_dq);
 }
 

@@ -114,6 +114,10 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.window = 0;
   s.qk_cols = 1 << 20;  // no narrower tensor: every column is stored
   s.v_cols = 1 << 20;
+  s.mask = nullptr;
+  s.mask_sb = s.mask_sh = s.mask_sn = 0;
+  s.mask_t = nullptr;
+  s.mt_sb = s.mt_sh = s.mt_sn = 0;
   return s;
 }
 
@@ -515,10 +519,27 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
 // the kernels store only the first D columns of dQ / dK and the first Dv of
 // O / dV (AttnShape::qk_cols, v_cols).  The MMAs on the padded columns are
 // wasted work: W = max(D, Dv) sets the cost.
+//
+// Dense boolean masks (fa_mask_pack, fa_fwd_masked, fa_bwd_masked; the
+// reference has none, README.md:93): the kernels take the packed bit rows
+// through AttnShape::mask / mask_t, in instantiations of their own.  A mask
+// goes with the dense layout, no GQA packing of the forward, no window and
+// no position offsets.
+
+// A packed mask's word strides {batch, head, row}: non-negative, 16-byte
+// aligned rows of at least `words` words.
+bool mask_ok(const uint32_t* bits, const int64_t* st, int words) {
+  if (!bits || !st || !aligned16(bits)) return false;
+  if (st[0] < 0 || st[1] < 0 || st[2] < words) return false;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] % 4 != 0) return false;
+  return true;
+}
+
 int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
                   int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
                   const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal, void* stream,
-                  int dtype) {
+                  int dtype, const uint32_t* mask = nullptr, const int64_t* mask_strides = nullptr) {
   if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   const int W = D > Dv ? D : Dv;
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
@@ -526,8 +547,9 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
   if (!q || !k || !v || !o || !lse || !q_strides || !k_strides || !v_strides || !o_strides) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
+  if (mask && !mask_ok(mask, mask_strides, (Nk + 127) / 128 * 4)) return FA_ERR_MISALIGNED;
   FwdArgs a;
-  const int pack = gqa_pack(Hq, Hkv, Nq);
+  const int pack = mask ? 0 : gqa_pack(Hq, Hkv, Nq);
   if ((rc = make_q_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, dtype, pack, D))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, 128, dtype, 1, D))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, 128, dtype, 1, Dv))) return rc;
@@ -535,6 +557,12 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
   a.shape.pack_g = pack;
   a.shape.qk_cols = D;
   a.shape.v_cols = Dv;
+  if (mask) {
+    a.shape.mask = mask;
+    a.shape.mask_sb = mask_strides[0];
+    a.shape.mask_sh = mask_strides[1];
+    a.shape.mask_sn = mask_strides[2];
+  }
   a.dtype = dtype;
   a.o = o;
   a.o_sb = o_strides[0];
@@ -550,7 +578,9 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
                   int D, int Dv, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                   const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
                   const int64_t* dk_strides, const int64_t* dv_strides, float softmax_scale, int causal,
-                  int deterministic, void* stream, int dtype) {
+                  int deterministic, void* stream, int dtype, const uint32_t* mask = nullptr,
+                  const int64_t* mask_strides = nullptr, const uint32_t* mask_t = nullptr,
+                  const int64_t* mask_t_strides = nullptr) {
   if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   const int W = D > Dv ? D : Dv;
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
@@ -566,6 +596,9 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
       !out_strides_ok(dk, dk_strides, 2) || !out_strides_ok(dv, dv_strides, 2) || !aligned16(delta) ||
       (fused && !aligned16(dq_accum)))
     return FA_ERR_MISALIGNED;
+  if ((mask || mask_t) && (!mask_ok(mask, mask_strides, (Nk + 127) / 128 * 4) ||
+                           !mask_ok(mask_t, mask_t_strides, (Nq + 127) / 128 * 4)))
+    return FA_ERR_MISALIGNED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Delta = rowsum(O * dO) over the Dv columns
   if ((rc = launch_bwd_delta(o, o_strides[0], o_strides[1], o_strides[2], dO, do_strides[0], do_strides[1],
@@ -576,6 +609,16 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, 0, 0);
   a.shape.qk_cols = D;
   a.shape.v_cols = Dv;
+  if (mask) {
+    a.shape.mask = mask;
+    a.shape.mask_sb = mask_strides[0];
+    a.shape.mask_sh = mask_strides[1];
+    a.shape.mask_sn = mask_strides[2];
+    a.shape.mask_t = mask_t;
+    a.shape.mt_sb = mask_t_strides[0];
+    a.shape.mt_sh = mask_t_strides[1];
+    a.shape.mt_sn = mask_t_strides[2];
+  }
   a.lse = lse;
   a.delta = delta;
   a.dk = dk;
@@ -856,4 +899,77 @@ extern "C" int fa_bwd_vdim_bf16(const void* q, const void* k, const void* v, con
                        causal, deterministic, stream, DT_BF16);
 }
 
-extern "C" int fa_version(void) { return 10400; }
+// Dense boolean masks.
+extern "C" int fa_mask_pack(const void* mask, int Bm, int Hm, int Nq, int Nk, const int64_t* mask_strides,
+                            uint32_t* bits, uint32_t* bits_t, void* stream) {
+  if (Bm <= 0 || Hm <= 0 || Nq <= 0 || Nk <= 0 || !mask || !mask_strides || !bits || !bits_t) return FA_ERR_BAD_SHAPE;
+  for (int i = 0; i < 4; ++i)
+    if (mask_strides[i] < 0) return FA_ERR_BAD_SHAPE;
+  if (!aligned16(bits) || !aligned16(bits_t)) return FA_ERR_MISALIGNED;
+  return launch_mask_pack(mask, mask_strides[0], mask_strides[1], mask_strides[2], mask_strides[3], Bm, Hm, Nq, Nk,
+                          bits, bits_t, static_cast<cudaStream_t>(stream));
+}
+static int fwd_masked_entry(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                            int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, const int64_t* o_strides, const uint32_t* mask_bits,
+                            const int64_t* mask_strides, float softmax_scale, int causal, void* stream, int dtype) {
+  if (!mask_bits || !mask_strides) return FA_ERR_BAD_SHAPE;
+  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                       softmax_scale, causal, stream, dtype, mask_bits, mask_strides);
+}
+extern "C" int fa_fwd_masked(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                             int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, const int64_t* o_strides, const uint32_t* mask_bits,
+                             const int64_t* mask_strides, float softmax_scale, int causal, void* stream) {
+  return fwd_masked_entry(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                          mask_bits, mask_strides, softmax_scale, causal, stream, DT_F16);
+}
+extern "C" int fa_fwd_masked_bf16(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                                  int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                  const uint32_t* mask_bits, const int64_t* mask_strides, float softmax_scale,
+                                  int causal, void* stream) {
+  return fwd_masked_entry(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                          mask_bits, mask_strides, softmax_scale, causal, stream, DT_BF16);
+}
+static int bwd_masked_entry(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                            const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B,
+                            int Hq, int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                            const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                            const int64_t* dv_strides, const uint32_t* mask_bits, const int64_t* mask_strides,
+                            const uint32_t* mask_bits_t, const int64_t* mask_t_strides, float softmax_scale,
+                            int causal, int deterministic, void* stream, int dtype) {
+  if (!mask_bits || !mask_strides || !mask_bits_t || !mask_t_strides) return FA_ERR_BAD_SHAPE;
+  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                       k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
+                       causal, deterministic, stream, dtype, mask_bits, mask_strides, mask_bits_t, mask_t_strides);
+}
+extern "C" int fa_bwd_masked(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                             const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B,
+                             int Hq, int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                             const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                             const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                             const int64_t* dv_strides, const uint32_t* mask_bits, const int64_t* mask_strides,
+                             const uint32_t* mask_bits_t, const int64_t* mask_t_strides, float softmax_scale,
+                             int causal, int deterministic, void* stream) {
+  return bwd_masked_entry(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                          k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, mask_bits,
+                          mask_strides, mask_bits_t, mask_t_strides, softmax_scale, causal, deterministic, stream,
+                          DT_F16);
+}
+extern "C" int fa_bwd_masked_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                  const float* lse, void* dq, void* dk, void* dv, float* delta, float* dq_accum,
+                                  int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                  const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                                  const int64_t* dv_strides, const uint32_t* mask_bits, const int64_t* mask_strides,
+                                  const uint32_t* mask_bits_t, const int64_t* mask_t_strides, float softmax_scale,
+                                  int causal, int deterministic, void* stream) {
+  return bwd_masked_entry(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                          k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, mask_bits,
+                          mask_strides, mask_bits_t, mask_t_strides, softmax_scale, causal, deterministic, stream,
+                          DT_BF16);
+}
+
+extern "C" int fa_version(void) { return 10500; }

@@ -78,7 +78,26 @@ struct AttnShape {
   // with zeros (they add nothing to Q K^T, P V or the gradients), and its
   // output columns at or past the width are not stored.  Multiples of 32.
   int qk_cols, v_cols;
+  // Dense boolean mask (dense layout only): when mask is not null, key k is
+  // visible to query row r of head h in batch b only if bit (k & 31) of word
+  // mask[b * mask_sb + h * mask_sh + r * mask_sn + (k >> 5)] is set; a row
+  // holds roundup(Nk, 128) / 32 words, so a 128-key tile is one aligned
+  // 16-byte load.  mask_t is the same mask transposed (a row per key, a bit
+  // per query, roundup(Nq, 128) / 32 words a row) for the kernels whose
+  // threads own key rows.  Strides in words; a stride of 0 broadcasts.
+  const uint32_t* mask;
+  long long mask_sb, mask_sh, mask_sn;
+  const uint32_t* mask_t;
+  long long mt_sb, mt_sh, mt_sn;
 };
+
+// Hides the columns of s whose bit in words is clear (bit c & 31 of word
+// c >> 5; 1 = visible).
+template <int N>
+__device__ __forceinline__ void apply_mask_bits(float (&s)[N], const uint32_t (&words)[(N + 31) / 32]) {
+#pragma unroll
+  for (int c = 0; c < N; ++c) s[c] = ((words[c >> 5] >> (c & 31)) & 1u) ? s[c] : -INFINITY;
+}
 
 // Rows of batch b: query rows [q0, q0 + nq) and key rows [k0, k0 + nk) of
 // the tensors, and tb, b's coordinate in the 4-D tensor maps (0 when packed).

@@ -152,7 +152,7 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
 
 }  // namespace fwd
 
-template <int D, int DT, bool PACK, bool WIN>
+template <int D, int DT, bool PACK, bool WIN, bool BITS>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
@@ -468,6 +468,12 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         lim = c < lim ? int(c) : lim;  // may be negative: no visible key
         if (WIN) lo = c - shp.window + 1;
       }
+      // dense boolean mask: this row's bit words (a row past the queries reads the last one)
+      const uint32_t* mrow = nullptr;
+      if constexpr (BITS) {
+        const int rr = r < w.sq.nq ? r : w.sq.nq - 1;
+        mrow = shp.mask + (long long)w.b * shp.mask_sb + (long long)hq * shp.mask_sh + (long long)rr * shp.mask_sn;
+      }
       if constexpr (C::SEP_P && TURNS) {
         // empty turns for the leading key tiles the other query tile has and this one lacks
         for (int j = 0; j < js && ok; ++j) {
@@ -479,6 +485,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       float m = -INFINITY;  // running exponent base (scaled log2 units)
       float l = 0.f;        // running row sum of exp2(s * c2 - m)
       for (int j = js; j < nt; ++j) {
+        uint4 mw;
+        if constexpr (BITS) mw = __ldg(reinterpret_cast<const uint4*>(mrow + (w.kt0 + j) * (BN / 32)));
         if (!mbar_wait_warp(s_full + t, uint32_t(cnt) & 1, ctl, 20 + t)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
@@ -499,6 +507,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
           const long long lo_j = lo - key0;
 #pragma unroll
           for (int c = 0; c < BN; ++c) s[c] = c >= lo_j ? s[c] : -INFINITY;
+        }
+        if constexpr (BITS) {
+          const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
+          apply_mask_bits<BN>(s, words);
         }
         // row max: 8 independent 3-input max chains, then a short tree
         float a8[8];
@@ -646,11 +658,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool PACK, bool WIN>
+template <int D, int DT, bool PACK, bool WIN, bool BITS = false>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D, DT, PACK, WIN>;
+  auto kern = fa_fwd_kernel<D, DT, PACK, WIN, BITS>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -673,10 +685,11 @@ int launch_fwd_t(const FwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-// GQA-packed and plain query tiles, and sliding-window and plain masks, are
-// separate instantiations.
+// GQA-packed and plain query tiles, and sliding-window, boolean and plain
+// masks, are separate instantiations.
 template <int D, int DT>
 int launch_fwd_l(const FwdArgs& a) {
+  if (a.shape.mask) return launch_fwd_t<D, DT, false, false, true>(a);  // dense, unpacked, no window
   if (a.shape.window > 0)
     return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, true>(a) : launch_fwd_t<D, DT, false, true>(a);
   return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, false>(a) : launch_fwd_t<D, DT, false, false>(a);

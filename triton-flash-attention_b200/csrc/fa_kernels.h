@@ -67,6 +67,11 @@ int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D);
 // acc_w: the accumulator's row width (0: D); dq receives its first D columns.
 int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
                       int dtype, cudaStream_t stream, int acc_w = 0);
+// Dense boolean mask (bytes, element strides {sb, sh, sq, sk}, Bm x Hm x Nq x
+// Nk) -> bits (Bm, Hm, Nq, roundup(Nk, 128) / 32) and bits_t (Bm, Hm, Nk,
+// roundup(Nq, 128) / 32) uint32 words, contiguous.
+int launch_mask_pack(const void* mask, long long sb, long long sh, long long sq, long long sk, int Bm, int Hm, int Nq,
+                     int Nk, uint32_t* bits, uint32_t* bits_t, cudaStream_t stream);
 int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
                          int D, int dtype, cudaStream_t stream);
 
