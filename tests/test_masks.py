@@ -9,7 +9,8 @@ CPU tests pin the oracle's masked attention against PyTorch's float64 SDPA
 and its bit layout (``mask_bits_reference``) by a round trip, and check the
 Python validation and the ABI's argument checks.  GPU tests:
 * the pack kernel's words equal the oracle's bit for bit (contiguous,
-  broadcast and transposed masks, ragged lengths);
+  broadcast and transposed masks, ragged lengths; both the 4-byte and the
+  byte-wise variant);
 * parity with the float64 oracle through the public API, forward and
   backward, at the equal-width tolerances (O 2e-3, gradients 1e-2), for
   random masks of every broadcast form, with and without causal, self- and
@@ -141,6 +142,7 @@ def _as_u32(t):
     ((1, 1, 129, 1000), 129, 1000, "plain"),
     ((2, 3, 300, 200), 200, 300, "transposed view"),
     ((1, 1, 1, 1), 1, 1, "plain"),
+    ((2, 3, 77, 333), 77, 333, "plain"),  # Nk % 4 != 0: the byte-wise kernel
 ])
 def test_mask_pack_kernel_bitwise(shape, nq, nk, form):
     mask = _random_mask(shape, seed=nq * 7 + nk).cuda()

@@ -408,19 +408,29 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
       // key rows past the batch's keys (the next batch's, when packed) see no query
       const bool key_out = VL && wt.kv0 + rl >= wt.sq.nk;
+      // dense boolean mask: this key row's bits of item i's queries (a row
+      // past the keys reads the last one), loaded one item of this
+      // warpgroup ahead
+      auto mask_words = [&](int i) -> uint2 {
+        const int h = wt.kvh * group + i / wt.per_head;
+        const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
+        const int qi = (wt.i_start + i % wt.per_head) * BQ;
+        return __ldg(reinterpret_cast<const uint2*>(shp.mask_t + (long long)wt.b * shp.mt_sb + (long long)h * shp.mt_sh +
+                                                    (long long)kr * shp.mt_sn + (qi >> 5)));
+      };
+      const int it0 = (gi & 1) == w ? 0 : 1;
+      uint2 mw_next;
+      if constexpr (BITS) {
+        if (it0 < wt.n_items) mw_next = mask_words(it0);
+      }
       // this warpgroup's items of the tile: global parity w
-      for (int it = ((gi & 1) == w ? 0 : 1); it < wt.n_items; it += 2) {
+      for (int it = it0; it < wt.n_items; it += 2) {
         const int g = gi + it;
         const int s = g % C::NST;
-        // dense boolean mask: this key row's bits of the item's queries (a
-        // row past the keys reads the last one)
         uint2 mw;
         if constexpr (BITS) {
-          const int h = wt.kvh * group + it / wt.per_head;
-          const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
-          const int qm = (wt.i_start + it % wt.per_head) * BQ;
-          mw = __ldg(reinterpret_cast<const uint2*>(shp.mask_t + (long long)wt.b * shp.mt_sb +
-                                                    (long long)h * shp.mt_sh + (long long)kr * shp.mt_sn + (qm >> 5)));
+          mw = mw_next;
+          if (it + 2 < wt.n_items) mw_next = mask_words(it + 2);
         }
         if (!mbar_wait_warp(st_full + w, uint32_t(g >> 1) & 1, ctl, 80 + w)) { ok = false; break; }
         // the stage's lse2/Delta values: their phase completed before st_full
@@ -449,7 +459,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         }
         if constexpr (BITS) {
           const uint32_t words[2] = {mw.x, mw.y};
-          apply_mask_bits<BQ>(st, words);
+          if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<BQ>(st, words);
         }
         // stage values are stored negated: -lse2 and -Delta
         const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ);
@@ -936,20 +946,28 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
       const long long cmin_base = (long long)wt.kv0 + rl + shp.k_off - shp.q_off;
       // key rows past the batch's keys (the next batch's, when packed) see no query
       const bool key_out = VL && wt.kv0 + rl >= wt.sq.nk;
+      // dense boolean mask: this key row's bits of item i's 128 queries (a
+      // row past the keys reads the last one), loaded one item ahead
+      auto mask_words = [&](int i) -> uint4 {
+        const int h = wt.kvh * group + i / wt.per_head;
+        const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
+        const int qi = (wt.i_start + i % wt.per_head) * BQ;
+        return __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb + (long long)h * shp.mt_sh +
+                                                    (long long)kr * shp.mt_sn + (qi >> 5)));
+      };
+      uint4 mw_next;
+      if constexpr (BITS) {
+        if (w == 0 && wt.n_items > 0) mw_next = mask_words(0);
+      }
       for (int it = 0; it < wt.n_items && ok; ++it) {
         const int g = gi + it;
         const int s = g % C::NST;
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
         if (w == 0) {
-          // dense boolean mask: this key row's bits of the item's 128 queries
-          // (a row past the keys reads the last one)
           uint4 mw;
           if constexpr (BITS) {
-            const int h = wt.kvh * group + it / wt.per_head;
-            const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
-            mw = __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb +
-                                                      (long long)h * shp.mt_sh + (long long)kr * shp.mt_sn +
-                                                      (q0 >> 5)));
+            mw = mw_next;
+            if (it + 1 < wt.n_items) mw_next = mask_words(it + 1);
           }
           if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 180)) { ok = false; break; }
           // the stage's -lse2/-Delta: its phase completed before S^T was issued
@@ -979,7 +997,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             }
             if constexpr (BITS) {
               const uint32_t words[2] = {hh ? mw.z : mw.x, hh ? mw.w : mw.y};
-              apply_mask_bits<64>(st, words);
+              if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<64>(st, words);
             }
             const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
             uint32_t pk_p[32];

@@ -324,10 +324,19 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       }
       const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
       const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
+      // mask words are loaded one key tile ahead
+      uint2 mw_next;
+      if constexpr (BITS) {
+        if (cur.n_kv > 0) mw_next = __ldg(reinterpret_cast<const uint2*>(mrow + ((cur.kt0 * BN + 64 * w) >> 5)));
+      }
       for (int j = 0; j < cur.n_kv; ++j) {
         const int g = gj + j;
         uint2 mw;
-        if constexpr (BITS) mw = __ldg(reinterpret_cast<const uint2*>(mrow + (((cur.kt0 + j) * BN + 64 * w) >> 5)));
+        if constexpr (BITS) {
+          mw = mw_next;
+          if (j + 1 < cur.n_kv)
+            mw_next = __ldg(reinterpret_cast<const uint2*>(mrow + (((cur.kt0 + j + 1) * BN + 64 * w) >> 5)));
+        }
         if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 150 + w)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * w);
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         }
         if constexpr (BITS) {
           const uint32_t words[2] = {mw.x, mw.y};
-          apply_mask_bits<64>(sv, words);
+          if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<64>(sv, words);
         }
         uint32_t pk_p[32];
 #pragma unroll

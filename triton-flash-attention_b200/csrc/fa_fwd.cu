@@ -484,9 +484,17 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       float m = -INFINITY;  // running exponent base (scaled log2 units)
       float l = 0.f;        // running row sum of exp2(s * c2 - m)
+      // mask words are loaded one key tile ahead, so the load's latency hides behind a tile
+      uint4 mw_next;
+      if constexpr (BITS) {
+        if (js < nt) mw_next = __ldg(reinterpret_cast<const uint4*>(mrow + (w.kt0 + js) * (BN / 32)));
+      }
       for (int j = js; j < nt; ++j) {
         uint4 mw;
-        if constexpr (BITS) mw = __ldg(reinterpret_cast<const uint4*>(mrow + (w.kt0 + j) * (BN / 32)));
+        if constexpr (BITS) {
+          mw = mw_next;
+          if (j + 1 < nt) mw_next = __ldg(reinterpret_cast<const uint4*>(mrow + (w.kt0 + j + 1) * (BN / 32)));
+        }
         if (!mbar_wait_warp(s_full + t, uint32_t(cnt) & 1, ctl, 20 + t)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
@@ -510,7 +518,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         }
         if constexpr (BITS) {
           const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
-          apply_mask_bits<BN>(s, words);
+          // a tile row with every key visible needs no select
+          if ((words[0] & words[1] & words[2] & words[3]) != 0xffffffffu) apply_mask_bits<BN>(s, words);
         }
         // row max: 8 independent 3-input max chains, then a short tree
         float a8[8];
