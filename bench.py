@@ -42,6 +42,8 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
   sequences padded and run dense.  Informational.
 * ``--workload decode``: one query per sequence over a paged K/V cache
   (``scaled_dot_product_attention_paged``), HBM roofline.  Informational.
+* ``--workload masked``: boolean ``attn_mask`` forms (key padding, all
+  true, random) at the C2 shape beside the unmasked call.  Informational.
 """
 
 from __future__ import annotations
@@ -742,6 +744,70 @@ def run_varlen(args) -> None:
     }), flush=True)
 
 
+def run_masked(args) -> None:
+    """Dense boolean masks (no counterpart in the reference): the C2 shape
+    (B4 H16 N4096 D64, fp16), forward and forward+backward through
+    ``scaled_dot_product_attention`` with no mask, a key-padding mask
+    (B, 1, 1, N) hiding each batch's last 512 * (b + 1) keys, a mask with
+    every bit set, and a seeded random (B, 1, N, N) mask of density 0.7, each
+    bidirectional and causal; plus the pack kernel alone on the random mask.
+    The masked times include packing the mask (once per forward).
+    Informational, one JSON line."""
+    import torch
+
+    import triton_flash_attention_b200 as fa
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    q, k, v, do = (torch.randn(B, H, N, D, device=dev, dtype=torch.float16, generator=g) for _ in range(4))
+    q, k, v = (t.requires_grad_() for t in (q, k, v))
+    padding = torch.ones(B, 1, 1, N, dtype=torch.bool, device=dev)
+    for b in range(B):
+        padding[b, ..., N - 512 * (b + 1):] = False
+    masks = {
+        "none": None,
+        "key_padding": padding,
+        "all_true": torch.ones(N, N, dtype=torch.bool, device=dev),
+        "random_0.7": torch.rand(B, 1, N, N, generator=g, device=dev) < 0.7,
+    }
+    steps = max(1, min(args.steps, 20))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    rows = {}
+    for causal in (False, True):
+        for name, m in masks.items():
+            def fwd():
+                with torch.no_grad():
+                    fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m)
+
+            def fwd_bwd():
+                o = fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m)
+                torch.autograd.grad(o, (q, k, v), do)
+
+            rows[f"{'causal' if causal else 'bidirectional'}/{name}"] = {
+                "fwd_ms": round(timed(fwd), 4), "fwd_bwd_ms": round(timed(fwd_bwd), 4)}
+    pack_ms = timed(lambda: fa.pack_attention_mask(masks["random_0.7"], B, H, N, N))
+    print(json.dumps({
+        "workload": "masked", "batch": B, "heads": H, "seq_len": N, "head_dim": D, "dtype": "fp16",
+        "data": "synthetic: seeded N(0,1); seeded masks", "steps": steps, "times": rows,
+        "pack_random_mask_ms": round(pack_ms, 4),
+        "pack_random_mask_gbs": round(B * N * N / (pack_ms * 1e-3) / 1e9, 1),
+        "note": "masked times include fa_mask_pack; key_padding hides 512..2048 trailing keys per batch",
+    }), flush=True)
+
+
 DECODE_B, DECODE_HQ, DECODE_HKV, DECODE_D, DECODE_CTX, DECODE_PAGE = 16, 32, 8, 128, 8192, 64
 
 
@@ -810,11 +876,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--deterministic", action="store_true",
                     help="time the bitwise-reproducible backward (separate dQ and dK/dV kernels)")
-    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen", "decode"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen", "decode", "masked"], default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
                          "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel; "
                          "varlen: a packed batch of ragged sequences beside its padded dense equivalent; "
-                         "decode: one query per sequence over a paged K/V cache")
+                         "decode: one query per sequence over a paged K/V cache; "
+                         "masked: boolean attn_mask forms at the C2 shape")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -831,6 +898,8 @@ def main() -> None:
         run_varlen(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "masked":
+        run_masked(args)
     else:
         run_ours(args)
 

@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
                        const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                        void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh, const long long dk_sn,
                        void* __restrict__ dv_out, const long long dv_sb, const long long dv_sh, const long long dv_sn,
-                       const int accumulate_fp32, const int n_tiles) {
+                       const int accumulate_fp32, const int n_tiles, const MaskBits mk) {
   using namespace bkv;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -415,8 +415,8 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         const int h = wt.kvh * group + i / wt.per_head;
         const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
         const int qi = (wt.i_start + i % wt.per_head) * BQ;
-        return __ldg(reinterpret_cast<const uint2*>(shp.mask_t + (long long)wt.b * shp.mt_sb + (long long)h * shp.mt_sh +
-                                                    (long long)kr * shp.mt_sn + (qi >> 5)));
+        return __ldg(reinterpret_cast<const uint2*>(mk.bits_t + (long long)wt.b * mk.tsb + (long long)h * mk.tsh +
+                                                    (long long)kr * mk.tsn + (qi >> 5)));
       };
       const int it0 = (gi & 1) == w ? 0 : 1;
       uint2 mw_next;
@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
                             void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh,
                             const long long dk_sn, void* __restrict__ dv_out, const long long dv_sb,
                             const long long dv_sh, const long long dv_sn, const int accumulate_fp32,
-                            const int n_tiles) {
+                            const int n_tiles, const MaskBits mk) {
   using namespace bkvw;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -952,8 +952,8 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
         const int h = wt.kvh * group + i / wt.per_head;
         const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
         const int qi = (wt.i_start + i % wt.per_head) * BQ;
-        return __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb + (long long)h * shp.mt_sh +
-                                                    (long long)kr * shp.mt_sn + (qi >> 5)));
+        return __ldg(reinterpret_cast<const uint4*>(mk.bits_t + (long long)wt.b * mk.tsb + (long long)h * mk.tsh +
+                                                    (long long)kr * mk.tsn + (qi >> 5)));
       };
       uint4 mw_next;
       if constexpr (BITS) {
@@ -1126,7 +1126,7 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bkvw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv, a.dv_sb,
-      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles);
+      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -1151,7 +1151,7 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bkv::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv, a.dv_sb,
-      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles);
+      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -1160,10 +1160,10 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
 template <int D, int DT>
 int launch_bwd_dkdv_l(const BwdArgs& a) {
   if constexpr (D == 128) {
-    if (a.shape.mask) return launch_bwd_dkdv_t<D, DT, false, true>(a);  // dense layout only
+    if (a.mask.bits) return launch_bwd_dkdv_t<D, DT, false, true>(a);  // dense layout only
     return a.shape.cu_q ? launch_bwd_dkdv_t<D, DT, true>(a) : launch_bwd_dkdv_t<D, DT, false>(a);
   } else {
-    if (a.shape.mask) return launch_bwd_dkdv_wide_t<D, DT, false, true>(a);
+    if (a.mask.bits) return launch_bwd_dkdv_wide_t<D, DT, false, true>(a);
     return a.shape.cu_q ? launch_bwd_dkdv_wide_t<D, DT, true>(a) : launch_bwd_dkdv_wide_t<D, DT, false>(a);
   }
 }

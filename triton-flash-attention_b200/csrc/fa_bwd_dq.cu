@@ -95,7 +95,8 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                           const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                           void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh,
-                          const long long dq_sn, const int accumulate_fp32, const int n_tiles) {
+                          const long long dq_sn, const int accumulate_fp32, const int n_tiles,
+                          const MaskBits mk) {
   using namespace bdqw;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       const uint32_t* mrow = nullptr;
       if constexpr (BITS) {
         const int rr = r < cur.sq.nq ? r : cur.sq.nq - 1;
-        mrow = shp.mask + (long long)cur.b * shp.mask_sb + (long long)cur.h * shp.mask_sh + (long long)rr * shp.mask_sn;
+        mrow = mk.bits + (long long)cur.b * mk.sb + (long long)cur.h * mk.sh + (long long)rr * mk.sn;
       }
       const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
       const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
@@ -456,14 +457,14 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bdqw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
-      a.accumulate_fp32, n_tiles);
+      a.accumulate_fp32, n_tiles, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 // Sliding-window, boolean and plain masks are separate instantiations.
 template <int D, int DT>
 int launch_bwd_dq_l(const BwdArgs& a) {
-  if (a.shape.mask) return launch_bwd_dq_wide_t<D, DT, false, true>(a);  // dense, no window
+  if (a.mask.bits) return launch_bwd_dq_wide_t<D, DT, false, true>(a);  // dense, no window
   return a.shape.window > 0 ? launch_bwd_dq_wide_t<D, DT, true>(a) : launch_bwd_dq_wide_t<D, DT, false>(a);
 }
 

@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
                         const float* __restrict__ lse, const float* __restrict__ delta, void* __restrict__ dk_out,
                         const long long dk_sb, const long long dk_sh, const long long dk_sn,
                         void* __restrict__ dv_out, const long long dv_sb, const long long dv_sh,
-                        const long long dv_sn, const int accumulate_fp32, const int n_tiles) {
+                        const long long dv_sn, const int accumulate_fp32, const int n_tiles,
+                        const MaskBits mk) {
   using namespace bfz;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -476,8 +477,8 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         const int h = wt.kvh * group + i / wt.per_head;
         const int kr = wt.kv0 + rl < wt.sq.nk ? wt.kv0 + rl : wt.sq.nk - 1;
         const int qi = (wt.i_start + i % wt.per_head) * BQ;
-        return __ldg(reinterpret_cast<const uint4*>(shp.mask_t + (long long)wt.b * shp.mt_sb + (long long)h * shp.mt_sh +
-                                                    (long long)kr * shp.mt_sn + (qi >> 5)));
+        return __ldg(reinterpret_cast<const uint4*>(mk.bits_t + (long long)wt.b * mk.tsb + (long long)h * mk.tsh +
+                                                    (long long)kr * mk.tsn + (qi >> 5)));
       };
       uint4 mw_next;
       if constexpr (BITS) {
@@ -729,7 +730,7 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bfz::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, tmap_dq, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn,
-      a.dv, a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles);
+      a.dv, a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -737,7 +738,7 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
 // dense kernels carry no per-batch offset arithmetic.
 template <int D, int DT>
 int launch_bwd_fused_l(const BwdArgs& a, const CUtensorMap& tmap_dq) {
-  if (a.shape.mask) return launch_bwd_fused_t<D, DT, false, true>(a, tmap_dq);  // dense layout only
+  if (a.mask.bits) return launch_bwd_fused_t<D, DT, false, true>(a, tmap_dq);  // dense layout only
   return a.shape.cu_q ? launch_bwd_fused_t<D, DT, true>(a, tmap_dq) : launch_bwd_fused_t<D, DT, false>(a, tmap_dq);
 }
 

@@ -114,10 +114,6 @@ AttnShape make_shape(int B, int Hq, int Hkv, int Nq, int Nk, float scale, int ca
   s.window = 0;
   s.qk_cols = 1 << 20;  // no narrower tensor: every column is stored
   s.v_cols = 1 << 20;
-  s.mask = nullptr;
-  s.mask_sb = s.mask_sh = s.mask_sn = 0;
-  s.mask_t = nullptr;
-  s.mt_sb = s.mt_sh = s.mt_sn = 0;
   return s;
 }
 
@@ -522,7 +518,7 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
 //
 // Dense boolean masks (fa_mask_pack, fa_fwd_masked, fa_bwd_masked; the
 // reference has none, README.md:93): the kernels take the packed bit rows
-// through AttnShape::mask / mask_t, in instantiations of their own.  A mask
+// through a MaskBits kernel parameter, in instantiations of their own.  A mask
 // goes with the dense layout, no GQA packing of the forward, no window and
 // no position offsets.
 
@@ -558,10 +554,10 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
   a.shape.qk_cols = D;
   a.shape.v_cols = Dv;
   if (mask) {
-    a.shape.mask = mask;
-    a.shape.mask_sb = mask_strides[0];
-    a.shape.mask_sh = mask_strides[1];
-    a.shape.mask_sn = mask_strides[2];
+    a.mask.bits = mask;
+    a.mask.sb = mask_strides[0];
+    a.mask.sh = mask_strides[1];
+    a.mask.sn = mask_strides[2];
   }
   a.dtype = dtype;
   a.o = o;
@@ -610,14 +606,14 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
   a.shape.qk_cols = D;
   a.shape.v_cols = Dv;
   if (mask) {
-    a.shape.mask = mask;
-    a.shape.mask_sb = mask_strides[0];
-    a.shape.mask_sh = mask_strides[1];
-    a.shape.mask_sn = mask_strides[2];
-    a.shape.mask_t = mask_t;
-    a.shape.mt_sb = mask_t_strides[0];
-    a.shape.mt_sh = mask_t_strides[1];
-    a.shape.mt_sn = mask_t_strides[2];
+    a.mask.bits = mask;
+    a.mask.sb = mask_strides[0];
+    a.mask.sh = mask_strides[1];
+    a.mask.sn = mask_strides[2];
+    a.mask.bits_t = mask_t;
+    a.mask.tsb = mask_t_strides[0];
+    a.mask.tsh = mask_t_strides[1];
+    a.mask.tsn = mask_t_strides[2];
   }
   a.lse = lse;
   a.delta = delta;

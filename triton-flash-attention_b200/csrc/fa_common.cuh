@@ -78,17 +78,22 @@ struct AttnShape {
   // with zeros (they add nothing to Q K^T, P V or the gradients), and its
   // output columns at or past the width are not stored.  Multiples of 32.
   int qk_cols, v_cols;
-  // Dense boolean mask (dense layout only): when mask is not null, key k is
-  // visible to query row r of head h in batch b only if bit (k & 31) of word
-  // mask[b * mask_sb + h * mask_sh + r * mask_sn + (k >> 5)] is set; a row
-  // holds roundup(Nk, 128) / 32 words, so a 128-key tile is one aligned
-  // 16-byte load.  mask_t is the same mask transposed (a row per key, a bit
-  // per query, roundup(Nq, 128) / 32 words a row) for the kernels whose
-  // threads own key rows.  Strides in words; a stride of 0 broadcasts.
-  const uint32_t* mask;
-  long long mask_sb, mask_sh, mask_sn;
-  const uint32_t* mask_t;
-  long long mt_sb, mt_sh, mt_sn;
+};
+
+// Dense boolean mask (dense layout only), a kernel parameter of its own so
+// that the unmasked kernels keep their parameter block: key k is visible to
+// query row r of head h in batch b only if bit (k & 31) of word
+// bits[b * sb + h * sh + r * sn + (k >> 5)] is set; a row holds
+// roundup(Nk, 128) / 32 words, so a 128-key tile is one aligned 16-byte
+// load.  bits_t is the same mask transposed (a row per key, a bit per query,
+// roundup(Nq, 128) / 32 words a row) for the kernels whose threads own key
+// rows.  Strides in words; a stride of 0 broadcasts.  bits == nullptr: no
+// mask.
+struct MaskBits {
+  const uint32_t* bits = nullptr;
+  long long sb = 0, sh = 0, sn = 0;
+  const uint32_t* bits_t = nullptr;
+  long long tsb = 0, tsh = 0, tsn = 0;
 };
 
 // Hides the columns of s whose bit in words is clear (bit c & 31 of word

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
                   const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr,
-                  const int n_units) {
+                  const int n_units, const MaskBits mk) {
   using namespace fwd;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       const uint32_t* mrow = nullptr;
       if constexpr (BITS) {
         const int rr = r < w.sq.nq ? r : w.sq.nq - 1;
-        mrow = shp.mask + (long long)w.b * shp.mask_sb + (long long)hq * shp.mask_sh + (long long)rr * shp.mask_sn;
+        mrow = mk.bits + (long long)w.b * mk.sb + (long long)hq * mk.sh + (long long)rr * mk.sn;
       }
       if constexpr (C::SEP_P && TURNS) {
         // empty turns for the leading key tiles the other query tile has and this one lacks
@@ -690,7 +690,7 @@ int launch_fwd_t(const FwdArgs& a) {
   const int sms = device_sm_count();
   const int n_cta = n_units < sms ? n_units : sms;
   kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, static_cast<uint16_t*>(a.o),
-                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units);
+                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -698,7 +698,7 @@ int launch_fwd_t(const FwdArgs& a) {
 // masks, are separate instantiations.
 template <int D, int DT>
 int launch_fwd_l(const FwdArgs& a) {
-  if (a.shape.mask) return launch_fwd_t<D, DT, false, false, true>(a);  // dense, unpacked, no window
+  if (a.mask.bits) return launch_fwd_t<D, DT, false, false, true>(a);  // dense, unpacked, no window
   if (a.shape.window > 0)
     return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, true>(a) : launch_fwd_t<D, DT, false, true>(a);
   return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, false>(a) : launch_fwd_t<D, DT, false, false>(a);

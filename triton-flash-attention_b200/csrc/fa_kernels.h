@@ -21,6 +21,7 @@ struct FwdArgs {
   void* o;
   long long o_sb, o_sh, o_sn;
   float* lse;
+  MaskBits mask;  // dense boolean mask (bits == nullptr: none)
   cudaStream_t stream;
 };
 
@@ -37,6 +38,7 @@ struct BwdArgs {
   long long dk_sb, dk_sh, dk_sn;
   long long dv_sb, dv_sh, dv_sn;
   int accumulate_fp32;
+  MaskBits mask;  // dense boolean mask (bits == nullptr: none)
   cudaStream_t stream;
 };
 

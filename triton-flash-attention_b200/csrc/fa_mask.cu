@@ -1,5 +1,5 @@
 // fa_mask.cu -- packs a dense boolean attention mask into the bit rows the
-// attention kernels read (AttnShape::mask and mask_t).
+// attention kernels read (MaskBits::bits and bits_t).
 //
 // The input is a byte per (query, key) position (a torch.bool tensor; any
 // nonzero byte = visible) with arbitrary element strides, so broadcast
