@@ -43,7 +43,8 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 * ``--workload decode``: one query per sequence over a paged K/V cache
   (``scaled_dot_product_attention_paged``), HBM roofline.  Informational.
 * ``--workload masked``: boolean ``attn_mask`` forms (key padding, all
-  true, random) at the C2 shape beside the unmasked call.  Informational.
+  true, random) and ``dropout_p`` at the C2 shape beside the unmasked call.
+  Informational.
 """
 
 from __future__ import annotations
@@ -745,13 +746,14 @@ def run_varlen(args) -> None:
 
 
 def run_masked(args) -> None:
-    """Dense boolean masks (no counterpart in the reference): the C2 shape
-    (B4 H16 N4096 D64, fp16), forward and forward+backward through
-    ``scaled_dot_product_attention`` with no mask, a key-padding mask
-    (B, 1, 1, N) hiding each batch's last 512 * (b + 1) keys, a mask with
-    every bit set, and a seeded random (B, 1, N, N) mask of density 0.7, each
-    bidirectional and causal; plus the pack kernel alone on the random mask.
-    The masked times include packing the mask (once per forward).
+    """Dense boolean masks and attention dropout (no counterpart in the
+    reference): the C2 shape (B4 H16 N4096 D64, fp16), forward and
+    forward+backward through ``scaled_dot_product_attention`` with no mask,
+    a key-padding mask (B, 1, 1, N) hiding each batch's last 512 * (b + 1)
+    keys, a mask with every bit set, a seeded random (B, 1, N, N) mask of
+    density 0.7, and dropout at p = 0.1, each bidirectional and causal; plus
+    the pack kernel alone on the random mask.  The masked times include
+    packing the mask (once per forward); dropout runs the split backward.
     Informational, one JSON line."""
     import torch
 
@@ -769,6 +771,7 @@ def run_masked(args) -> None:
         "key_padding": padding,
         "all_true": torch.ones(N, N, dtype=torch.bool, device=dev),
         "random_0.7": torch.rand(B, 1, N, N, generator=g, device=dev) < 0.7,
+        "dropout_0.1": None,
     }
     steps = max(1, min(args.steps, 20))
 
@@ -788,12 +791,14 @@ def run_masked(args) -> None:
     rows = {}
     for causal in (False, True):
         for name, m in masks.items():
+            p = 0.1 if name.startswith("dropout") else 0.0
+
             def fwd():
                 with torch.no_grad():
-                    fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m)
+                    fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m, dropout_p=p)
 
             def fwd_bwd():
-                o = fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m)
+                o = fa.scaled_dot_product_attention(q, k, v, is_causal=causal, attn_mask=m, dropout_p=p)
                 torch.autograd.grad(o, (q, k, v), do)
 
             rows[f"{'causal' if causal else 'bidirectional'}/{name}"] = {
@@ -881,7 +886,7 @@ def main() -> None:
                          "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel; "
                          "varlen: a packed batch of ragged sequences beside its padded dense equivalent; "
                          "decode: one query per sequence over a paged K/V cache; "
-                         "masked: boolean attn_mask forms at the C2 shape")
+                         "masked: boolean attn_mask forms and dropout at the C2 shape")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     args = ap.parse_args()
     if args.warmup < 3:

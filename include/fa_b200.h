@@ -379,6 +379,50 @@ FA_API int fa_bwd_masked_bf16(const void* q, const void* k, const void* v, const
                               const uint32_t* mask_bits_t, const int64_t* mask_t_strides,
                               float softmax_scale, int causal, int deterministic, void* stream);
 
+/* Attention dropout (PyTorch SDPA's dropout_p; the reference has none,
+ * README.md:93).  fa_fwd_dropout is fa_fwd_vdim with the softmax
+ * probabilities dropped at rate dropout_p and the kept ones scaled by
+ * 1 / (1 - p); fa_bwd_dropout is its whole backward (Delta into the caller's
+ * (B, Hq, Nq) fp32 buffer, then the separate dQ and dK/dV kernels; bitwise
+ * reproducible).  dropout_p must lie in (0, 1) and is applied as
+ * p = t / 256 with t = round(256 * dropout_p) clamped to [1, 255], the
+ * scale as 256 / (256 - t).  Whether (query q, key k) of head h, batch b is
+ * kept is a stateless function of (seed, b * Hq + h, q, k): one 32-bit word
+ * per 2 x 2 block of positions, word = mix32(key2 ^ ((q >> 1) << 16 |
+ * (k >> 1))) with the low 16 bits of each half, key2 = mix32(key_bh ^
+ * ((q >> 17) << 16 | (k >> 17))), key_bh = mix32(seed_lo ^ mix32(seed_hi +
+ * (b * Hq + h) * 0x9E3779B9)), mix32 the "lowbias32" hash (xorshift 16,
+ * * 0x7feb352d, xorshift 15, * 0x846ca68b, xorshift 16); the position's
+ * byte is byte 2 * (q & 1) + (k & 1) of the word and the value is kept iff
+ * byte >= t.  The forward and the backward of one step take the same seed.
+ * Dense layout, no mask, no window, no position offsets. */
+FA_API int fa_fwd_dropout(const void* q, const void* k, const void* v, void* o, float* lse,
+                          int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                          const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, const int64_t* o_strides,
+                          float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_dropout(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                          const float* lse, void* dq, void* dk, void* dv, float* delta,
+                          int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                          const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, const int64_t* o_strides,
+                          const int64_t* do_strides, const int64_t* dq_strides,
+                          const int64_t* dk_strides, const int64_t* dv_strides,
+                          float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream);
+FA_API int fa_fwd_dropout_bf16(const void* q, const void* k, const void* v, void* o, float* lse,
+                               int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                               const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, const int64_t* o_strides,
+                               float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream);
+FA_API int fa_bwd_dropout_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                               const float* lse, void* dq, void* dk, void* dv, float* delta,
+                               int B, int Hq, int Hkv, int Nq, int Nk, int D, int Dv,
+                               const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, const int64_t* o_strides,
+                               const int64_t* do_strides, const int64_t* dq_strides,
+                               const int64_t* dk_strides, const int64_t* dv_strides,
+                               float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream);
+
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded wait gives up: 0 = healthy, else FA_ERR_DEVICE_TIMEOUT in the
  * low byte and the barrier site in bits 8..15.  Synchronises the device. */
@@ -390,7 +434,7 @@ FA_API const char* fa_status_string(int code);
 /* Library version: major * 10000 + minor * 100 + patch (1.1.0 adds bf16,
  * 1.2.0 the fused backward, 1.3.0 packed variable-length batches and the
  * paged K/V forward, 1.4.0 value head sizes different from D, 1.5.0 dense
- * boolean masks). */
+ * boolean masks, 1.6.0 attention dropout). */
 FA_API int fa_version(void);
 
 #ifdef __cplusplus

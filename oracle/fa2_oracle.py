@@ -72,12 +72,16 @@ def causal_mask(nq: int, nk: int, q_offset: int = 0, k_offset: int = 0, window: 
 
 
 def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None,
-                   q_offset: int = 0, k_offset: int = 0, window: int = 0, mask=None):
+                   q_offset: int = 0, k_offset: int = 0, window: int = 0, mask=None,
+                   dropout_keep=None, dropout_scale: float = 1.0):
     """Dense attention in float64 (the math behind attention.py:774-786).
 
     ``mask`` (optional) is a bool array broadcastable to (B, Hq, Nq, Nk):
     False hides the key, as ``attn_mask`` of PyTorch's SDPA (combined with
-    ``causal`` by AND).
+    ``causal`` by AND).  ``dropout_keep`` (optional, (B, Hq, Nq, Nk) bool)
+    applies attention dropout: O = (P Z r) V with Z the keep pattern and r
+    ``dropout_scale``; then dV = (P Z r)^T dO, dS = P (Z r dP - Delta) with
+    Delta = rowsum(O dO), and lse is that of the undropped P.
 
     Returns a dict with ``o``, ``lse`` (natural log), ``lse2`` (base-2 log of
     the row sum of exp2(scale*log2(e)*s), the unit the reference saves,
@@ -106,18 +110,63 @@ def sdpa_reference(q, k, v, *, causal: bool, scale: float | None = None, do=None
     with np.errstate(divide="ignore", invalid="ignore"):
         p = np.where(l > 0, e / np.where(l > 0, l, 1.0), 0.0)
         lse = np.where(l[..., 0] > 0, mx_safe[..., 0] + np.log(np.where(l[..., 0] > 0, l[..., 0], 1.0)), -np.inf)
-    o = np.einsum("bhqk,bhkd->bhqd", p, ve)
+    zr = 1.0 if dropout_keep is None else np.asarray(dropout_keep, dtype=np.float64) * dropout_scale
+    pd = p * zr
+    o = np.einsum("bhqk,bhkd->bhqd", pd, ve)
     out = {"o": o, "lse": lse, "lse2": lse * INV_LN2}
     if do is not None:
         do = np.asarray(do, dtype=np.float64)
         delta = (o * do).sum(axis=-1)
         dp = np.einsum("bhqd,bhkd->bhqk", do, ve)
-        ds = p * (dp - delta[..., None])
+        ds = p * (dp * zr - delta[..., None])
         dq = np.einsum("bhqk,bhkd->bhqd", ds, ke) * scale
         dke = np.einsum("bhqk,bhqd->bhkd", ds, q) * scale
-        dve = np.einsum("bhqk,bhqd->bhkd", p, do)
+        dve = np.einsum("bhqk,bhqd->bhkd", pd, do)
         out.update(delta=delta, dq=dq, dk=_reduce_kv(dke, hkv), dv=_reduce_kv(dve, hkv))
     return out
+
+
+def _mix32(x):
+    """The "lowbias32" integer hash (C. Wellons, hash-prospector): xorshift
+    16, multiply by 0x7feb352d, xorshift 15, multiply by 0x846ca68b,
+    xorshift 16, all modulo 2**32."""
+    x = np.asarray(x, dtype=np.uint32)
+    x = x ^ (x >> np.uint32(16))
+    x = x * np.uint32(0x7FEB352D)
+    x = x ^ (x >> np.uint32(15))
+    x = x * np.uint32(0x846CA68B)
+    x = x ^ (x >> np.uint32(16))
+    return x
+
+
+def dropout_threshold(dropout_p: float):
+    """(t, r): the library applies p as t / 256, t = round(256 p) (half to
+    even, on the float32 value of p) clamped to [1, 255], and scales kept
+    values by r = 256 / (256 - t)."""
+    t = int(round(float(np.float32(dropout_p)) * 256.0))
+    t = min(max(t, 1), 255)
+    return t, 256.0 / (256 - t)
+
+
+def dropout_keep_reference(seed: int, batch: int, heads: int, nq: int, nk: int, dropout_p: float):
+    """The library's dropout pattern (fa_fwd_dropout / fa_bwd_dropout): a
+    bool (batch, heads, nq, nk) array, True where the probability is kept.
+    One 32-bit word per 2 x 2 block of (query, key) positions; the
+    position's byte is byte 2 (q & 1) + (k & 1) of it, kept iff byte >= t.
+    No counterpart in the reference (it has no dropout, README.md:93)."""
+    t, _ = dropout_threshold(dropout_p)
+    seed = int(seed) & 0xFFFFFFFFFFFFFFFF
+    lo, hi = np.uint32(seed & 0xFFFFFFFF), np.uint32(seed >> 32)
+    bh = np.arange(batch * heads, dtype=np.uint32).reshape(batch, heads)
+    key_bh = _mix32(lo ^ _mix32(hi + bh * np.uint32(0x9E3779B9)))
+    q = np.arange(nq, dtype=np.uint32)[:, None]
+    k = np.arange(nk, dtype=np.uint32)[None, :]
+    key2 = _mix32(key_bh[..., None, None] ^ (((q >> np.uint32(17)) << np.uint32(16)) | (k >> np.uint32(17))))
+    ctr = (((q >> np.uint32(1)) & np.uint32(0xFFFF)) << np.uint32(16)) | ((k >> np.uint32(1)) & np.uint32(0xFFFF))
+    word = _mix32(key2 ^ ctr)
+    shift = np.uint32(8) * (np.uint32(2) * (q & np.uint32(1)) + (k & np.uint32(1)))
+    byte = (word >> shift) & np.uint32(0xFF)
+    return byte >= np.uint32(t)
 
 
 def mask_bits_reference(mask):

@@ -23,6 +23,11 @@ from .attention import (
     fused_backward_enabled,
     scaled_dot_product_attention,
 )
+from .dropout import (
+    B200DropoutAttention,
+    attention_backward_dropout,
+    attention_forward_dropout,
+)
 from .flops import attention_flops, delta_bytes, memory_model
 from .masks import (
     B200MaskedAttention,
@@ -41,6 +46,7 @@ from .varlen import (
 
 __all__ = [
     "B200Attention",
+    "B200DropoutAttention",
     "B200MaskedAttention",
     "B200VarlenAttention",
     "DispatchDecision",
@@ -49,12 +55,14 @@ __all__ = [
     "TritonAttention",
     "attention_backward_dkdv",
     "attention_backward_dq",
+    "attention_backward_dropout",
     "attention_backward_fused",
     "attention_backward_masked",
     "attention_backward_vdim",
     "attention_delta",
     "attention_flops",
     "attention_forward",
+    "attention_forward_dropout",
     "attention_forward_masked",
     "attention_forward_vdim",
     "delta_bytes",

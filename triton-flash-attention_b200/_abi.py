@@ -62,8 +62,14 @@ SIGNATURES.update({
     "fa_fwd_masked": (_i, [_p] * 5 + [_i] * 7 + [_s] * 4 + [_p, _s, _f, _i, _p]),
     "fa_bwd_masked": (_i, [_p] * 11 + [_i] * 7 + [_s] * 8 + [_p, _s, _p, _s, _f, _i, _i, _p]),
 })
+_u64 = ctypes.c_uint64
+SIGNATURES.update({
+    "fa_fwd_dropout": (_i, [_p] * 5 + [_i] * 7 + [_s] * 4 + [_f, _u64, _f, _i, _p]),
+    "fa_bwd_dropout": (_i, [_p] * 10 + [_i] * 7 + [_s] * 8 + [_f, _u64, _f, _i, _p]),
+})
 SIGNATURES.update({name + "_bf16": SIGNATURES[name]
-                   for name in ("fa_fwd_vdim", "fa_bwd_vdim", "fa_fwd_masked", "fa_bwd_masked")})
+                   for name in ("fa_fwd_vdim", "fa_bwd_vdim", "fa_fwd_masked", "fa_bwd_masked",
+                                "fa_fwd_dropout", "fa_bwd_dropout")})
 SIGNATURES.update({
     "fa_bwd_fused_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
                                   _s, _s, _s, _s, _s, _s, _s, _s, _f, _i, _p]),

@@ -310,7 +310,7 @@ TritonAttention = B200Attention
 
 def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, scale: float | None = None,
                                  enable_gqa: bool = False, backend: Backend = "auto",
-                                 attn_mask: torch.Tensor | None = None) -> torch.Tensor:
+                                 attn_mask: torch.Tensor | None = None, dropout_p: float = 0.0) -> torch.Tensor:
     """Scaled dot-product attention on the B200 kernels (attention.py:789-845).
 
     Forward and backward, causal and bidirectional attention, arbitrary
@@ -323,7 +323,13 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
     a bool tensor broadcastable to (batch, query heads, query length, key
     length), ``True`` where the key takes part, as in PyTorch's SDPA; with
     ``is_causal`` a key must pass both.  A query row that sees no key gets
-    zeros (PyTorch returns NaN)."""
+    zeros (PyTorch returns NaN).
+
+    ``dropout_p`` (an addition; the reference has no dropout) drops the
+    softmax probabilities at that rate, as PyTorch's SDPA does, applied in
+    steps of 1/256; the pattern is drawn from a seed taken from PyTorch's
+    default generator (``torch.manual_seed`` repeats it).  It cannot be
+    combined with ``attn_mask``."""
     if backend == "torch":
         raise RuntimeError(
             "backend='torch' (the PyTorch SDPA fallback) is not part of this package; "
@@ -336,6 +342,8 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
         raise TypeError("enable_gqa must be a bool")
     if scale is not None and (not isinstance(scale, Real) or not math.isfinite(float(scale))):
         raise ValueError("scale must be a finite real number or None")
+    if isinstance(dropout_p, bool) or not isinstance(dropout_p, Real) or not 0.0 <= float(dropout_p) < 1.0:
+        raise ValueError("dropout_p must be a real number in [0, 1)")
     _validate_inputs(query, key, value, enable_gqa=enable_gqa)
     decision = explain_dispatch(query, key, value, enable_gqa=enable_gqa)
     if decision.backend != "cuda":
@@ -343,6 +351,8 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
     if attn_mask is not None:
         from .masks import validate_attention_mask
         validate_attention_mask(attn_mask, query, key)
+        if dropout_p > 0.0:
+            raise RuntimeError("B200 CUDA backend is unavailable: attn_mask and dropout_p together are not supported")
     query_c = query.contiguous()
     key_c = key.contiguous()
     value_c = value.contiguous()
@@ -350,4 +360,8 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
     if attn_mask is not None:
         from .masks import B200MaskedAttention
         return B200MaskedAttention.apply(query_c, key_c, value_c, attn_mask, is_causal, softmax_scale)
+    if dropout_p > 0.0:
+        from .dropout import B200DropoutAttention, new_dropout_seed
+        return B200DropoutAttention.apply(query_c, key_c, value_c, is_causal, softmax_scale, float(dropout_p),
+                                          new_dropout_seed())
     return B200Attention.apply(query_c, key_c, value_c, is_causal, softmax_scale)

@@ -133,14 +133,15 @@ struct ItemCursor {
 
 }  // namespace bkv
 
-template <int D, int DT, bool VL, bool BITS>
+template <int D, int DT, bool VL, bool BITS, bool DROP>
 __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                        const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                        void* __restrict__ dk_out, const long long dk_sb, const long long dk_sh, const long long dk_sn,
                        void* __restrict__ dv_out, const long long dv_sb, const long long dv_sh, const long long dv_sn,
-                       const int accumulate_fp32, const int n_tiles, const MaskBits mk) {
+                       const int accumulate_fp32, const int n_tiles, const MaskBits mk,
+                       const DropArgs dr) {
   using namespace bkv;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -440,6 +441,11 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
         tmem_ld64(tS, st);
         tmem_ld64(tS + 64, dpt);
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
+        // dropout: P~ = Z P feeds dV, dS = P (Z r dP - Delta); this key row
+        // uses bytes (k & 1) and 2 + (k & 1) of each 2 x 2 block word
+        uint32_t drop_k2 = 0;
+        if constexpr (DROP)
+          drop_k2 = drop_key2(drop_key_bh(dr, wt.b * shp.Hq + wt.kvh * group + it / wt.per_head), q0, wt.kv0 + rl);
         int cmin = key_out ? BQ : 0;
         if (shp.causal && !key_out) {
           const long long x = cmin_base - q0;
@@ -472,12 +478,26 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
           const int c = c4 * 4;
           const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
           const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
-          const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-          const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-          pk_p[c4 * 2] = p01;
-          pk_p[c4 * 2 + 1] = p23;
-          pk_ds[c4 * 2] = mul2<DT>(p01, d01);
-          pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+          if constexpr (DROP) {
+            const int kb = (wt.kv0 + rl) & 1;
+            const uint32_t m01 = keep_mask2(drop_word(drop_k2, q0 + c, wt.kv0 + rl), kb, 2 + kb, dr.t);
+            const uint32_t m23 = keep_mask2(drop_word(drop_k2, q0 + c + 2, wt.kv0 + rl), kb, 2 + kb, dr.t);
+            const uint64_t r2 = f2pack(dr.r, dr.r);
+            const uint32_t n01 = pack2_f2<DT>(f2pack(nd.x, nd.y)), n23 = pack2_f2<DT>(f2pack(nd.z, nd.w));
+            const uint32_t k01 = pack2_f2<DT>(ffma2(f2pack(dpt[c], dpt[c + 1]), r2, f2pack(nd.x, nd.y)));
+            const uint32_t k23 = pack2_f2<DT>(ffma2(f2pack(dpt[c + 2], dpt[c + 3]), r2, f2pack(nd.z, nd.w)));
+            pk_p[c4 * 2] = p01 & m01;
+            pk_p[c4 * 2 + 1] = p23 & m23;
+            pk_ds[c4 * 2] = mul2<DT>(p01, (k01 & m01) | (n01 & ~m01));
+            pk_ds[c4 * 2 + 1] = mul2<DT>(p23, (k23 & m23) | (n23 & ~m23));
+          } else {
+            const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
+            const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+            pk_p[c4 * 2] = p01;
+            pk_p[c4 * 2 + 1] = p23;
+            pk_ds[c4 * 2] = mul2<DT>(p01, d01);
+            pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+          }
         }
         tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
         tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
@@ -495,7 +515,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       }
       const int kr = wt.kv0 + rl;
       const bool row_ok = kr < wt.sq.nk;
-      const float sc = w == 0 ? 1.f : shp.scale;
+      const float sc = w == 0 ? (DROP ? dr.r : 1.f) : shp.scale;  // dV of dropped-out P~ carries r
       const uint32_t tAcc = tmem_addr(tmem, uint32_t(wq * 32), uint32_t(w == 0 ? C::DV_COL : C::DK_COL));
       void* out = w == 0 ? dv_out : dk_out;
       const long long krow = (long long)wt.sq.k0 + kr;
@@ -1130,10 +1150,10 @@ int launch_bwd_dkdv_wide_t(const BwdArgs& a) {
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, int DT, bool VL, bool BITS = false>
+template <int D, int DT, bool VL, bool BITS = false, bool DROP = false>
 int launch_bwd_dkdv_t(const BwdArgs& a) {
   using C = bkv::Cfg<D>;
-  auto kern = fa_bwd_dkdv_kernel<D, DT, VL, BITS>;
+  auto kern = fa_bwd_dkdv_kernel<D, DT, VL, BITS, DROP>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -1151,7 +1171,7 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bkv::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn, a.dv, a.dv_sb,
-      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask);
+      a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask, a.drop);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -1159,6 +1179,9 @@ int launch_bwd_dkdv_t(const BwdArgs& a) {
 // dense kernels carry no per-batch offset arithmetic.
 template <int D, int DT>
 int launch_bwd_dkdv_l(const BwdArgs& a) {
+  // dropout: every head size runs the kernel whose warpgroups build P^T and
+  // dS^T of an item together in registers (dense layout, no mask)
+  if (a.drop.t) return launch_bwd_dkdv_t<D, DT, false, false, true>(a);
   if constexpr (D == 128) {
     if (a.mask.bits) return launch_bwd_dkdv_t<D, DT, false, true>(a);  // dense layout only
     return a.shape.cu_q ? launch_bwd_dkdv_t<D, DT, true>(a) : launch_bwd_dkdv_t<D, DT, false>(a);

@@ -89,14 +89,14 @@ __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
 }
 }  // namespace bdqw
 
-template <int D, int DT, bool WIN, bool BITS>
+template <int D, int DT, bool WIN, bool BITS, bool DROP>
 __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
     fa_bwd_dq_wide_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                           const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                           const AttnShape shp, const float* __restrict__ lse, const float* __restrict__ delta,
                           void* __restrict__ dq_out, const long long dq_sb, const long long dq_sh,
                           const long long dq_sn, const int accumulate_fp32, const int n_tiles,
-                          const MaskBits mk) {
+                          const MaskBits mk, const DropArgs dr) {
   using namespace bdqw;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -325,6 +325,15 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
       }
       const uint64_t nlse2 = f2pack(-lse_r, -lse_r);
       const uint64_t ndelta2 = f2pack(-delta_r, -delta_r);
+      // dropout: dS = P (Z r dP - Delta), Z = 1 where the position's byte is kept
+      uint32_t drop_kbh = 0, nd_pk = 0;
+      const int drop_b0 = 2 * (r & 1);
+      uint64_t r2 = 0;
+      if constexpr (DROP) {
+        drop_kbh = drop_key_bh(dr, cur.b * shp.Hq + cur.h);
+        nd_pk = pack2_f2<DT>(ndelta2);
+        r2 = f2pack(dr.r, dr.r);
+      }
       // mask words are loaded one key tile ahead
       uint2 mw_next;
       if constexpr (BITS) {
@@ -369,9 +378,19 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         float dp[64];
         tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
         uint32_t pk_ds[32];
+        if constexpr (DROP) {
+          const uint32_t k2 = drop_key2(drop_kbh, r, key0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          pk_ds[i] = mul2<DT>(pk_p[i], pack2_f2<DT>(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+          for (int i = 0; i < 32; ++i) {
+            const uint32_t m = keep_mask2(drop_word(k2, r, key0 + 2 * i), drop_b0, drop_b0 + 1, dr.t);
+            const uint32_t dk = pack2_f2<DT>(ffma2(f2pack(dp[2 * i], dp[2 * i + 1]), r2, ndelta2));
+            pk_ds[i] = mul2<DT>(pk_p[i], (dk & m) | (nd_pk & ~m));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            pk_ds[i] = mul2<DT>(pk_p[i], pack2_f2<DT>(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+        }
         tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
         tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
         tmem_st_wait();
@@ -445,10 +464,10 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool WIN, bool BITS = false>
+template <int D, int DT, bool WIN, bool BITS = false, bool DROP = false>
 int launch_bwd_dq_wide_t(const BwdArgs& a) {
   using C = bdqw::Cfg<D>;
-  auto kern = fa_bwd_dq_wide_kernel<D, DT, WIN, BITS>;
+  auto kern = fa_bwd_dq_wide_kernel<D, DT, WIN, BITS, DROP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess)
     return FA_ERR_LAUNCH;
   const int n_qt = (a.shape.Nq + bdqw::BM - 1) / bdqw::BM;
@@ -457,13 +476,14 @@ int launch_bwd_dq_wide_t(const BwdArgs& a) {
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bdqw::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
       a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, a.shape, a.lse, a.delta, a.dq, a.dq_sb, a.dq_sh, a.dq_sn,
-      a.accumulate_fp32, n_tiles, a.mask);
+      a.accumulate_fp32, n_tiles, a.mask, a.drop);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 // Sliding-window, boolean and plain masks are separate instantiations.
 template <int D, int DT>
 int launch_bwd_dq_l(const BwdArgs& a) {
+  if (a.drop.t) return launch_bwd_dq_wide_t<D, DT, false, false, true>(a);  // dense, no mask or window
   if (a.mask.bits) return launch_bwd_dq_wide_t<D, DT, false, true>(a);  // dense, no window
   return a.shape.window > 0 ? launch_bwd_dq_wide_t<D, DT, true>(a) : launch_bwd_dq_wide_t<D, DT, false>(a);
 }

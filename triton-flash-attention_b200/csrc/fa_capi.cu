@@ -535,7 +535,8 @@ bool mask_ok(const uint32_t* bits, const int64_t* st, int words) {
 int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
                   int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
                   const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal, void* stream,
-                  int dtype, const uint32_t* mask = nullptr, const int64_t* mask_strides = nullptr) {
+                  int dtype, const uint32_t* mask = nullptr, const int64_t* mask_strides = nullptr,
+                  const DropArgs* drop = nullptr) {
   if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   const int W = D > Dv ? D : Dv;
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
@@ -545,7 +546,7 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
   if (!out_strides_ok(o, o_strides, 2)) return FA_ERR_MISALIGNED;
   if (mask && !mask_ok(mask, mask_strides, (Nk + 127) / 128 * 4)) return FA_ERR_MISALIGNED;
   FwdArgs a;
-  const int pack = mask ? 0 : gqa_pack(Hq, Hkv, Nq);
+  const int pack = (mask || drop) ? 0 : gqa_pack(Hq, Hkv, Nq);
   if ((rc = make_q_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, dtype, pack, D))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, 128, dtype, 1, D))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, 128, dtype, 1, Dv))) return rc;
@@ -559,6 +560,7 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
     a.mask.sh = mask_strides[1];
     a.mask.sn = mask_strides[2];
   }
+  if (drop) a.drop = *drop;
   a.dtype = dtype;
   a.o = o;
   a.o_sb = o_strides[0];
@@ -576,7 +578,7 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
                   const int64_t* dk_strides, const int64_t* dv_strides, float softmax_scale, int causal,
                   int deterministic, void* stream, int dtype, const uint32_t* mask = nullptr,
                   const int64_t* mask_strides = nullptr, const uint32_t* mask_t = nullptr,
-                  const int64_t* mask_t_strides = nullptr) {
+                  const int64_t* mask_t_strides = nullptr, const DropArgs* drop = nullptr) {
   if (!supported_d(D) || !supported_d(Dv)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   const int W = D > Dv ? D : Dv;
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, W);
@@ -586,7 +588,9 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
       !dv_strides)
     return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
-  const bool fused = W <= 64 && !deterministic;
+  // dropout runs the separate dQ and dK/dV kernels, whose threads hold P and
+  // dS of an element together
+  const bool fused = W <= 64 && !deterministic && !drop;
   if (fused && !dq_accum) return FA_ERR_BAD_SHAPE;
   if (!out_strides_ok(o, o_strides, 2) || !out_strides_ok(dO, do_strides, 2) || !out_strides_ok(dq, dq_strides, 2) ||
       !out_strides_ok(dk, dk_strides, 2) || !out_strides_ok(dv, dv_strides, 2) || !aligned16(delta) ||
@@ -615,6 +619,7 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
     a.mask.tsh = mask_t_strides[1];
     a.mask.tsn = mask_t_strides[2];
   }
+  if (drop) a.drop = *drop;
   a.lse = lse;
   a.delta = delta;
   a.dk = dk;
@@ -652,7 +657,7 @@ int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, co
   a.dq_sh = dq_strides[1];
   a.dq_sn = dq_strides[2];
   if ((rc = launch_bwd_dq(a, W))) return rc;
-  const int bq = W <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
+  const int bq = (W <= 64 && !drop) ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ;
   if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, W, q_strides, bq, dtype, 1, D))) return rc;
   if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, W, do_strides, bq, dtype, 1, Dv))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, dkdv_cfg::BM, dtype, 1, D))) return rc;
@@ -968,4 +973,76 @@ extern "C" int fa_bwd_masked_bf16(const void* q, const void* k, const void* v, c
                           DT_BF16);
 }
 
-extern "C" int fa_version(void) { return 10500; }
+// Attention dropout.
+static int drop_args(float p, uint64_t seed, DropArgs* d) {
+  if (!(p > 0.f && p < 1.f)) return FA_ERR_BAD_SHAPE;
+  long t = std::lrint(double(p) * 256.0);
+  if (t < 1) t = 1;
+  if (t > 255) t = 255;
+  d->t = uint32_t(t);
+  d->r = float(256.0 / double(256 - t));
+  d->seed_lo = uint32_t(seed);
+  d->seed_hi = uint32_t(seed >> 32);
+  return FA_OK;
+}
+static int fwd_dropout_entry(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
+                             int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, const int64_t* o_strides, float dropout_p, uint64_t seed,
+                             float softmax_scale, int causal, void* stream, int dtype) {
+  DropArgs d;
+  int rc = drop_args(dropout_p, seed, &d);
+  if (rc) return rc;
+  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                       softmax_scale, causal, stream, dtype, nullptr, nullptr, &d);
+}
+extern "C" int fa_fwd_dropout(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                              int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                              const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                              float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream) {
+  return fwd_dropout_entry(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                           dropout_p, seed, softmax_scale, causal, stream, DT_F16);
+}
+extern "C" int fa_fwd_dropout_bf16(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                                   int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                   const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                   float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream) {
+  return fwd_dropout_entry(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+                           dropout_p, seed, softmax_scale, causal, stream, DT_BF16);
+}
+static int bwd_dropout_entry(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                             const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int Hq, int Hkv,
+                             int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                             const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                             float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream,
+                             int dtype) {
+  DropArgs d;
+  int rc = drop_args(dropout_p, seed, &d);
+  if (rc) return rc;
+  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, nullptr, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+                       k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
+                       causal, 1, stream, dtype, nullptr, nullptr, nullptr, nullptr, &d);
+}
+extern "C" int fa_bwd_dropout(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                              const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int Hq, int Hkv,
+                              int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                              const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                              float dropout_p, uint64_t seed, float softmax_scale, int causal, void* stream) {
+  return bwd_dropout_entry(q, k, v, o, dO, lse, dq, dk, dv, delta, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides,
+                           v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, dropout_p, seed,
+                           softmax_scale, causal, stream, DT_F16);
+}
+extern "C" int fa_bwd_dropout_bf16(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                   const float* lse, void* dq, void* dk, void* dv, float* delta, int B, int Hq,
+                                   int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
+                                   const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                   const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                                   const int64_t* dv_strides, float dropout_p, uint64_t seed, float softmax_scale,
+                                   int causal, void* stream) {
+  return bwd_dropout_entry(q, k, v, o, dO, lse, dq, dk, dv, delta, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides,
+                           v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, dropout_p, seed,
+                           softmax_scale, causal, stream, DT_BF16);
+}
+
+extern "C" int fa_version(void) { return 10600; }

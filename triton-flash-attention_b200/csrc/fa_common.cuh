@@ -96,6 +96,52 @@ struct MaskBits {
   long long tsb = 0, tsh = 0, tsn = 0;
 };
 
+// Attention dropout (a kernel parameter of its own): P is kept where the
+// position's random byte is at least t (so p = t / 256, t in [1, 255]) and
+// the kept values are scaled by r = 1 / (1 - t / 256).  The random bytes are
+// a stateless function of (seed, batch * Hq + head, query, key), so the
+// forward and the backward kernels regenerate the same ones in any order:
+//   key_bh  = mix32(seed_lo ^ mix32(seed_hi + bh * 0x9E3779B9))
+//   key2    = mix32(key_bh ^ ((q >> 17) << 16 | (k >> 17)))
+//   word    = mix32(key2 ^ (((q >> 1) & 0xFFFF) << 16 | ((k >> 1) & 0xFFFF)))
+//   byte    = word >> 8 * (2 * (q & 1) + (k & 1))
+// -- one 32-bit word for each 2 x 2 block of (query, key) positions, so a
+// thread that owns a query row and one that owns a key row each use two of
+// its four bytes.  mix32 is the "lowbias32" integer hash published by
+// C. Wellons (hash-prospector): xorshift 16, multiply 0x7feb352d, xorshift
+// 15, multiply 0x846ca68b, xorshift 16.  t == 0: no dropout.
+struct DropArgs {
+  uint32_t t = 0;
+  float r = 1.f;
+  uint32_t seed_lo = 0, seed_hi = 0;
+};
+
+__host__ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+__device__ __forceinline__ uint32_t drop_key_bh(const DropArgs& dr, int bh) {
+  return mix32(dr.seed_lo ^ mix32(dr.seed_hi + uint32_t(bh) * 0x9E3779B9u));
+}
+// key2 of the (query, key) positions whose indices agree above bit 16
+__device__ __forceinline__ uint32_t drop_key2(uint32_t key_bh, int q, int k) {
+  return mix32(key_bh ^ ((uint32_t(q) >> 17) << 16 | (uint32_t(k) >> 17)));
+}
+__device__ __forceinline__ uint32_t drop_word(uint32_t key2, int q, int k) {
+  return mix32(key2 ^ ((((uint32_t(q) >> 1) & 0xFFFFu) << 16) | ((uint32_t(k) >> 1) & 0xFFFFu)));
+}
+// Lane mask (0xFFFF per kept 16-bit lane) of an element pair: bytes b0 (low
+// lane) and b1 (high lane) of word.
+__device__ __forceinline__ uint32_t keep_mask2(uint32_t word, int b0, int b1, uint32_t t) {
+  const uint32_t lo = ((word >> (8 * b0)) & 0xFFu) >= t ? 0x0000FFFFu : 0u;
+  const uint32_t hi = ((word >> (8 * b1)) & 0xFFu) >= t ? 0xFFFF0000u : 0u;
+  return lo | hi;
+}
+
 // Hides the columns of s whose bit in words is clear (bit c & 31 of word
 // c >> 5; 1 = visible).
 template <int N>

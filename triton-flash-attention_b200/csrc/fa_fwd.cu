@@ -152,12 +152,12 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
 
 }  // namespace fwd
 
-template <int D, int DT, bool PACK, bool WIN, bool BITS>
+template <int D, int DT, bool PACK, bool WIN, bool BITS, bool DROP>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
                   const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr,
-                  const int n_units, const MaskBits mk) {
+                  const int n_units, const MaskBits mk, const DropArgs dr) {
   using namespace fwd;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -482,6 +482,10 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         }
         if (!ok) break;
       }
+      // dropout: this row's random-byte positions within a block word
+      uint32_t drop_kbh = 0;
+      const int drop_b0 = 2 * (r & 1);
+      if constexpr (DROP) drop_kbh = drop_key_bh(dr, w.b * shp.Hq + hq);
       float m = -INFINITY;  // running exponent base (scaled log2 units)
       float l = 0.f;        // running row sum of exp2(s * c2 - m)
       // mask words are loaded one key tile ahead, so the load's latency hides behind a tile
@@ -547,6 +551,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         }
         uint64_t sum2[4] = {0, 0, 0, 0};
         uint32_t pk[C::SEP_P ? BN / 2 : 1];  // P_t, packed, until the previous P_t V has run
+        uint32_t drop_k2 = 0;
+        if constexpr (DROP) drop_k2 = drop_key2(drop_kbh, r, key0);
 #pragma unroll
         for (int cc = 0; cc < BN / 32; ++cc) {
           uint32_t packed[16];
@@ -557,7 +563,9 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             // POLY_MASK of every 8 pairs on the FMA pipe, the rest on MUFU
             const uint64_t e = (i & 7) < poly_mask<D>() ? exp2_poly2(x) : exp2_mufu2(x);
             packed[i] = pack2_f2<DT>(e);
-            sum2[i & 3] = fadd2(sum2[i & 3], e);
+            sum2[i & 3] = fadd2(sum2[i & 3], e);  // the row sum counts dropped values too
+            if constexpr (DROP)
+              packed[i] &= keep_mask2(drop_word(drop_k2, r, key0 + c0), drop_b0, drop_b0 + 1, dr.t);
           }
           if constexpr (C::SEP_P) {
 #pragma unroll
@@ -624,7 +632,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         tc_fence_after();
       }
       const bool row_ok = r < w.sq.nq;
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float inv_l = (l > 0.f ? 1.f / l : 0.f) * (DROP ? dr.r : 1.f);
       uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)hq * o_sh + (long long)(w.sq.q0 + r) * o_sn;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
@@ -667,11 +675,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool PACK, bool WIN, bool BITS = false>
+template <int D, int DT, bool PACK, bool WIN, bool BITS = false, bool DROP = false>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D, DT, PACK, WIN, BITS>;
+  auto kern = fa_fwd_kernel<D, DT, PACK, WIN, BITS, DROP>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -690,7 +698,7 @@ int launch_fwd_t(const FwdArgs& a) {
   const int sms = device_sm_count();
   const int n_cta = n_units < sms ? n_units : sms;
   kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, static_cast<uint16_t*>(a.o),
-                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units, a.mask);
+                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units, a.mask, a.drop);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -698,6 +706,7 @@ int launch_fwd_t(const FwdArgs& a) {
 // masks, are separate instantiations.
 template <int D, int DT>
 int launch_fwd_l(const FwdArgs& a) {
+  if (a.drop.t) return launch_fwd_t<D, DT, false, false, false, true>(a);  // dense, unpacked, no mask or window
   if (a.mask.bits) return launch_fwd_t<D, DT, false, false, true>(a);  // dense, unpacked, no window
   if (a.shape.window > 0)
     return a.shape.pack_g > 1 ? launch_fwd_t<D, DT, true, true>(a) : launch_fwd_t<D, DT, false, true>(a);

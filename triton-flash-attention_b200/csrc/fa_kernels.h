@@ -22,6 +22,7 @@ struct FwdArgs {
   long long o_sb, o_sh, o_sn;
   float* lse;
   MaskBits mask;  // dense boolean mask (bits == nullptr: none)
+  DropArgs drop;  // attention dropout (t == 0: none)
   cudaStream_t stream;
 };
 
@@ -39,6 +40,7 @@ struct BwdArgs {
   long long dv_sb, dv_sh, dv_sn;
   int accumulate_fp32;
   MaskBits mask;  // dense boolean mask (bits == nullptr: none)
+  DropArgs drop;  // attention dropout (t == 0: none)
   cudaStream_t stream;
 };
 
