@@ -479,9 +479,14 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
           const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
           const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
           if constexpr (DROP) {
-            const int kb = (wt.kv0 + rl) & 1;
-            const uint32_t m01 = keep_mask2(drop_word(drop_k2, q0 + c, wt.kv0 + rl), kb, 2 + kb, dr.t);
-            const uint32_t m23 = keep_mask2(drop_word(drop_k2, q0 + c + 2, wt.kv0 + rl), kb, 2 + kb, dr.t);
+            // the words of query pairs (c, c+1) and (c+2, c+3) for this key row pair
+            const int kb = rl & 1;  // kv0 is even
+            uint32_t w01, w23;
+            shared_words(drop_word(drop_k2, q0 + c + 2 * kb, wt.kv0 + rl), kb, w01, w23);
+            const uint32_t sel = kb ? keep_sel(1, 3) : keep_sel(0, 2);
+            const uint32_t tt = (256u - dr.t) * 0x10001u;
+            const uint32_t m01 = keep_mask2(w01, sel, tt);
+            const uint32_t m23 = keep_mask2(w23, sel, tt);
             const uint64_t r2 = f2pack(dr.r, dr.r);
             const uint32_t n01 = pack2_f2<DT>(f2pack(nd.x, nd.y)), n23 = pack2_f2<DT>(f2pack(nd.z, nd.w));
             const uint32_t k01 = pack2_f2<DT>(ffma2(f2pack(dpt[c], dpt[c + 1]), r2, f2pack(nd.x, nd.y)));

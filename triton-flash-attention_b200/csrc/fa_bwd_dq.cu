@@ -380,11 +380,19 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
         uint32_t pk_ds[32];
         if constexpr (DROP) {
           const uint32_t k2 = drop_key2(drop_kbh, r, key0);
+          const uint32_t sel = drop_b0 ? keep_sel(2, 3) : keep_sel(0, 1);
+          const uint32_t tt = (256u - dr.t) * 0x10001u;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const uint32_t m = keep_mask2(drop_word(k2, r, key0 + 2 * i), drop_b0, drop_b0 + 1, dr.t);
-            const uint32_t dk = pack2_f2<DT>(ffma2(f2pack(dp[2 * i], dp[2 * i + 1]), r2, ndelta2));
-            pk_ds[i] = mul2<DT>(pk_p[i], (dk & m) | (nd_pk & ~m));
+          for (int j = 0; j < 16; ++j) {
+            uint32_t w2[2];
+            shared_words(drop_word(k2, r, key0 + 4 * j + 2 * (r & 1)), r & 1, w2[0], w2[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int i = 2 * j + h;
+              const uint32_t m = keep_mask2(w2[h], sel, tt);
+              const uint32_t dk = pack2_f2<DT>(ffma2(f2pack(dp[2 * i], dp[2 * i + 1]), r2, ndelta2));
+              pk_ds[i] = mul2<DT>(pk_p[i], (dk & m) | (nd_pk & ~m));
+            }
           }
         } else {
 #pragma unroll

@@ -135,11 +135,23 @@ __device__ __forceinline__ uint32_t drop_word(uint32_t key2, int q, int k) {
   return mix32(key2 ^ ((((uint32_t(q) >> 1) & 0xFFFFu) << 16) | ((uint32_t(k) >> 1) & 0xFFFFu)));
 }
 // Lane mask (0xFFFF per kept 16-bit lane) of an element pair: bytes b0 (low
-// lane) and b1 (high lane) of word.
-__device__ __forceinline__ uint32_t keep_mask2(uint32_t word, int b0, int b1, uint32_t t) {
-  const uint32_t lo = ((word >> (8 * b0)) & 0xFFu) >= t ? 0x0000FFFFu : 0u;
-  const uint32_t hi = ((word >> (8 * b1)) & 0xFFu) >= t ? 0xFFFF0000u : 0u;
-  return lo | hi;
+// lane) and b1 (high lane) of word.  sel = b0 | 0x40 | b1 << 8 | 0x4000 moves
+// them to bits 0-7 and 16-23 (byte_perm), tt = (256 - t) * 0x10001 carries
+// each into bit 8 / 24 iff byte >= t.
+__host__ __device__ constexpr uint32_t keep_sel(int b0, int b1) {
+  return uint32_t(b0) | 0x40u | (uint32_t(b1) << 8) | 0x4000u;
+}
+__device__ __forceinline__ uint32_t keep_mask2(uint32_t word, uint32_t sel, uint32_t tt) {
+  const uint32_t z = __byte_perm(word, 0u, sel) + tt;
+  return ((z >> 8) & 0x00010001u) * 0xFFFFu;
+}
+// Words of the block pairs (2j, 2j + 1) that lanes l and l ^ 1 share (rows,
+// or key rows, 2i and 2i + 1 lie in one 2 x 2 block): this lane hashes the
+// one of index 2j + odd and takes the other from its partner.
+__device__ __forceinline__ void shared_words(uint32_t mine, int odd, uint32_t& w_even, uint32_t& w_odd) {
+  const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+  w_even = odd ? other : mine;
+  w_odd = odd ? mine : other;
 }
 
 // Hides the columns of s whose bit in words is clear (bit c & 31 of word

@@ -564,8 +564,17 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
             const uint64_t e = (i & 7) < poly_mask<D>() ? exp2_poly2(x) : exp2_mufu2(x);
             packed[i] = pack2_f2<DT>(e);
             sum2[i & 3] = fadd2(sum2[i & 3], e);  // the row sum counts dropped values too
-            if constexpr (DROP)
-              packed[i] &= keep_mask2(drop_word(drop_k2, r, key0 + c0), drop_b0, drop_b0 + 1, dr.t);
+          }
+          if constexpr (DROP) {
+            const uint32_t sel = (r & 1) ? keep_sel(2, 3) : keep_sel(0, 1);
+            const uint32_t tt = (256u - dr.t) * 0x10001u;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint32_t we, wo;
+              shared_words(drop_word(drop_k2, r, key0 + cc * 32 + 4 * j + 2 * (r & 1)), r & 1, we, wo);
+              packed[2 * j] &= keep_mask2(we, sel, tt);
+              packed[2 * j + 1] &= keep_mask2(wo, sel, tt);
+            }
           }
           if constexpr (C::SEP_P) {
 #pragma unroll
