@@ -12,7 +12,10 @@ saves.  p is applied in steps of 1/256 (t = round(256 p) of 256 random byte
 values are dropped), and the scale is 256 / (256 - t), so the expectation is
 exact for the p actually applied.  The seed comes from PyTorch's default
 CPU generator, so ``torch.manual_seed`` makes runs repeatable.  The backward
-runs the separate dQ and dK/dV kernels (bitwise reproducible).
+runs the separate dQ and dK/dV kernels (bitwise reproducible).  The seed is
+a kernel argument: a CUDA graph captured around a dropout call replays the
+pattern it was captured with; call the functions below with a new seed per
+step to draw new patterns outside a graph.
 """
 
 from __future__ import annotations
