@@ -505,6 +505,11 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
 }
 
 // ---------------------------------------------------------------------------
+// fwd_dense_impl / bwd_dense_impl: the dense-layout forward and whole
+// backward with the options the plain calls lack -- a value head size of
+// its own, a packed boolean mask, dropout -- behind fa_*_vdim, fa_*_masked
+// and fa_*_dropout.
+//
 // Value head size Dv different from the query/key head size D (the
 // reference hands these inputs to PyTorch, attention.py:639-646).  The
 // kernels run at width W = max(D, Dv): the narrower operands are read
@@ -521,6 +526,11 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
 // through a MaskBits kernel parameter, in instantiations of their own.  A mask
 // goes with the dense layout, no GQA packing of the forward, no window and
 // no position offsets.
+//
+// Dropout (fa_fwd_dropout, fa_bwd_dropout; the reference has none): a
+// DropArgs kernel parameter (threshold, scale, seed) in instantiations of
+// their own; the backward always runs the separate dQ and dK/dV kernels,
+// whose threads hold P and dS of an element together.
 
 // A packed mask's word strides {batch, head, row}: non-negative, 16-byte
 // aligned rows of at least `words` words.
@@ -532,7 +542,7 @@ bool mask_ok(const uint32_t* bits, const int64_t* st, int words) {
   return true;
 }
 
-int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
+int fwd_dense_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv, int Nq,
                   int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
                   const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal, void* stream,
                   int dtype, const uint32_t* mask = nullptr, const int64_t* mask_strides = nullptr,
@@ -571,7 +581,7 @@ int fwd_vdim_impl(const void* q, const void* k, const void* v, void* o, float* l
   return launch_fwd(a, W);
 }
 
-int bwd_vdim_impl(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
+int bwd_dense_impl(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
                   void* dq, void* dk, void* dv, float* delta, float* dq_accum, int B, int Hq, int Hkv, int Nq, int Nk,
                   int D, int Dv, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                   const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
@@ -867,14 +877,14 @@ extern "C" int fa_fwd_vdim(const void* q, const void* k, const void* v, void* o,
                            int Nq, int Nk, int D, int Dv, const int64_t* q_strides, const int64_t* k_strides,
                            const int64_t* v_strides, const int64_t* o_strides, float softmax_scale, int causal,
                            void* stream) {
-  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+  return fwd_dense_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
                        softmax_scale, causal, stream, DT_F16);
 }
 extern "C" int fa_fwd_vdim_bf16(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
                                 int Hkv, int Nq, int Nk, int D, int Dv, const int64_t* q_strides,
                                 const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
                                 float softmax_scale, int causal, void* stream) {
-  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+  return fwd_dense_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
                        softmax_scale, causal, stream, DT_BF16);
 }
 extern "C" int fa_bwd_vdim(const void* q, const void* k, const void* v, const void* o, const void* dO,
@@ -884,7 +894,7 @@ extern "C" int fa_bwd_vdim(const void* q, const void* k, const void* v, const vo
                            const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
                            const int64_t* dv_strides, float softmax_scale, int causal, int deterministic,
                            void* stream) {
-  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+  return bwd_dense_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
                        k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
                        causal, deterministic, stream, DT_F16);
 }
@@ -895,7 +905,7 @@ extern "C" int fa_bwd_vdim_bf16(const void* q, const void* k, const void* v, con
                                 const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
                                 const int64_t* dv_strides, float softmax_scale, int causal, int deterministic,
                                 void* stream) {
-  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+  return bwd_dense_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
                        k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
                        causal, deterministic, stream, DT_BF16);
 }
@@ -915,7 +925,7 @@ static int fwd_masked_entry(const void* q, const void* k, const void* v, void* o
                             const int64_t* v_strides, const int64_t* o_strides, const uint32_t* mask_bits,
                             const int64_t* mask_strides, float softmax_scale, int causal, void* stream, int dtype) {
   if (!mask_bits || !mask_strides) return FA_ERR_BAD_SHAPE;
-  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+  return fwd_dense_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
                        softmax_scale, causal, stream, dtype, mask_bits, mask_strides);
 }
 extern "C" int fa_fwd_masked(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq, int Hkv,
@@ -942,7 +952,7 @@ static int bwd_masked_entry(const void* q, const void* k, const void* v, const v
                             const uint32_t* mask_bits_t, const int64_t* mask_t_strides, float softmax_scale,
                             int causal, int deterministic, void* stream, int dtype) {
   if (!mask_bits || !mask_strides || !mask_bits_t || !mask_t_strides) return FA_ERR_BAD_SHAPE;
-  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+  return bwd_dense_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, dq_accum, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
                        k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
                        causal, deterministic, stream, dtype, mask_bits, mask_strides, mask_bits_t, mask_t_strides);
 }
@@ -992,7 +1002,7 @@ static int fwd_dropout_entry(const void* q, const void* k, const void* v, void* 
   DropArgs d;
   int rc = drop_args(dropout_p, seed, &d);
   if (rc) return rc;
-  return fwd_vdim_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
+  return fwd_dense_impl(q, k, v, o, lse, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides, k_strides, v_strides, o_strides,
                        softmax_scale, causal, stream, dtype, nullptr, nullptr, &d);
 }
 extern "C" int fa_fwd_dropout(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
@@ -1019,7 +1029,7 @@ static int bwd_dropout_entry(const void* q, const void* k, const void* v, const 
   DropArgs d;
   int rc = drop_args(dropout_p, seed, &d);
   if (rc) return rc;
-  return bwd_vdim_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, nullptr, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
+  return bwd_dense_impl(q, k, v, o, dO, lse, dq, dk, dv, delta, nullptr, B, Hq, Hkv, Nq, Nk, D, Dv, q_strides,
                        k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, softmax_scale,
                        causal, 1, stream, dtype, nullptr, nullptr, nullptr, nullptr, &d);
 }
