@@ -89,6 +89,21 @@ def test_dropout_argument_checks():
         assert rc == _abi.FA_ERR_BAD_SHAPE, p
 
 
+def test_dropout_with_mask_is_refused(monkeypatch):
+    """attn_mask and dropout_p together raise before any CUDA call (the
+    device checks are faked, no GPU here)."""
+    class FakeDevice:
+        type = "cuda"
+
+    fake = FakeDevice()
+    q = torch.zeros(1, 2, 8, 64, dtype=torch.float16)
+    mask = torch.ones(8, 8, dtype=torch.bool)
+    monkeypatch.setattr(torch.Tensor, "device", property(lambda self: fake), raising=False)
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
+    with pytest.raises(RuntimeError, match="attn_mask and dropout_p together"):
+        fa.scaled_dot_product_attention(q, q, q, attn_mask=mask, dropout_p=0.1)
+
+
 # ---------------------------------------------------------------------------
 # GPU
 
