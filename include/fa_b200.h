@@ -59,7 +59,9 @@ enum {
   FA_ERR_DRIVER = 6,               /* the driver entry point could not be resolved */
   FA_ERR_DEVICE_TIMEOUT = 7,       /* a kernel's bounded wait gave up (see fa_device_status) */
   FA_ERR_NO_DEVICE = 8,            /* no sm_100 device is current */
-  FA_ERR_SCRATCH_LIMIT = 9         /* the call needs more than FA_NOALLOC_SCRATCH_BYTES */
+  FA_ERR_SCRATCH_LIMIT = 9,        /* the call needs more than FA_NOALLOC_SCRATCH_BYTES */
+  FA_ERR_OUT_OF_MEMORY = 10,       /* the device had no memory for the library's scratch array */
+  FA_ERR_CUDA = 11                 /* another CUDA runtime call failed (fa_status_string names it) */
 };
 
 /* Forward: O = softmax(scale * Q K^T [+ causal mask]) V and the base-2 LSE.
@@ -273,7 +275,13 @@ FA_API int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_c
  * FA_ERR_SCRATCH_LIMIT before touching the GPU.  The library allocates
  * nothing on this path.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress, with that device current); make that
- * first call before any stream capture.  All calls share the array and it
+ * first call before any stream capture.  When the lookup fails the call
+ * returns FA_ERR_OUT_OF_MEMORY (the module that holds the array could not be
+ * loaded) or FA_ERR_CUDA (any other runtime error, e.g. a lookup inside a
+ * stream capture; fa_status_string(FA_ERR_CUDA) then gives CUDA's text).
+ * The looked-up address is cached per device for the life of the process,
+ * which assumes the device's primary context is never reset
+ * (cudaDeviceReset) while the library is loaded.  All calls share the array and it
  * keeps the last call's contents (each call re-zeroes what must start at
  * zero), so calls that overlap on the GPU -- on two streams, or from two
  * host threads on one device -- race and give wrong gradients. */

@@ -10,7 +10,7 @@ fixed entry of the reference's own autotune tables (attention.py:82-87,
 arguments of ``TritonAttention.forward/backward`` (attention.py:676-771).
 
 Usage (in a checkout that has the reference at REF_ROOT):
-    python tests/golden/make_golden.py [REF_ROOT]
+    python tests/golden/make_golden.py REF_ROOT   (the reference checkout; required)
 writes ``tests/golden/golden.npz``.  Inputs follow the reference's CUDA test
 (tests/test_cuda_correctness.py:26-60): q/k/v = 0.5 * randn, dO = 0.1 * randn,
 fp16, with the seeds listed in CASES.
@@ -90,4 +90,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <root of the reference checkout>")
+    main(sys.argv[1])

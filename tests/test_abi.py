@@ -38,6 +38,8 @@ def test_version_and_status_strings():
     assert "head_dim" in _abi.status_string(_abi.FA_ERR_UNSUPPORTED_HEAD_DIM)
     assert "16-byte" in _abi.status_string(_abi.FA_ERR_MISALIGNED)
     assert "timed out" in _abi.status_string(_abi.FA_ERR_DEVICE_TIMEOUT)
+    assert "out of device memory" in _abi.status_string(_abi.FA_ERR_OUT_OF_MEMORY)
+    assert _abi.status_string(_abi.FA_ERR_CUDA)  # CUDA's text once a call recorded one
 
 
 def _strides():

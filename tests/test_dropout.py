@@ -13,7 +13,8 @@ oracle's dropout attention equals PyTorch float64 autograd of
 and the ABI.  GPU tests:
 * the kernels' patterns equal the oracle's bit for bit: the forward's read
   out of O with uniform scores and V = I (O[q, k] = Z[q, k] r / Nk), the
-  dK/dV kernel's out of dV with dO = I, including query indices past 2^17;
+  dK/dV kernel's out of dV with dO = I, including query and key indices
+  past 2^17;
 * parity of forward and backward with the float64 oracle on the same
   pattern (D 32/64/128, causal, GQA, cross-attention, Dv != D, p 0.1 and
   0.5, bf16) at the equal-width tolerances scaled by r;
@@ -89,6 +90,15 @@ def test_dropout_argument_checks():
         assert rc == _abi.FA_ERR_BAD_SHAPE, p
 
 
+def test_dropout_rate_that_rounds_to_nothing_is_refused():
+    """Rates are applied as the nearest multiple of 1/256 (at least 1/256):
+    a rate below 1/512 would silently run at 1/256 and is refused."""
+    t = torch.zeros(1, 1, 4, 32, dtype=torch.float16)
+    for bad in (0.001, 1e-6, 0.999):
+        with pytest.raises(ValueError, match="steps of 1/256"):
+            fa.scaled_dot_product_attention(t, t, t, dropout_p=bad)
+
+
 def test_dropout_with_mask_is_refused(monkeypatch):
     """attn_mask and dropout_p together raise before any CUDA call (the
     device checks are faked, no GPU here)."""
@@ -145,6 +155,30 @@ def test_dkdv_pattern_bitwise(d):
     got = (dv > 0).cpu().numpy()  # (b, h, nk, d = nq)
     want = orc.dropout_keep_reference(seed, b, h, nq, nk, p).swapaxes(2, 3)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.gpu
+def test_key_index_high_bits_pattern():
+    """Key indices past 2^17 (the key half of the block word's high bits,
+    drop_key2): the forward's pattern read out of O with V one-hot on the keys
+    [2^17 + 128, 2^17 + 160) (O[q, j] = Z[q, k0 + j] r / Nk), and the dK/dV
+    kernel's out of dV with dO = I over every key."""
+    b = h = 1
+    nq = d = 32
+    nk, k0 = 2 ** 17 + 256, 2 ** 17 + 128
+    p, seed = 0.3, 2 ** 33 + 99
+    q = torch.zeros(b, h, nq, d, device="cuda", dtype=torch.float16)
+    k = torch.zeros(b, h, nk, d, device="cuda", dtype=torch.float16)
+    v = torch.zeros(b, h, nk, d, device="cuda", dtype=torch.float16)
+    v[0, 0, k0 + torch.arange(d), torch.arange(d)] = 1
+    o, lse = fa.attention_forward_dropout(q, k, v, False, 1.0, p, seed)
+    want = orc.dropout_keep_reference(seed, b, h, nq, nk, p)  # (b, h, nq, nk)
+    torch.cuda.synchronize()
+    assert np.array_equal((o > 0).cpu().numpy(), want[..., k0:k0 + d])
+    do = torch.eye(nq, d, device="cuda", dtype=torch.float16).expand(b, h, nq, d).contiguous()
+    _, _, dv = fa.attention_backward_dropout(q, k, v, o, do, lse, False, 1.0, p, seed)
+    torch.cuda.synchronize()
+    assert np.array_equal((dv > 0).cpu().numpy(), want.swapaxes(2, 3))
 
 
 CASES = [

@@ -25,6 +25,8 @@ FA_ERR_DRIVER = 6
 FA_ERR_DEVICE_TIMEOUT = 7
 FA_ERR_NO_DEVICE = 8
 FA_ERR_SCRATCH_LIMIT = 9
+FA_ERR_OUT_OF_MEMORY = 10
+FA_ERR_CUDA = 11
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -103,12 +105,20 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+_entries: dict = {}
+
+
 def entry(name: str, dtype) -> ctypes._CFuncPtr:
     """The entry point ``name`` for operands of ``dtype`` (torch.float16 or
-    torch.bfloat16): the fp16 symbol or its ``_bf16`` twin."""
-    import torch
+    torch.bfloat16): the fp16 symbol or its ``_bf16`` twin (looked up once)."""
+    key = (name, dtype)
+    fn = _entries.get(key)
+    if fn is None:
+        import torch
 
-    return getattr(lib(), name + "_bf16" if dtype == torch.bfloat16 else name)
+        fn = getattr(lib(), name + "_bf16" if dtype == torch.bfloat16 else name)
+        _entries[key] = fn
+    return fn
 
 
 def status_string(code: int) -> str:
@@ -120,12 +130,24 @@ def check(rc: int, what: str) -> None:
         raise RuntimeError(f"{what} failed: {status_string(rc)} (code {rc})")
 
 
+_Strides3 = ctypes.c_int64 * 3
+_strides_cache: dict = {}
+
+
 def strides3(t) -> ctypes.Array:
-    """(batch, head, seq) element strides of a 4-D (B, H, N, D) tensor."""
+    """(batch, head, seq) element strides of a 4-D (B, H, N, D) tensor, as a
+    ctypes array shared by every call with the same strides (the library
+    only reads it)."""
     s = t.stride()
     if s[3] != 1:
         raise ValueError("the head dimension must be contiguous (unit stride)")
-    return (ctypes.c_int64 * 3)(s[0], s[1], s[2])
+    key = s[:3]
+    arr = _strides_cache.get(key)
+    if arr is None:
+        if len(_strides_cache) > 1024:
+            _strides_cache.clear()
+        arr = _strides_cache[key] = _Strides3(*key)
+    return arr
 
 
 def device_status(reset: bool = False) -> int:

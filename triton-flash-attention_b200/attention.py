@@ -72,6 +72,21 @@ def _validate_inputs(query, key, value, *, enable_gqa: bool) -> None:
             "key/value heads")
 
 
+_capability: dict = {}
+
+
+def _device_capability(device: torch.device) -> tuple[int, int]:
+    """(major, minor) compute capability of a CUDA device, queried once per
+    device index."""
+    index = getattr(device, "index", None)
+    if index is None:
+        return torch.cuda.get_device_capability(device)
+    cap = _capability.get(index)
+    if cap is None:
+        cap = _capability[index] = torch.cuda.get_device_capability(device)
+    return cap
+
+
 def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> DispatchDecision:
     """Explain whether the B200 kernels can serve these inputs
     (attention.py:629-670).  Query and key lengths may differ (the causal
@@ -79,6 +94,11 @@ def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> Dispatch
     query/key and value head sizes (the reference sends both to PyTorch,
     attention.py:639-646); each head size must be 32, 64 or 128."""
     _validate_inputs(query, key, value, enable_gqa=enable_gqa)
+    return _dispatch(query, value)
+
+
+def _dispatch(query, value) -> DispatchDecision:
+    """The dispatch decision for inputs that passed ``_validate_inputs``."""
     if query.device.type != "cuda":
         return DispatchDecision("unsupported", "the B200 kernel requires a CUDA tensor")
     if torch.version.hip is not None:
@@ -93,7 +113,7 @@ def explain_dispatch(query, key, value, *, enable_gqa: bool = False) -> Dispatch
     if value.shape[-1] not in SUPPORTED_HEAD_DIMS:
         return DispatchDecision(
             "unsupported", f"the value head_dim must be one of ({supported}) for the B200 path")
-    major, minor = torch.cuda.get_device_capability(query.device)
+    major, minor = _device_capability(query.device)
     if (major, minor) != (10, 0):
         return DispatchDecision(
             "unsupported", "the kernels are built for sm_100a (B200) GPUs only")
@@ -228,6 +248,8 @@ def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale
 
 
 FUSED_BWD_HEAD_DIMS = (32, 64)
+# dropout rates are applied in steps of 1/256 (include/fa_b200.h, fa_fwd_dropout)
+DROPOUT_STEP = 1.0 / 256
 
 
 def fused_backward_enabled(head_dim: int) -> bool:
@@ -248,8 +270,13 @@ def attention_backward_fused(q, k, v, o, do, lse, causal: bool, softmax_scale: f
     b, hq, nq, d = q.shape
     hkv, nk = k.shape[1], k.shape[2]
     stream = _stream_handle(q.device)
-    delta = torch.empty((b, hq, nq), device=q.device, dtype=torch.float32)
-    dq_acc = torch.empty((b, hq, nq, d), device=q.device, dtype=torch.float32)
+    # Delta and the dQ accumulator in one allocation; the accumulator starts
+    # 256 bytes aligned
+    rows = b * hq * nq
+    rows_pad = (rows + 63) // 64 * 64
+    scratch = torch.empty(rows_pad + rows * d, device=q.device, dtype=torch.float32)
+    delta = scratch[:rows].view(b, hq, nq)
+    dq_acc = scratch[rows_pad:].view(b, hq, nq, d)
     rc = _abi.entry("fa_bwd_preprocess", o.dtype)(o.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_acc.data_ptr(),
                                                   b, hq, nq, d, _abi.strides3(o), _abi.strides3(do), stream)
     _abi.check(rc, "fa_bwd_preprocess")
@@ -326,10 +353,11 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
     zeros (PyTorch returns NaN).
 
     ``dropout_p`` (an addition; the reference has no dropout) drops the
-    softmax probabilities at that rate, as PyTorch's SDPA does, applied in
-    steps of 1/256; the pattern is drawn from a seed taken from PyTorch's
-    default generator (``torch.manual_seed`` repeats it).  It cannot be
-    combined with ``attn_mask``."""
+    softmax probabilities at that rate, as PyTorch's SDPA does, applied as
+    the nearest multiple of 1/256 (rates below 1/512, which would round to
+    nothing, raise ``ValueError``); the pattern is drawn from a seed taken
+    from PyTorch's default generator (``torch.manual_seed`` repeats it).  It
+    cannot be combined with ``attn_mask``."""
     if backend == "torch":
         raise RuntimeError(
             "backend='torch' (the PyTorch SDPA fallback) is not part of this package; "
@@ -344,8 +372,13 @@ def scaled_dot_product_attention(query, key, value, *, is_causal: bool = False, 
         raise ValueError("scale must be a finite real number or None")
     if isinstance(dropout_p, bool) or not isinstance(dropout_p, Real) or not 0.0 <= float(dropout_p) < 1.0:
         raise ValueError("dropout_p must be a real number in [0, 1)")
+    if dropout_p > 0.0 and not DROPOUT_STEP / 2 <= float(dropout_p) <= 1.0 - DROPOUT_STEP / 2:
+        raise ValueError(
+            f"dropout_p is applied in steps of 1/256 (the nearest multiple, from 1/256 to 255/256); "
+            f"{float(dropout_p):g} would run at {max(1, min(255, round(256 * float(dropout_p)))) / 256:g}: "
+            f"pass 0 or a rate in [1/512, 511/512]")
     _validate_inputs(query, key, value, enable_gqa=enable_gqa)
-    decision = explain_dispatch(query, key, value, enable_gqa=enable_gqa)
+    decision = _dispatch(query, value)
     if decision.backend != "cuda":
         raise RuntimeError(f"B200 CUDA backend is unavailable: {decision.reason}")
     if attn_mask is not None:

@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -856,6 +857,17 @@ extern "C" int fa_device_status(int reset) {
   return v;
 }
 
+namespace fa {
+namespace {
+std::atomic<const char*> g_last_cuda_error{nullptr};
+}  // namespace
+void record_cuda_error(cudaError_t e) { g_last_cuda_error.store(cudaGetErrorString(e)); }
+const char* last_cuda_error_text() {
+  const char* t = g_last_cuda_error.load();
+  return t ? t : "a CUDA runtime call failed";
+}
+}  // namespace fa
+
 extern "C" const char* fa_status_string(int code) {
   switch (code & 0xff) {
     case FA_OK: return "ok";
@@ -868,6 +880,8 @@ extern "C" const char* fa_status_string(int code) {
     case FA_ERR_DEVICE_TIMEOUT: return "a kernel wait timed out on the device";
     case FA_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
     case FA_ERR_SCRATCH_LIMIT: return "the call needs more scratch than FA_NOALLOC_SCRATCH_BYTES (32 MiB)";
+    case FA_ERR_OUT_OF_MEMORY: return "out of device memory for the library's scratch array";
+    case FA_ERR_CUDA: return last_cuda_error_text();
     default: return "unknown error";
   }
 }

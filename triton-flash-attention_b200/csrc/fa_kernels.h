@@ -58,6 +58,11 @@ inline int device_sm_count() {
   return cache[dev];
 }
 
+// The text of the CUDA runtime error behind the last FA_ERR_CUDA status
+// (cudaGetErrorString's static string), for fa_status_string.
+void record_cuda_error(cudaError_t e);
+const char* last_cuda_error_text();
+
 int launch_fwd(const FwdArgs& a, int D);
 int launch_bwd_dq(const BwdArgs& a, int D);
 int launch_bwd_dkdv(const BwdArgs& a, int D);

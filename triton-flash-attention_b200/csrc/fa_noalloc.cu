@@ -33,6 +33,9 @@ static __device__ __align__(256) float g_bwd_scratch[kScratchFloats];
 namespace {
 
 // Device address of this device's scratch array, looked up once per device.
+// The cached address assumes the device's primary context is never reset
+// (cudaDeviceReset) while the library is loaded: a new context loads the
+// module again, possibly at another address.
 float* scratch_ptr(int* rc) {
   static float* ptrs[64] = {nullptr};
   static std::mutex mu;
@@ -47,7 +50,14 @@ float* scratch_ptr(int* rc) {
     const cudaError_t e = cudaGetSymbolAddress(&p, g_bwd_scratch);
     if (e != cudaSuccess || p == nullptr) {
       cudaGetLastError();  // clear the error so that the next CUDA call does not report it
-      *rc = FA_ERR_NO_DEVICE;
+      if (e == cudaErrorMemoryAllocation) {
+        *rc = FA_ERR_OUT_OF_MEMORY;  // the module holding the array could not be loaded
+      } else if (e == cudaErrorNoDevice || e == cudaErrorInvalidDevice) {
+        *rc = FA_ERR_NO_DEVICE;
+      } else {
+        fa::record_cuda_error(e == cudaSuccess ? cudaErrorInvalidSymbol : e);
+        *rc = FA_ERR_CUDA;
+      }
       return nullptr;
     }
     ptrs[dev] = static_cast<float*>(p);
