@@ -25,12 +25,25 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 * ``graph``: the same step captured once in a CUDA graph (torch.cuda.graph)
   and replayed -- the launch gaps between the four kernels removed; an extra
   key, the metric stays the eager ``value``.
-* ``cpu_baseline``: the oracle's float32 restatement of the reference's CPU
-  path timed on the host cores on a bounded sample (whole heads of C2).
+* ``cpu_baseline``: the reference's own CPU path (``backend="auto"`` on CPU
+  fp16 tensors, which the reference sends to PyTorch's SDPA) from the
+  unmodified install in baseline/_ref, timed on every host core on a bounded
+  sample (whole C2 batch elements); the oracle's float32 restatement stands
+  in when the reference is not installed (``kind: "port"``).
+* ``per_rank``: every rank's mean, median and slowest step; the timed region
+  is enqueued while the stream is held by a bounded spin, so a host stall
+  cannot open a gap in it, and one clock sampler runs per node.
+* comparators (1 GPU): the same step through the reference's own Triton
+  kernel (``reference_triton_ms``), PyTorch's SDPA (``torch_sdpa_ms``,
+  ``cudnn_sdpa_ms``) and this build's public API (``api_ms_per_step``), with
+  each one's max-abs error against fp32 on two heads.
+* ``ring``: C5 (B1 Hq32 Hkv8 N131072 D128 causal) with ring context
+  parallelism over the job's GPUs -- its ms per step, and a parity check of
+  the ring against the single-GPU kernels and fp32 at N 16384.
 * Multi-GPU (torchrun): weak scaling -- every rank runs its own C2-sized
   batch shard; no collective touches the data path.
-* ``--impl reference``: the reference's CPU implementation of the path (the
-  oracle port of its SDPA fallback) on the host cores; rank 0 only.
+* ``--impl reference``: the reference's CPU path as above, on the host
+  cores; rank 0 only.
 * ``--workload sweep``: the parity/measurement configurations C3 (non-causal,
   B4 H16, D in {32,64,128} x N in {512,...,8192}) and C4 (GQA causal), forward
   and forward+backward through the public API, one JSON line per
@@ -86,28 +99,35 @@ def read_peaks() -> dict:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi clocks and throttle reasons of the given GPUs during
+    the timed region.  One sampler per node (the caller starts it on local
+    rank 0 only), so the ranks' timed loops do not share the host with one
+    nvidia-smi process each."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices, active: bool = True, period_ms: int = 200):
+        self.indices = list(indices)
+        self.active = active
+        self.period_ms = period_ms
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
-        time.sleep(0.3)
+        if self.active:
+            try:
+                ids = ",".join(str(i) for i in self.indices)
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={ids}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                     "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self.proc = None
+            time.sleep(0.3)
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -119,16 +139,19 @@ class ClockSampler:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
         return False
 
-    def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
+    def summary(self) -> dict | None:
+        if not self.active:
+            return None
+        sm, mx, reasons, gpus = [], None, set(), set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
             try:
                 sm.append(float(f[1]))
                 mx = float(f[2])
+                gpus.add(f[0])
             except ValueError:
                 continue
             for name, val in zip(names, f[5:9]):
@@ -136,37 +159,95 @@ class ClockSampler:
                     reasons.add(name)
         loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": len(gpus)}
+
+
+def hold_stream(ms: float = 50.0) -> None:
+    """Occupies the current stream for about ``ms`` milliseconds (torch's
+    bounded clock spin) before a timed region, so that the host enqueues the
+    whole region while the GPU is still busy: a host-side stall (scheduler,
+    an nvidia-smi query, the interpreter) then cannot open a gap inside the
+    timed region.  The spin runs before the start event and is not timed."""
+    import torch
+    torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_baseline(max_seconds: float = 12.0) -> dict:
-    """Oracle (float32 numpy/BLAS) forward+backward on whole C2 heads, timed
-    on the host cores until ``max_seconds`` of work; TFLOP/s of the sample."""
-    import numpy as np
+def _reference_pkg():
+    """The unmodified reference package installed in baseline/_ref, or None."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "triton_flash_attention")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        import triton_flash_attention as ref
+    except Exception:
+        return None
+    return ref
 
-    from oracle import fa2_oracle as orc
+
+def reference_cpu_run(steps: int, warmup: int, batch: int = 1) -> dict:
+    """The reference's own CPU path -- ``scaled_dot_product_attention(...,
+    backend="auto")`` on CPU fp16 tensors, which the reference dispatches to
+    PyTorch's SDPA (attention.py:774-786, 832-839) -- forward + backward on
+    ``batch`` of C2's batch elements (all 16 heads, N 4096, D 64) per step,
+    on every host core.  Falls back to the oracle's float32 restatement of
+    that path when the reference is not installed."""
+    import torch
+
     from triton_flash_attention_b200.flops import attention_flops
 
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max((i.get("num_threads") or 1) for i in threadpool_info()) if threadpool_info() else 1
-    except Exception:
-        cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    heads = 0
-    t_total = 0.0
-    while heads < B * H and (t_total < max_seconds or heads == 0):
-        q, k, v, do = (rng.standard_normal((N, D)).astype(np.float16) for _ in range(4))
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    ref = _reference_pkg()
+    fl = attention_flops(batch=batch, query_heads=H, sequence=N, head_dim=D, causal=CAUSAL, mode="forward-backward")
+    times = []
+    if ref is not None:
+        g = torch.Generator().manual_seed(0)
+        q, k, v, do = (torch.randn(batch, H, N, D, generator=g).half() for _ in range(4))
+        q, k, v = (t.requires_grad_() for t in (q, k, v))
+
+        def step():
+            o = ref.scaled_dot_product_attention(q, k, v, is_causal=CAUSAL, backend="auto")
+            torch.autograd.grad(o, (q, k, v), do)
+
+        decision = ref.explain_dispatch(q, k, v)
+        kind, what = "reference", (f"triton_flash_attention (unmodified, baseline/_ref), "
+                                   f"backend='auto' -> {decision.backend} ({decision.reason})")
+    else:
+        import numpy as np
+
+        from oracle import fa2_oracle as orc
+        rng = np.random.default_rng(0)
+        qn, kn, vn, don = (rng.standard_normal((N, D)).astype(np.float16) for _ in range(4))
+
+        def step():
+            for _ in range(batch * H):
+                orc.sdpa_head_fwd_bwd_fp32(qn, kn, vn, don, causal=CAUSAL, scale=D ** -0.5)
+
+        kind, what = "port", "the oracle's float32 numpy restatement of the reference's CPU path"
+    for _ in range(warmup):
+        step()
+    for _ in range(steps):
         t0 = time.perf_counter()
-        orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
-        t_total += time.perf_counter() - t0
-        heads += 1
-    fl = attention_flops(batch=1, query_heads=heads, sequence=N, head_dim=D, causal=CAUSAL,
-                         mode="forward-backward")
-    return {"value": fl / t_total / 1e12, "unit": "TFLOP/s", "cores": int(cores), "kind": "port",
-            "sample": f"{heads} of {B * H} (batch, head) pairs of C2, fwd+bwd, float32 numpy+BLAS, "
-                      f"{t_total:.1f} s"}
+        step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": fl / sec / 1e12, "unit": "TFLOP/s", "cores": int(torch.get_num_threads()), "kind": kind,
+            "sec_per_step": sec,
+            "sample": f"each step = fwd+bwd of {batch} of C2's {B} batch elements (B{batch} H{H} N{N} D{D}, causal, "
+                      f"fp16 CPU tensors), median of {steps} steps after {warmup} warm-up; {what}"}
+
+
+def cpu_baseline(max_seconds: float = 15.0) -> dict:
+    """The reference's CPU path timed on the host cores on a bounded sample
+    of C2 (whole batch elements, about ``max_seconds`` of work)."""
+    probe = reference_cpu_run(steps=1, warmup=1)
+    steps = max(3, min(20, int(max_seconds / max(probe["sec_per_step"], 1e-3))))
+    r = reference_cpu_run(steps=steps, warmup=0)
+    r.pop("sec_per_step", None)
+    return r
 
 
 # ------------------------------------------------------------------ distributed plumbing
@@ -195,10 +276,208 @@ def barrier_max(world: int, value: float) -> float:
     return float(t.item())
 
 
+def gather_floats(world: int, values: list[float]) -> list[list[float]]:
+    """Every rank's ``values`` (same length on every rank), in rank order."""
+    if world == 1:
+        return [list(values)]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, device="cuda", dtype=torch.float64)
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.tolist() for p in parts]
+
+
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+def timed_loop(fn, steps: int, warmup: int, world: int = 1, per_step: bool = False):
+    """Runs ``fn`` warmup times, then times ``steps`` calls on the current
+    stream with CUDA events (barrier + synchronize on both sides, the stream
+    held while the host enqueues).  Returns (ms per step on this rank,
+    sorted per-step ms or None)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)] if per_step else []
+    torch.cuda.synchronize()
+    barrier(world)
+    hold_stream()
+    start.record(stream)
+    for i in range(steps):
+        if per_step:
+            evs[i][0].record(stream)
+        fn()
+        if per_step:
+            evs[i][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    return ms, (sorted(a.elapsed_time(b) for a, b in evs) if per_step else None)
+
+
+# ------------------------------------------------------------------ comparators (1 GPU)
+def comparators(args, q, k, v, do) -> dict:
+    """The same C2 step through (a) the reference's own Triton kernel,
+    unmodified, from baseline/_ref (backend="triton"), (b) PyTorch's SDPA
+    (its default backend, and cuDNN forced), and (c) this build's public API
+    (scaled_dot_product_attention + autograd), all with device-resident
+    inputs in this process; plus the max-abs errors of the reference kernel
+    and of this build against fp32 math on two heads."""
+    import torch
+    import torch.nn.functional as F
+
+    import triton_flash_attention_b200 as fa
+
+    fl = flops_step()
+    steps = max(3, min(args.steps, 20))
+    out = {}
+    qc, kc, vc = (t.clone().requires_grad_() for t in (q, k, v))
+    impls = [("api", lambda a, b_, c: fa.scaled_dot_product_attention(a, b_, c, is_causal=CAUSAL))]
+    ref = _reference_pkg()
+    if ref is not None:
+        impls.append(("reference_triton",
+                      lambda a, b_, c: ref.scaled_dot_product_attention(a, b_, c, is_causal=CAUSAL, backend="triton")))
+    impls.append(("torch_sdpa", lambda a, b_, c: F.scaled_dot_product_attention(a, b_, c, is_causal=CAUSAL)))
+
+    def cudnn(a, b_, c):
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            return F.scaled_dot_product_attention(a, b_, c, is_causal=CAUSAL)
+
+    impls.append(("cudnn_sdpa", cudnn))
+    # fp32 math on two heads, the error reference
+    q32, k32, v32 = (t[:1, :2].detach().float().requires_grad_() for t in (q, k, v))
+    o32 = F.scaled_dot_product_attention(q32, k32, v32, is_causal=CAUSAL)
+    g32 = (o32.detach(),) + torch.autograd.grad(o32, (q32, k32, v32), do[:1, :2].float())
+    for name, fn in impls:
+        try:
+            def step():
+                o = fn(qc, kc, vc)
+                torch.autograd.grad(o, (qc, kc, vc), do)
+
+            ms, _ = timed_loop(step, steps, max(args.warmup, 3))
+            qs, ks, vs = (t[:1, :2].detach().clone().requires_grad_() for t in (q, k, v))
+            o = fn(qs, ks, vs)
+            got = (o.detach(),) + torch.autograd.grad(o, (qs, ks, vs), do[:1, :2])
+            errs = {n: round(float((a.float() - r).abs().max()), 6) for n, a, r in zip(("o", "dq", "dk", "dv"), got, g32)}
+            out[name] = {"ms_per_step": round(ms, 4), "tflops": round(fl / ms / 1e9, 2), "max_abs_err_vs_fp32": errs}
+        except Exception as exc:  # reported, not fatal
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+    return out
+
+
+# ------------------------------------------------------------------ ring section (C5)
+RING_B, RING_HQ, RING_HKV, RING_N, RING_D = 1, 32, 8, 131072, 128
+RING_CHECK_N, RING_CHECK_HQ, RING_CHECK_HKV = 16384, 8, 2
+
+
+def ring_parity(world: int, rank: int, dev) -> dict | None:
+    """The ring (zig-zag shards over the ranks, NCCL P2P) at a reduced
+    length, B1 Hq8 Hkv2 N16384 D128 causal: its O, dQ, dK, dV gathered and
+    un-sharded on rank 0 and compared with (a) the single-GPU kernels on the
+    whole sequence and (b) fp32 math on the first GQA group (4 query heads,
+    1 K/V head).  Returns the max-abs differences on rank 0."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    import triton_flash_attention_b200 as fa
+    import triton_flash_attention_b200.ring as ring
+
+    n, hq, hkv, d = RING_CHECK_N, RING_CHECK_HQ, RING_CHECK_HKV, RING_D
+    scale = d ** -0.5
+    group = dist.group.WORLD if world > 1 else None
+    g = torch.Generator(device=dev).manual_seed(4242)
+    full = [torch.randn(1, h, n, d, device=dev, dtype=torch.float16, generator=g) for h in (hq, hkv, hkv, hq)]
+    q, k, v, do = (ring.zigzag_shard(t, world, rank).contiguous() for t in full)
+    o, lse = ring.ring_forward(q, k, v, causal=True, scale=scale, group=group)
+    dq, dk, dv = ring.ring_backward(q, k, v, o, lse, do, causal=True, scale=scale, group=group)
+
+    def gathered(t):
+        if world == 1:
+            return t
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        return ring.zigzag_unshard(parts)
+
+    got = dict(zip(("o", "dq", "dk", "dv"), (gathered(t) for t in (o, dq, dk, dv))))
+    if rank != 0:
+        return None
+    fq, fk, fv, fdo = full
+    qc, kc, vc = (t.clone().requires_grad_() for t in (fq, fk, fv))
+    o1 = fa.scaled_dot_product_attention(qc, kc, vc, is_causal=True, enable_gqa=True)
+    single = dict(zip(("o", "dq", "dk", "dv"), (o1.detach(),) + torch.autograd.grad(o1, (qc, kc, vc), fdo)))
+    grp = hq // hkv
+    q32 = fq[:, :grp].float().requires_grad_()
+    k32, v32 = (t[:, :1].float().requires_grad_() for t in (fk, fv))
+    o32 = F.scaled_dot_product_attention(q32, k32.expand(1, grp, n, d).contiguous(),
+                                         v32.expand(1, grp, n, d).contiguous(), is_causal=True)
+    ref32 = dict(zip(("o", "dq", "dk", "dv"), (o32.detach(),) + torch.autograd.grad(o32, (q32, k32, v32),
+                                                                                     fdo[:, :grp].float())))
+    heads = {"o": grp, "dq": grp, "dk": 1, "dv": 1}
+    vs_single = {x: round(float((got[x].float() - single[x].float()).abs().max()), 6) for x in got}
+    vs_fp32 = {x: round(float((got[x][:, :heads[x]].float() - ref32[x]).abs().max()), 6) for x in got}
+    single_fp32 = {x: round(float((single[x][:, :heads[x]].float() - ref32[x]).abs().max()), 6) for x in got}
+    ok = all(vs_fp32[x] <= (2e-3 if x == "o" else 1e-2) for x in vs_fp32)
+    return {"config": f"B1 Hq{hq} Hkv{hkv} N{n} D{d} causal, zig-zag over {world} rank(s)",
+            "max_abs_vs_single_gpu": vs_single, "max_abs_vs_fp32_group0": vs_fp32,
+            "single_gpu_max_abs_vs_fp32_group0": single_fp32,
+            "tolerance": {"o": 2e-3, "grads": 1e-2}, "within_tolerance": ok}
+
+
+def ring_timing(args, world: int, rank: int, local: int, dev, ring_seq: int = 0) -> dict:
+    """C5 fwd+bwd (B1 Hq32 Hkv8 N131072 D128, causal) with ring context
+    parallelism over the ranks (strong scaling: the sequence is split
+    zig-zag into 2P chunks); each rank generates its own chunks from
+    per-chunk seeds.  CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import triton_flash_attention_b200 as fa
+    import triton_flash_attention_b200.ring as ring
+
+    n = ring_seq or RING_N
+    c = n // (2 * world)
+
+    def chunked(heads, tag):
+        parts = []
+        for cid in (rank, 2 * world - 1 - rank):
+            g = torch.Generator(device=dev).manual_seed(100003 * tag + cid)
+            parts.append(torch.randn(RING_B, heads, c, RING_D, device=dev, dtype=torch.float16, generator=g))
+        return torch.cat(parts, dim=2)
+
+    q, k, v, do = chunked(RING_HQ, 1), chunked(RING_HKV, 2), chunked(RING_HKV, 3), chunked(RING_HQ, 4)
+    scale = RING_D ** -0.5
+    group = dist.group.WORLD if world > 1 else None
+
+    def step():
+        o, lse = ring.ring_forward(q, k, v, causal=True, scale=scale, group=group)
+        ring.ring_backward(q, k, v, o, lse, do, causal=True, scale=scale, group=group)
+
+    steps = max(2, min(args.ring_steps, args.steps))
+    with ClockSampler(range(world), active=local == 0) as clk:
+        ms_local, _ = timed_loop(step, steps, 1, world)
+    ms = barrier_max(world, ms_local)
+    fl = fa.attention_flops(batch=RING_B, query_heads=RING_HQ, sequence=n, head_dim=RING_D, causal=True,
+                            mode="forward-backward")
+    per_rank = gather_floats(world, [ms_local])
+    return {"workload": f"C5: GQA causal B{RING_B} Hq{RING_HQ} Hkv{RING_HKV} N{n} D{RING_D}, ring context "
+                        f"parallel over {world} GPU(s), zig-zag chunks of {c}",
+            "ms_per_step": round(ms, 3), "value": round(fl / ms / 1e9, 2), "unit": "TFLOP/s", "steps": steps,
+            "scaling": "strong", "per_rank_ms": [round(x[0], 3) for x in per_rank],
+            "parallelism": f"ring-cp x{world} (NCCL P2P)" if world > 1 else "ring-cp x1 (no peer)",
+            "clocks": clk.summary()}
 
 
 # ------------------------------------------------------------------ our arm
@@ -227,6 +506,8 @@ def run_ours(args) -> None:
         dq_acc = torch.empty(B, H, N, D, device=dev, dtype=torch.float32)
         delta_buf = torch.empty(B, H, N, device=dev, dtype=torch.float32)
         dk_buf, dv_buf = torch.empty_like(q), torch.empty_like(q)
+    kv_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(max(args.steps, 1))]
 
     def step(record: bool):
         o, lse = fa.attention_forward(q, k, v, CAUSAL, scale)
@@ -236,8 +517,7 @@ def run_ours(args) -> None:
                                                     dq_acc.data_ptr(), B, H, N, D, _abi.strides3(o),
                                                     _abi.strides3(do), sh), "fa_bwd_preprocess")
             if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
+                e0, e1 = kv_ev[len(ev_kv)]
                 e0.record(stream)
             _abi.check(_abi.lib().fa_bwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
                                                lse.data_ptr(), delta_buf.data_ptr(), dq_acc.data_ptr(),
@@ -255,8 +535,7 @@ def run_ours(args) -> None:
         delta = fa.attention_delta(o, do)
         fa.attention_backward_dq(q, k, v, do, lse, delta, CAUSAL, scale)
         if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
+            e0, e1 = kv_ev[len(ev_kv)]
             e0.record(stream)
         fa.attention_backward_dkdv(q, k, v, do, lse, delta, CAUSAL, scale)
         if record:
@@ -266,30 +545,15 @@ def run_ours(args) -> None:
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize()
-    barrier(world)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        barrier(world)
-        step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)]
-        start.record(stream)
-        for i in range(args.steps):
-            step_ev[i][0].record(stream)
-            step(True)
-            step_ev[i][1].record(stream)
-        end.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-    ms_local = start.elapsed_time(end) / args.steps
+    with ClockSampler(range(world), active=local == 0) as clk:
+        ms_local, per_step = timed_loop(lambda: step(True), args.steps, 0, world, per_step=True)
+
     # per-step distribution, as the reference's benchmark reports it
     # (benchmarks/benchmark_attention.py:153-158): median, p20, p80
-    per_step = sorted(a.elapsed_time(b) for a, b in step_ev)
-
     def pct(p):
         return per_step[min(len(per_step) - 1, int(round(p * (len(per_step) - 1))))]
     ms = barrier_max(world, ms_local)
+    per_rank = gather_floats(world, [ms_local, pct(0.5), per_step[-1]])
     kv_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_kv)
     value = world * fl / (ms * 1e-3) / 1e12
     status = fa._abi.device_status()
@@ -301,23 +565,14 @@ def run_ours(args) -> None:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step(False)
-        for _ in range(args.warmup):
-            graph.replay()
-        torch.cuda.synchronize()
-        barrier(world)
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        gms = barrier_max(world, g0.elapsed_time(g1) / args.steps)
+        gms_local, _ = timed_loop(graph.replay, args.steps, args.warmup, world)
+        gms = barrier_max(world, gms_local)
         graph_info = {"ms_per_step": round(gms, 4), "value": round(world * fl / (gms * 1e-3) / 1e12, 2),
                       "note": "the same step captured in one CUDA graph (torch.cuda.graph) and replayed"}
         del graph
     except Exception as exc:  # reported, not fatal: the eager number above is the metric
         graph_info = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+        barrier(world)
 
     # ---------------- end to end through the public API, host buffers
     # Every step copies its q, k, v, dO from pinned host memory and its O,
@@ -378,6 +633,27 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = barrier_max(world, s2.elapsed_time(e2) / e2e_steps)
     e2e_value = world * fl / (e2e_ms * 1e-3) / 1e12
+    del bufs, outs, hq, hk, hv, hdo
+
+    # ---------------- the same step through other implementations (1 GPU)
+    comp = None
+    if world == 1 and not args.no_comparators:
+        comp = comparators(args, q, k, v, do)
+
+    # ---------------- C5 ring context parallelism: parity and timing
+    ring_info = None
+    if not args.no_ring:
+        del q, k, v, do
+        if fused:
+            del dq_acc, delta_buf, dk_buf, dv_buf
+        torch.cuda.empty_cache()
+        try:
+            ring_info = {"parity": ring_parity(world, rank, dev)}
+            torch.cuda.empty_cache()
+            ring_info.update(ring_timing(args, world, rank, local, dev))
+        except Exception as exc:  # reported, not fatal: the C2 line above is the metric
+            ring_info = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -402,6 +678,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms, 4),
             "step_ms_quantiles": {"p20": round(pct(0.2), 4), "p50": round(pct(0.5), 4), "p80": round(pct(0.8), 4)},
+            "per_rank": {"ms_mean": [round(x[0], 4) for x in per_rank], "ms_p50": [round(x[1], 4) for x in per_rank],
+                         "ms_max_step": [round(x[2], 4) for x in per_rank]},
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
@@ -409,7 +687,9 @@ def run_ours(args) -> None:
             "data": "synthetic: seeded N(0,1) q, k, v, dO (no dataset involved)",
             "config": {"workload": WORKLOAD, "global_batch": B * world, "heads": H, "seq_len": N,
                        "head_dim": D, "causal": CAUSAL, "parallelism": f"batch-shard x{world} (no collective)",
-                       "l2": "per-step working set 256 MiB > 126 MB L2; no flush"},
+                       "l2": "per-step working set 256 MiB > 126 MB L2; no flush",
+                       "timing": "CUDA events on the launching stream; the stream is held by a bounded spin "
+                                 "while the host enqueues the timed steps (not timed)"},
             "pct_of_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
@@ -426,6 +706,13 @@ def run_ours(args) -> None:
             "clocks": clk.summary(),
             "device_status": status,
         }
+        if comp is not None:
+            line["comparators"] = comp
+            for key, name in (("api_ms_per_step", "api"), ("reference_triton_ms", "reference_triton"),
+                              ("torch_sdpa_ms", "torch_sdpa"), ("cudnn_sdpa_ms", "cudnn_sdpa")):
+                line[key] = comp.get(name, {}).get("ms_per_step")
+        if ring_info is not None:
+            line["ring"] = ring_info
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -433,100 +720,40 @@ def run_ours(args) -> None:
 
 
 # ------------------------------------------------------------------ ring workload (C5)
-RING_B, RING_HQ, RING_HKV, RING_N, RING_D = 1, 32, 8, 131072, 128
-
-
 def run_ring(args) -> None:
-    """C5: long-context GQA causal fwd+bwd with ring context parallelism over
-    the ranks (strong scaling: the global sequence is fixed and split zig-zag
-    into 2P chunks).  Each rank generates its own chunks from per-chunk seeds,
-    so no rank materialises the whole sequence."""
+    """C5 alone (``--workload ring``): the ring's parity check and its
+    timing, as the ``ring`` key of the default line reports them."""
     import torch
-    import torch.distributed as dist
-
-    import triton_flash_attention_b200 as fa
-    import triton_flash_attention_b200.ring as ring
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    n = args.ring_seq or RING_N
-    c = n // (2 * world)
-
-    def chunked(heads, tag):
-        parts = []
-        for cid in (rank, 2 * world - 1 - rank):
-            g = torch.Generator(device=dev).manual_seed(100003 * tag + cid)
-            parts.append(torch.randn(RING_B, heads, c, RING_D, device=dev, dtype=torch.float16, generator=g))
-        return torch.cat(parts, dim=2)
-
-    q, k, v, do = chunked(RING_HQ, 1), chunked(RING_HKV, 2), chunked(RING_HKV, 3), chunked(RING_HQ, 4)
-    scale = RING_D ** -0.5
-    group = dist.group.WORLD if world > 1 else None
-
-    def step():
-        o, lse = ring.ring_forward(q, k, v, causal=True, scale=scale, group=group)
-        ring.ring_backward(q, k, v, o, lse, do, causal=True, scale=scale, group=group)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        start.record()
-        for _ in range(args.steps):
-            step()
-        end.record()
-        torch.cuda.synchronize()
-        barrier(world)
-    ms = barrier_max(world, start.elapsed_time(end) / args.steps)
-    fl = fa.attention_flops(batch=RING_B, query_heads=RING_HQ, sequence=n, head_dim=RING_D, causal=True,
-                            mode="forward-backward")
+    info = {"parity": None if args.no_ring_parity else ring_parity(world, rank, dev)}
+    torch.cuda.empty_cache()
+    info.update(ring_timing(args, world, rank, local, dev, ring_seq=args.ring_seq))
     if rank == 0:
-        print(json.dumps({
-            "metric": "causal fp16 fwd+bwd TFLOP/s, ring context parallel (C5)", "value": round(fl / ms / 1e9, 2),
-            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "fp16", "data": "synthetic: seeded N(0,1) per zig-zag chunk",
-            "config": {"workload": "C5: GQA causal B1 Hq32 Hkv8 D128 ring context parallel", "seq_len": n,
-                       "chunk": c, "parallelism": f"ring-cp x{world} (NCCL P2P)"},
-            "clocks": clk.summary()}), flush=True)
+        line = {"metric": "causal fp16 fwd+bwd TFLOP/s, ring context parallel (C5)", "value": info["value"],
+                "unit": "TFLOP/s", "n_gpus": world, "steps": info["steps"], "warmup": 1,
+                "ms_per_step": info["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "fp16", "data": "synthetic: seeded N(0,1) per zig-zag chunk",
+                "config": {"workload": info["workload"], "parallelism": info["parallelism"]},
+                "clocks": info["clocks"], "ring": info}
+        print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
 
 
 # ------------------------------------------------------------------ reference arm
 def run_reference(args) -> None:
+    """The reference's own CPU path (``backend="auto"`` on CPU tensors, which
+    the reference sends to PyTorch's SDPA) on every host core, rank 0 only;
+    each step is forward + backward of one of C2's four batch elements."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
-
-    from oracle import fa2_oracle as orc
-    from triton_flash_attention_b200.flops import attention_flops
-
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max((i.get("num_threads") or 1) for i in threadpool_info()) if threadpool_info() else 1
-    except Exception:
-        cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    heads_per_step = 1
-    q, k, v, do = (rng.standard_normal((N, D)).astype(np.float16) for _ in range(4))
-    for _ in range(args.warmup):
-        orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        for _h in range(heads_per_step):
-            orc.sdpa_head_fwd_bwd_fp32(q, k, v, do, causal=CAUSAL, scale=D ** -0.5)
-        times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
-    fl = attention_flops(batch=1, query_heads=heads_per_step, sequence=N, head_dim=D, causal=CAUSAL,
-                         mode="forward-backward")
-    value = fl / sec / 1e12
+    r = reference_cpu_run(steps=args.steps, warmup=args.warmup)
+    value = r["value"]
     line = {
         "impl": "reference",
         "metric": "causal fp16 fwd+bwd TFLOP/s, B4 H16 N4096 D64; % of B200 FP16 tensor peak",
@@ -535,18 +762,16 @@ def run_reference(args) -> None:
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(sec * 1e3, 3),
+        "ms_per_step": round(r["sec_per_step"] * 1e3, 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "fp16 inputs, fp32 CPU math",
+        "dtype": "fp16",
         "data": "synthetic: seeded N(0,1) q, k, v, dO",
         "config": {"workload": WORKLOAD, "global_batch": B, "heads": H, "seq_len": N, "head_dim": D,
                    "causal": CAUSAL, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": int(cores), "kind": "port",
-                         "sample": f"each step = fwd+bwd of {heads_per_step} of the {B * H} (batch, head) "
-                                   "pairs of C2 (the reference's CPU path: PyTorch SDPA math, restated in "
-                                   "float32 numpy/BLAS)"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": r["cores"], "kind": r["kind"],
+                         "sample": r["sample"]},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -888,6 +1113,11 @@ def main() -> None:
                          "decode: one query per sequence over a paged K/V cache; "
                          "masked: boolean attn_mask forms and dropout at the C2 shape")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
+    ap.add_argument("--ring-steps", type=int, default=3, help="timed C5 steps (the ring key / ring workload)")
+    ap.add_argument("--no-ring", action="store_true", help="skip the C5 ring key of the default line")
+    ap.add_argument("--no-ring-parity", action="store_true", help="ring workload: skip the parity check")
+    ap.add_argument("--no-comparators", action="store_true",
+                    help="skip the reference-kernel / PyTorch SDPA / public-API keys of the default line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
