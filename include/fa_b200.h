@@ -124,9 +124,11 @@ FA_API int fa_bwd_preprocess(const void* o, const void* dO, float* delta, float*
                       const int64_t* o_strides, const int64_t* do_strides,
                       void* stream);
 
-/* Fused backward, step 2 of 3 (D = 32 or 64): dK, dV as fa_bwd_dkdv
+/* Fused backward, step 2 of 3 (D = 32, 64 or 128): dK, dV as fa_bwd_dkdv
  * and, in the same pass over the (key tile, query tile) pairs, dQ added into
- * dq_accum, the caller's contiguous (B, Hq, Nq, D) fp32 buffer.  Replaces the
+ * dq_accum, the caller's contiguous (B, Hq, Nq, D) fp32 buffer (with
+ * position offsets, the ring's fp32 dQ accumulator of a chunk: the partials
+ * add to what it holds).  Replaces the
  * whole _attn_bwd launch (attention.py:746-783, kernel :383-573), which
  * rebuilds P and dS once for dK/dV and once for dQ; here they are built once.
  * dQ is summed with fp32 reduce-adds whose order follows the schedule, so it

@@ -73,14 +73,16 @@ def test_rejects_misaligned_output_and_nonfinite_scale():
 
 
 def test_fused_backward_validation_without_cuda():
-    """The fused backward serves D = 32 and 64 only and wants a 16-byte
-    aligned fp32 dQ accumulator; both are refused before any CUDA call."""
+    """The fused backward serves D = 32, 64 and 128 and wants a 16-byte
+    aligned fp32 dQ accumulator; other head dims and a misaligned
+    accumulator are refused before any CUDA call."""
     s = _strides()
     lib = _abi.lib()
     for name in ("fa_bwd_fused", "fa_bwd_fused_bf16"):
-        rc = getattr(lib, name)(16, 16, 16, 16, 16, 16, 16, 16, 16, 1, 1, 1, 8, 8, 128, s, s, s, s, s, s,
-                                0.1, 1, 0, 0, 0, None)
-        assert rc == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
+        for d in (48, 96, 256):
+            rc = getattr(lib, name)(16, 16, 16, 16, 16, 16, 16, 16, 16, 1, 1, 1, 8, 8, d, s, s, s, s, s, s,
+                                    0.1, 1, 0, 0, 0, None)
+            assert rc == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM, d
     assert lib.fa_bwd_preprocess(16, 16, 16, 18, 1, 1, 8, 64, s, s, None) == _abi.FA_ERR_MISALIGNED
     assert lib.fa_bwd_dq_convert(18, 16, 1, 1, 8, 64, s, None) == _abi.FA_ERR_MISALIGNED
     assert lib.fa_bwd_dq_convert(16, 16, 1, 1, 8, 48, s, None) == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM

@@ -1,6 +1,6 @@
 """The fused backward (one pass over the key tiles yields dQ, dK and dV;
-D = 32, 64) against the separate dQ and dK/dV kernels and the float64
-oracle (GPU only).
+D = 32, 64 and, with its own kernel, 128) against the separate dQ and dK/dV
+kernels and the float64 oracle (GPU only).
 
 dK and dV follow the dK/dV kernel's MMA accumulation order, but the two
 kernels split the exponentials differently between MUFU and the FMA-pipe
@@ -63,10 +63,19 @@ CASES = [
     (1, 2, 2, 333, 100, 64, True),
     (1, 4, 4, 2048, 2048, 64, True),
 ]
+# D = 128 (fa_bwd_fused128.cu: 64-query items, dQ^T = K^T dS^T)
+CASES_128 = [
+    (1, 2, 2, 65, 65, 128, True),
+    (2, 4, 2, 300, 300, 128, True),
+    (1, 4, 4, 257, 257, 128, False),
+    (2, 2, 1, 100, 333, 128, True),
+    (1, 2, 2, 333, 100, 128, False),
+    (1, 8, 2, 1000, 1000, 128, True),
+]
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", CASES + CASES_128)
 def test_fused_matches_separate_kernels(case, dtype):
     b, hq, hkv, nq, nk, d, causal = case
     q, k, v, do = _inputs(b, hq, hkv, nq, nk, d, seed=nq + 3 * nk + d, dtype=dtype)
@@ -82,7 +91,7 @@ def test_fused_matches_separate_kernels(case, dtype):
         assert e_fused <= 1.25 * e_sep + (5e-4 if dtype == torch.float16 else 4e-3), (e_fused, e_sep)
 
 
-@pytest.mark.parametrize("case", CASES[:6])
+@pytest.mark.parametrize("case", CASES[:6] + CASES_128[:5])
 def test_fused_against_float64(case):
     b, hq, hkv, nq, nk, d, causal = case
     q, k, v, do = _inputs(b, hq, hkv, nq, nk, d, seed=7 * nq + nk)
@@ -97,11 +106,10 @@ def test_fused_against_float64(case):
 
 
 def test_api_takes_fused_path_unless_deterministic():
-    assert fa.fused_backward_enabled(64) and fa.fused_backward_enabled(32)
-    assert not fa.fused_backward_enabled(128)
+    assert fa.fused_backward_enabled(64) and fa.fused_backward_enabled(32) and fa.fused_backward_enabled(128)
     torch.use_deterministic_algorithms(True)
     try:
-        assert not fa.fused_backward_enabled(64)
+        assert not fa.fused_backward_enabled(64) and not fa.fused_backward_enabled(128)
     finally:
         torch.use_deterministic_algorithms(False)
 
@@ -129,3 +137,25 @@ def test_full_size_c2_against_separate_kernels():
         rel = float(torch.linalg.vector_norm(a.float() - ref_t.float()) / torch.linalg.vector_norm(ref_t.float()))
         assert rel <= 2e-3, (name, rel)
     assert fa._abi.device_status() == 0
+
+
+def test_full_size_c4_against_separate_kernels():
+    """The GQA benchmark shape at D = 128 (C4: N 8191, causal; 8 of its 32
+    query heads, 2 K/V heads): fused vs separate."""
+    q, k, v, do = _inputs(1, 8, 2, 8191, 8191, 128, seed=4)
+    (fdq, fdk, fdv), (dq, dk, dv) = _both(q, k, v, do, True)
+    for name, a, ref_t in (("dq", fdq, dq), ("dk", fdk, dk), ("dv", fdv, dv)):
+        diff = (a.float() - ref_t.float()).abs()
+        assert bool((diff <= 5e-3 + 2e-2 * ref_t.float().abs()).all()), (name, float(diff.max()))
+        rel = float(torch.linalg.vector_norm(a.float() - ref_t.float()) / torch.linalg.vector_norm(ref_t.float()))
+        assert rel <= 2e-3, (name, rel)
+    assert fa._abi.device_status() == 0
+
+
+def test_fused128_dk_dv_equal_separate_kernel():
+    """At D = 128 the fused pass builds P and dS exactly as the dK/dV kernel
+    does (same exponentials, same 64-query items in the same order), so its
+    dK and dV are bitwise the dK/dV kernel's."""
+    q, k, v, do = _inputs(2, 4, 2, 500, 500, 128, seed=21)
+    (_, fdk, fdv), (_, dk, dv) = _both(q, k, v, do, True)
+    assert torch.equal(fdk, dk) and torch.equal(fdv, dv)

@@ -56,6 +56,15 @@ def test_block_decomposition_matches_full(causal, d, hq, hkv):
                      dv_acc[:, :, sl], 0, j * c)
     for acc, full in ((dq_acc, dq_full), (dk_acc, dk_full), (dv_acc, dv_full)):
         assert float((acc - full.float()).abs().max()) <= 1e-2
+    # the fused block op (one pass per block: dQ reduce-added, dK/dV added)
+    dq_acc.zero_(), dk_acc.zero_(), dv_acc.zero_()
+    for j in range(n // c):
+        sl = slice(j * c, (j + 1) * c)
+        ops.bwd_fused(q, k[:, :, sl], v[:, :, sl], do, lse_full, delta, causal, scale, dq_acc, dk_acc[:, :, sl],
+                      dv_acc[:, :, sl], 0, j * c)
+    for acc, full in ((dq_acc, dq_full), (dk_acc, dk_full), (dv_acc, dv_full)):
+        assert float((acc - full.float()).abs().max()) <= 1e-2
+    assert fa._abi.device_status() == 0
 
 
 def test_single_rank_ring_equals_kernel():

@@ -214,7 +214,7 @@ WINDOW_CASES = [
 @pytest.mark.parametrize("case", WINDOW_CASES)
 def test_varlen_sliding_window_against_float64(case):
     """Causal sliding window: forward (O, lse2) and both backward paths
-    (fused at D <= 64 and the deterministic split) against float64."""
+    (fused and the deterministic split) against float64."""
     lens, hq, hkv, d, window = case
     cu = _cu(lens)
     q, k, v, do = _inputs(lens, lens, hq, hkv, d, seed=window + d)

@@ -247,14 +247,14 @@ def attention_backward_dkdv(q, k, v, do, lse, delta, causal: bool, softmax_scale
     return dk, dv
 
 
-FUSED_BWD_HEAD_DIMS = (32, 64)
+FUSED_BWD_HEAD_DIMS = (32, 64, 128)
 # dropout rates are applied in steps of 1/256 (include/fa_b200.h, fa_fwd_dropout)
 DROPOUT_STEP = 1.0 / 256
 
 
 def fused_backward_enabled(head_dim: int) -> bool:
-    """Whether the backward runs as one fused dK/dV + dQ pass: head dims 32
-    and 64, unless ``torch.use_deterministic_algorithms(True)`` asks for
+    """Whether the backward runs as one fused dK/dV + dQ pass: every head
+    dim (32, 64, 128), unless ``torch.use_deterministic_algorithms(True)`` asks for
     bitwise-reproducible gradients (the fused pass sums dQ with fp32
     reduce-adds in schedule order; the separate dQ kernel does not)."""
     return head_dim in FUSED_BWD_HEAD_DIMS and not torch.are_deterministic_algorithms_enabled()

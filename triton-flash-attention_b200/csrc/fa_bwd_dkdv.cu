@@ -27,6 +27,7 @@
 //       dV at [256, 256+D), dK at [256+D, 256+2D).
 #include "fa_common.cuh"
 #include "fa_kernels.h"
+#include "fa_key_tiles.cuh"
 
 namespace fa {
 
@@ -70,67 +71,14 @@ struct Cfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-// A work tile: 128 keys of one (batch, kv head) and the 64-row query items
-// (query head of the group x query tile) that see them.
-struct Tile {
-  int kv0, b, kvh, i_start, per_head, n_items;
-  Seq sq;
-};
+// Work tiles of BM keys and their BQ-row query items (fa_key_tiles.cuh).
+using Tile = KeyTile;
 template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
-  const int BHkv = shp.B * shp.Hkv;
-  const int kv_tile = t / BHkv;
-  const int bhk = t % BHkv;
-  Tile w;
-  w.b = bhk / shp.Hkv;
-  w.kvh = bhk % shp.Hkv;
-  w.kv0 = kv_tile * BM;
-  w.sq = seq_of_v<VL>(shp, w.b);
-  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
-  int i_start = 0;
-  if (shp.causal) {
-    // first query tile holding a row at or after this tile's first key
-    const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
-    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
-    if (i_start > n_qt) i_start = n_qt;
-  }
-  int n_qt_w = n_qt;
-  if (VL && shp.causal && shp.window > 0) {  // windows come with the packed layout only
-    // sliding window: the last query that sees this tile's last key
-    const long long last_row = (long long)w.kv0 + BM - 1 + shp.window - 1 + shp.k_off - shp.q_off;
-    const long long i_end = last_row < 0 ? 0 : last_row / BQ + 1;
-    if (i_end < n_qt_w) n_qt_w = int(i_end);
-  }
-  w.i_start = i_start;
-  w.per_head = n_qt_w > i_start ? n_qt_w - i_start : 0;
-  w.n_items = w.per_head * (shp.Hq / shp.Hkv);
-  return w;
+  return key_tile_of<VL, BM, BQ>(shp, t);
 }
-
-// Walks the items of a CTA's non-empty tiles in issue order.
 template <bool VL>
-struct ItemCursor {
-  int k, it, pad;
-  Tile w;
-  // the first item of the first non-empty tile at snake position >= k
-  __device__ __forceinline__ bool seek(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
-    for (;; ++k) {
-      const int t = snake_unit(cta, k, n_cta, n_tiles);
-      if (t >= n_tiles) return false;
-      w = tile_of<VL>(shp, t);
-      if (w.n_items > 0) {
-        it = 0;
-        return true;
-      }
-    }
-  }
-  __device__ __forceinline__ bool next(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
-    if (++it < w.n_items) return true;
-    ++k;
-    return seek(shp, cta, n_cta, n_tiles);
-  }
-};
-
+using ItemCursor = KeyItemCursor<VL, BM, BQ>;
 }  // namespace bkv
 
 template <int D, int DT, bool VL, bool BITS, bool DROP>
@@ -225,7 +173,7 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
       // that see no key, get lse2 = +inf so that their P is 0.
       constexpr int PF = 2;
       float lv[PF + 1][2], dvv[PF + 1][2];
-      ItemCursor<VL> ahead{0, 0, 0, {}};
+      ItemCursor<VL> ahead{0, 0, {}};
       bool ahead_ok = is_q && ahead.seek(shp, cta, n_cta, n_tiles);
       auto fetch = [&](float (&l)[2], float (&d)[2]) {
 #pragma unroll
@@ -636,41 +584,14 @@ struct Cfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-// A work tile: 128 keys of one (batch, kv head) and the query items (query
-// head of the group x 128-row query tile) that see them.
-struct Tile {
-  int kv0, b, kvh, i_start, per_head, n_items;
-  Seq sq;
-};
+// Work tiles of BM keys and their BQ-row query items (fa_key_tiles.cuh).
+using Tile = KeyTile;
 template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
-  const int BHkv = shp.B * shp.Hkv;
-  const int kv_tile = t / BHkv;
-  const int bhk = t % BHkv;
-  Tile w;
-  w.b = bhk / shp.Hkv;
-  w.kvh = bhk % shp.Hkv;
-  w.kv0 = kv_tile * BM;
-  w.sq = seq_of_v<VL>(shp, w.b);
-  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
-  int i_start = 0;
-  if (shp.causal) {
-    const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
-    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
-    if (i_start > n_qt) i_start = n_qt;
-  }
-  int n_qt_w = n_qt;
-  if (VL && shp.causal && shp.window > 0) {  // windows come with the packed layout only
-    // sliding window: the last query that sees this tile's last key
-    const long long last_row = (long long)w.kv0 + BM - 1 + shp.window - 1 + shp.k_off - shp.q_off;
-    const long long i_end = last_row < 0 ? 0 : last_row / BQ + 1;
-    if (i_end < n_qt_w) n_qt_w = int(i_end);
-  }
-  w.i_start = i_start;
-  w.per_head = n_qt_w > i_start ? n_qt_w - i_start : 0;
-  w.n_items = w.per_head * (shp.Hq / shp.Hkv);
-  return w;
+  return key_tile_of<VL, BM, BQ>(shp, t);
 }
+template <bool VL>
+using ItemCursor = KeyItemCursor<VL, BM, BQ>;
 }  // namespace bkvw
 
 template <int D, int DT, bool VL, bool BITS>

@@ -36,6 +36,7 @@
 //   into [256,288) and [320,352); dV at [384,384+D), dK at [384+D,384+2D).
 #include "fa_common.cuh"
 #include "fa_kernels.h"
+#include "fa_key_tiles.cuh"
 
 namespace fa {
 
@@ -43,8 +44,14 @@ namespace bfz {
 constexpr int BM = 128;  // keys per tile
 constexpr int BQ = 128;  // query rows per item
 constexpr int NUM_THREADS = 512;
-constexpr int POLY_MASK = 0;  // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2 (none: measured fastest)
-constexpr int POLY_MASK_D32 = 2;  // the same at D = 32 (measured)
+#ifndef FA_FUSED_POLY_MASK
+#define FA_FUSED_POLY_MASK 0
+#endif
+#ifndef FA_FUSED_POLY_MASK_D32
+#define FA_FUSED_POLY_MASK_D32 2
+#endif
+constexpr int POLY_MASK = FA_FUSED_POLY_MASK;  // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2 (none: measured fastest)
+constexpr int POLY_MASK_D32 = FA_FUSED_POLY_MASK_D32;  // the same at D = 32 (measured)
 template <int D>
 constexpr int poly_mask() { return D == 32 ? POLY_MASK_D32 : POLY_MASK; }
 // Registers per thread: launched at 128 (512 threads); warps 0-3 drop to
@@ -91,66 +98,14 @@ struct Cfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-// A work tile: 128 keys of one (batch, kv head) and the query items (query
-// head of the group x 128-row query tile) that see them.
-struct Tile {
-  int kv0, b, kvh, i_start, per_head, n_items;
-  Seq sq;
-};
+// Work tiles of BM keys and their BQ-row query items (fa_key_tiles.cuh).
+using Tile = KeyTile;
 template <bool VL>
 __device__ __forceinline__ Tile tile_of(const AttnShape& shp, int t) {
-  const int BHkv = shp.B * shp.Hkv;
-  const int kv_tile = t / BHkv;
-  const int bhk = t % BHkv;
-  Tile w;
-  w.b = bhk / shp.Hkv;
-  w.kvh = bhk % shp.Hkv;
-  w.kv0 = kv_tile * BM;
-  w.sq = seq_of_v<VL>(shp, w.b);
-  const int n_qt = w.kv0 < w.sq.nk ? (w.sq.nq + BQ - 1) / BQ : 0;
-  int i_start = 0;
-  if (shp.causal) {
-    // first query tile holding a row at or after this tile's first key
-    const long long first_row = (long long)w.kv0 + shp.k_off - shp.q_off;
-    i_start = first_row <= 0 ? 0 : int(first_row / BQ);
-    if (i_start > n_qt) i_start = n_qt;
-  }
-  int n_qt_w = n_qt;
-  if (VL && shp.causal && shp.window > 0) {  // windows come with the packed layout only
-    // sliding window: the last query that sees this tile's last key
-    const long long last_row = (long long)w.kv0 + BM - 1 + shp.window - 1 + shp.k_off - shp.q_off;
-    const long long i_end = last_row < 0 ? 0 : last_row / BQ + 1;
-    if (i_end < n_qt_w) n_qt_w = int(i_end);
-  }
-  w.i_start = i_start;
-  w.per_head = n_qt_w > i_start ? n_qt_w - i_start : 0;
-  w.n_items = w.per_head * (shp.Hq / shp.Hkv);
-  return w;
+  return key_tile_of<VL, BM, BQ>(shp, t);
 }
-
-// Walks the items of a CTA's non-empty tiles in issue order.
 template <bool VL>
-struct ItemCursor {
-  int k, it;
-  Tile w;
-  // the first item of the first non-empty tile at snake position >= k
-  __device__ __forceinline__ bool seek(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
-    for (;; ++k) {
-      const int t = snake_unit(cta, k, n_cta, n_tiles);
-      if (t >= n_tiles) return false;
-      w = tile_of<VL>(shp, t);
-      if (w.n_items > 0) {
-        it = 0;
-        return true;
-      }
-    }
-  }
-  __device__ __forceinline__ bool next(const AttnShape& shp, int cta, int n_cta, int n_tiles) {
-    if (++it < w.n_items) return true;
-    ++k;
-    return seek(shp, cta, n_cta, n_tiles);
-  }
-};
+using ItemCursor = KeyItemCursor<VL, BM, BQ>;
 }  // namespace bfz
 
 template <int D, int DT, bool VL, bool BITS>
@@ -748,6 +703,8 @@ int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D) {
       return a.dtype == DT_BF16 ? launch_bwd_fused_l<32, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<32, DT_F16>(a, tmap_dq);
     case 64:
       return a.dtype == DT_BF16 ? launch_bwd_fused_l<64, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<64, DT_F16>(a, tmap_dq);
+    case 128:
+      return launch_bwd_fused128(a, tmap_dq);
     default:
       return FA_ERR_UNSUPPORTED_HEAD_DIM;
   }

@@ -184,18 +184,21 @@ int preprocess_impl(const void* o, const void* dO, float* delta, float* dq_accum
                           do_strides[2], delta, dq_accum, B, H, N, D, dtype, static_cast<cudaStream_t>(stream));
 }
 
-// 4-D fp32 tensor map over the contiguous (B, H, N, D) dQ accumulator: box
-// {32, 128, 1, 1} with the 128-byte swizzle the fused kernel stages with.
+// 4-D fp32 tensor map over the contiguous (B, H, N, D) dQ accumulator, with
+// the box and layout the fused kernel stages its partials in: at D <= 64
+// {32, 128, 1, 1} with the 128-byte swizzle, at D = 128 one warp's
+// {32, 64, 1, 1} piece without swizzle.
 int make_acc_map(CUtensorMap* map, float* ptr, int B, int H, int N, int D) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DRIVER;
   if (!aligned16(ptr)) return FA_ERR_MISALIGNED;
   cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(B)};
   cuuint64_t gstr[3] = {cuuint64_t(D) * 4, cuuint64_t(N) * D * 4, cuuint64_t(H) * N * D * 4};
-  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t box[4] = {32, cuuint32_t(fused_item_rows(D)), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   D <= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TENSOR_MAP;
 }
 
@@ -285,7 +288,6 @@ int fused_impl(const void* q, const void* k, const void* v, const void* dO, cons
                int causal, int q_offset, int k_offset, int accumulate_fp32, void* stream, int dtype) {
   int rc = check_shape(B, Hq, Hkv, Nq, Nk, D);
   if (rc) return rc;
-  if (D > 64) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (!q || !k || !v || !dO || !lse || !delta || !dq_accum || !dk || !dv) return FA_ERR_BAD_SHAPE;
   if (!q_strides || !k_strides || !v_strides || !do_strides || !dk_strides || !dv_strides) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
@@ -293,7 +295,7 @@ int fused_impl(const void* q, const void* k, const void* v, const void* dO, cons
   if (!out_strides_ok(dk, dk_strides, eb) || !out_strides_ok(dv, dv_strides, eb)) return FA_ERR_MISALIGNED;
   BwdArgs a;
   a.dtype = dtype;
-  const int bq = dkdv_cfg::BQ_WIDE;
+  const int bq = fused_item_rows(D);
   if ((rc = make_map(&a.tmap_q, q, B, Hq, Nq, D, q_strides, bq, dtype))) return rc;
   if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq, dtype))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM, dtype))) return rc;
@@ -401,7 +403,7 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
   if (window < 0 || (window > 0 && !causal)) return FA_ERR_BAD_SHAPE;
   if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv || !delta) return FA_ERR_BAD_SHAPE;
   if (!std::isfinite(softmax_scale)) return FA_ERR_BAD_SHAPE;
-  const bool fused = D <= 64 && !deterministic;
+  const bool fused = !deterministic;
   if (fused && !dq_accum) return FA_ERR_BAD_SHAPE;
   const PackedStrides sq(total_q, Hq, D), sk(total_k, Hkv, D);
   if (!out_strides_ok(o, sq.v, 2) || !out_strides_ok(dO, sq.v, 2) || !out_strides_ok(dq, sq.v, 2) ||
@@ -427,8 +429,8 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
   a.accumulate_fp32 = 0;
   a.stream = st;
   if (fused) {
-    if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dkdv_cfg::BQ_WIDE, dtype))) return rc;
-    if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, dkdv_cfg::BQ_WIDE, dtype))) return rc;
+    if ((rc = make_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, fused_item_rows(D), dtype))) return rc;
+    if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, fused_item_rows(D), dtype))) return rc;
     if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
     if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
     CUtensorMap tmap_dq;

@@ -46,8 +46,14 @@ constexpr int QT = 2;    // query tiles per work unit
 constexpr int NUM_THREADS = 384;
 constexpr bool TURNS = true;  // separate-P layout: the softmax warpgroups take turns at their exponentials
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P may reach 2^8 before O is rescaled
-constexpr int POLY_MASK = 0;               // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
-constexpr int POLY_MASK_D32 = 2;           // the same at D = 32 (half the MMA work per exponential; measured)
+#ifndef FA_FWD_POLY_MASK
+#define FA_FWD_POLY_MASK 0
+#endif
+#ifndef FA_FWD_POLY_MASK_D32
+#define FA_FWD_POLY_MASK_D32 2
+#endif
+constexpr int POLY_MASK = FA_FWD_POLY_MASK;          // pairs (i & 7) < POLY_MASK use the FMA-pipe exp2
+constexpr int POLY_MASK_D32 = FA_FWD_POLY_MASK_D32;  // the same at D = 32 (half the MMA work per exponential; measured)
 template <int D>
 constexpr int poly_mask() { return D == 32 ? POLY_MASK_D32 : POLY_MASK; }
 // Registers per thread: launched at 168 (384 threads); the control

@@ -71,8 +71,10 @@ int launch_bwd_dkdv(const BwdArgs& a, int D);
 int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_sn, const void* dO,
                      long long do_sb, long long do_sh, long long do_sn, float* delta, float* zero_acc, int B, int H,
                      int N, int D, int dtype, cudaStream_t stream);
-// Fused dK/dV + dQ backward (D <= 64); tmap_dq maps the fp32 accumulator.
+// Fused dK/dV + dQ backward (every D; D = 128 runs fa_bwd_fused128.cu, with
+// no boolean mask or dropout); tmap_dq maps the fp32 accumulator.
 int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D);
+int launch_bwd_fused128(const BwdArgs& a, const CUtensorMap& tmap_dq);
 // acc_w: the accumulator's row width (0: D); dq receives its first D columns.
 int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, long long sn, int B, int H, int N, int D,
                       int dtype, cudaStream_t stream, int acc_w = 0);
@@ -94,5 +96,7 @@ constexpr int BM = 128;  // key rows per tile (the MMA M dimension)
 constexpr int BQ = 64;   // query rows per tile (D = 128)
 constexpr int BQ_WIDE = 128;  // query rows per item (D <= 64)
 }  // namespace dkdv_cfg
+// Query rows per item of the fused backward (its Q / dO tensor-map boxes).
+constexpr int fused_item_rows(int D) { return D <= 64 ? dkdv_cfg::BQ_WIDE : dkdv_cfg::BQ; }
 
 }  // namespace fa

@@ -18,8 +18,9 @@ base-2 log-sum-exp (``fa_merge_partial``).
 
 Backward: the same ring in the same direction.  dQ accumulates locally in
 fp32; each K/V block travels with fp32 dK/dV accumulators that every rank adds
-its contribution to (``fa_bwd_dq`` / ``fa_bwd_dkdv`` with ``accumulate_fp32``),
-using the merged global LSE and Delta = rowsum(dO * O).  After P steps each
+its contribution to (one ``fa_bwd_fused`` pass per chunk pair with
+``accumulate_fp32``, or under deterministic algorithms ``fa_bwd_dq`` and
+``fa_bwd_dkdv``), using the merged global LSE and Delta = rowsum(dO * O).  After P steps each
 accumulator is one hop away from its owner and is sent home.
 
 The block-level operations are injectable (``BlockOps``) so the ring schedule
@@ -91,6 +92,8 @@ class BlockOps:
     delta(o, do) -> delta
     bwd_dq(q, k, v, do, lse, delta, causal, scale, dq_acc, q_off, k_off)      (in place)
     bwd_dkdv(q, k, v, do, lse, delta, causal, scale, dk_acc, dv_acc, q_off, k_off)  (in place)
+    bwd_fused(q, k, v, do, lse, delta, causal, scale, dq_acc, dk_acc, dv_acc, q_off, k_off)
+        (optional, in place: both of the above in one pass)
     """
 
     fwd: Callable
@@ -98,6 +101,7 @@ class BlockOps:
     delta: Callable
     bwd_dq: Callable
     bwd_dkdv: Callable
+    bwd_fused: Callable | None = None
 
 
 def cuda_block_ops() -> BlockOps:
@@ -124,7 +128,21 @@ def cuda_block_ops() -> BlockOps:
         attention_backward_dkdv(q, k, v, do, lse, delta, causal, scale, dk=dk_acc, dv=dv_acc,
                                 q_offset=q_off, k_offset=k_off)
 
-    return BlockOps(fwd=fwd, merge=merge, delta=attention_delta, bwd_dq=bwd_dq, bwd_dkdv=bwd_dkdv)
+    def bwd_fused(q, k, v, do, lse, delta, causal, scale, dq_acc, dk_acc, dv_acc, q_off, k_off):
+        # one pass: dQ reduce-added into the chunk's fp32 accumulator, dK/dV
+        # added into the travelling fp32 accumulators (fa_bwd_fused)
+        b, hq, nq, d = q.shape
+        hkv, nk = k.shape[1], k.shape[2]
+        rc = _abi.entry("fa_bwd_fused", q.dtype)(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+            dq_acc.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(), b, hq, hkv, nq, nk, d,
+            _abi.strides3(q), _abi.strides3(k), _abi.strides3(v), _abi.strides3(do), _abi.strides3(dk_acc),
+            _abi.strides3(dv_acc), float(scale), 1 if causal else 0, int(q_off), int(k_off), 1,
+            torch.cuda.current_stream(q.device).cuda_stream)
+        _abi.check(rc, "fa_bwd_fused")
+
+    return BlockOps(fwd=fwd, merge=merge, delta=attention_delta, bwd_dq=bwd_dq, bwd_dkdv=bwd_dkdv,
+                    bwd_fused=bwd_fused)
 
 
 # --------------------------------------------------------------------------- P2P
@@ -204,6 +222,9 @@ def ring_backward(q, k, v, o, lse, do, *, causal: bool, scale: float, group=None
     q_c = [_chunk(q, i, c) for i in range(2)]
     do_c = [_chunk(do, i, c) for i in range(2)]
     k_cur, v_cur = k.contiguous(), v.contiguous()
+    # one fused pass per chunk pair (dQ, dK, dV from one visit), unless
+    # deterministic algorithms ask for the bitwise-reproducible split kernels
+    fused = ops.bwd_fused is not None and not torch.are_deterministic_algorithms_enabled()
     dk_cur = torch.zeros(k_cur.shape, device=k.device, dtype=acc)
     dv_cur = torch.zeros(v_cur.shape, device=v.device, dtype=acc)
     for step in range(world):
@@ -214,9 +235,13 @@ def ring_backward(q, k, v, o, lse, do, *, causal: bool, scale: float, group=None
             nxt_kv, works = _exchange((k_cur, v_cur), group, world, rank)
         for i, j, diag in visible_pairs(world, rank, src, causal):
             kj, vj = _chunk(k_cur, j, c), _chunk(v_cur, j, c)
-            ops.bwd_dq(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dq_acc[i], qa[i] * c, kb[j] * c)
             dk_j = _chunk(dk_cur, j, c)
             dv_j = _chunk(dv_cur, j, c)
+            if fused:
+                ops.bwd_fused(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dq_acc[i], dk_j, dv_j,
+                              qa[i] * c, kb[j] * c)
+                continue
+            ops.bwd_dq(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dq_acc[i], qa[i] * c, kb[j] * c)
             ops.bwd_dkdv(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dk_j, dv_j,
                          qa[i] * c, kb[j] * c)
         # this block's gradient accumulators move on with it (the last hop

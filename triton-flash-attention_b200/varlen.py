@@ -101,7 +101,7 @@ def varlen_attention_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: 
 
 def varlen_attention_backward(q, k, v, o, do, lse, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
                               max_seqlen_k: int, causal: bool, softmax_scale: float, window: int = 0):
-    """dQ, dK, dV over packed sequences.  Head dims 32 and 64 run the fused
+    """dQ, dK, dV over packed sequences.  Every head dim runs the fused
     pass (fp32 dQ accumulator in caller scratch) unless
     ``torch.use_deterministic_algorithms(True)`` asks for the separate,
     bitwise-reproducible dQ and dK/dV kernels."""
