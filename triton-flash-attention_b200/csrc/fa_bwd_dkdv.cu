@@ -424,8 +424,10 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
           const float4 nl = l4[c4];
           const float4 nd = d4[c4];
           const int c = c4 * 4;
-          const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
-          const uint32_t p23 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
+          const uint64_t e01 = exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y)));
+          const uint64_t e23 = exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w)));
+          const uint32_t p01 = pack2_f2<DT>(e01);
+          const uint32_t p23 = pack2_f2<DT>(e23);
           if constexpr (DROP) {
             // the words of query pairs (c, c+1) and (c+2, c+3) for this key row pair
             const int kb = rl & 1;  // kv0 is even
@@ -444,12 +446,11 @@ __global__ void __launch_bounds__(bkv::NUM_THREADS, 1)
             pk_ds[c4 * 2] = mul2<DT>(p01, (k01 & m01) | (n01 & ~m01));
             pk_ds[c4 * 2 + 1] = mul2<DT>(p23, (k23 & m23) | (n23 & ~m23));
           } else {
-            const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-            const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
+            // dS = P (dP - Delta) in fp32, rounded once (attention.py:300-305)
             pk_p[c4 * 2] = p01;
             pk_p[c4 * 2 + 1] = p23;
-            pk_ds[c4 * 2] = mul2<DT>(p01, d01);
-            pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+            pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(e01, fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y))));
+            pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(e23, fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w))));
           }
         }
         tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
@@ -982,10 +983,12 @@ __global__ void __launch_bounds__(bkvw::NUM_THREADS, 1)
             for (int c4 = 0; c4 < 16; ++c4) {
               const float4 nd = d4[c4];
               const int c = c4 * 4;
-              const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-              const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-              pk_ds[c4 * 2] = mul2<DT>(__float_as_uint(pf[c4 * 2]), d01);
-              pk_ds[c4 * 2 + 1] = mul2<DT>(__float_as_uint(pf[c4 * 2 + 1]), d23);
+              // dS = P (dP - Delta) with P widened exactly from its packed
+              // form, the product in fp32, rounded once
+              const uint64_t d01 = fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y));
+              const uint64_t d23 = fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w));
+              pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(widen2<DT>(__float_as_uint(pf[c4 * 2])), d01));
+              pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(widen2<DT>(__float_as_uint(pf[c4 * 2 + 1])), d23));
             }
             tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
             tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));

@@ -367,18 +367,23 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           const uint32_t words[2] = {mw.x, mw.y};
           if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<64>(sv, words);
         }
-        uint32_t pk_p[32];
+        // P in fp32, kept in place of the scores: dS = P (dP - Delta) is
+        // formed in fp32 and rounded once, as the reference's
+        // ds = p * (dp - Di) before .to(float16) (attention.py:343-347)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const uint64_t x = ffma2(f2pack(sv[2 * i], sv[2 * i + 1]), c2x2, nlse2);
-          pk_p[i] = pack2_f2<DT>((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x));
+          f2unpack((i & 7) < POLY_MASK ? exp2_poly2(x) : exp2_mufu2(x), sv[2 * i], sv[2 * i + 1]);
         }
         if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 152 + w)) { ok = false; break; }
         tc_fence_after();
-        float dp[64];
-        tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
         uint32_t pk_ds[32];
         if constexpr (DROP) {
+          uint32_t pk_p[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk_p[i] = pack2<DT>(sv[2 * i], sv[2 * i + 1]);
+          float dp[64];
+          tmem_ld64(lane_base + uint32_t(C::DP_COL + 64 * w), dp);
           const uint32_t k2 = drop_key2(drop_kbh, r, key0);
           const uint32_t sel = drop_b0 ? keep_sel(2, 3) : keep_sel(0, 1);
           const uint32_t tt = (256u - dr.t) * 0x10001u;
@@ -396,8 +401,16 @@ __global__ void __launch_bounds__(bdqw::NUM_THREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            pk_ds[i] = mul2<DT>(pk_p[i], pack2_f2<DT>(fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+          for (int hd = 0; hd < 2; ++hd) {
+            float dp[32];
+            tmem_ld32(lane_base + uint32_t(C::DP_COL + 64 * w + 32 * hd), dp);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int ii = 16 * hd + i;
+              pk_ds[ii] = pack2_f2<DT>(fmul2(f2pack(sv[2 * ii], sv[2 * ii + 1]),
+                                             fadd2(f2pack(dp[2 * i], dp[2 * i + 1]), ndelta2)));
+            }
+          }
         }
         tmem_st16(tS, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
         tmem_st16(tS + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));

@@ -438,15 +438,14 @@ __global__ void __launch_bounds__(bf128::NUM_THREADS, 1)
             const float4 nl = l4[c4];
             const float4 nd = d4[c4];
             const int c = c4 * 4;
-            const uint32_t p01 = pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y))));
-            const uint32_t p23 =
-                pack2_f2<DT>(exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w))));
-            const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-            const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-            pk_p[c4 * 2] = p01;
-            pk_p[c4 * 2 + 1] = p23;
-            pk_ds[c4 * 2] = mul2<DT>(p01, d01);
-            pk_ds[c4 * 2 + 1] = mul2<DT>(p23, d23);
+            // dS = P (dP - Delta) in fp32, rounded once (as the reference's
+            // dsT = pT * (dpT - Di) before .to(float16), attention.py:300-305)
+            const uint64_t e01 = exp2_mufu2(ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y)));
+            const uint64_t e23 = exp2_mufu2(ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w)));
+            pk_p[c4 * 2] = pack2_f2<DT>(e01);
+            pk_p[c4 * 2 + 1] = pack2_f2<DT>(e23);
+            pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(e01, fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y))));
+            pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(e23, fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w))));
           }
           // packed halves land on columns this thread has already read
           tmem_st16(tB + uint32_t(16 * hh), pk_p);
