@@ -471,24 +471,6 @@ __device__ __forceinline__ float2 unpack2(uint32_t v) {
   }
 }
 
-// A packed pair of the operand type, widened to an fp32 pair exactly with
-// integer and FMA-pipe work only (the conversion unit is left to the
-// exponentials).  bf16: the bits are the top half of an fp32.  fp16 (no
-// sign: the callers' values are probabilities >= 0): the exponent and
-// mantissa bits shifted into an fp32's positions read as the value times
-// 2^-112, for normal and subnormal fp16 alike, and the multiply by 2^112
-// (a power of two, no rounding) restores it.
-template <int DT>
-__device__ __forceinline__ uint64_t widen2(uint32_t v) {
-  if constexpr (DT == 0) {
-    const uint64_t t = f2pack(__uint_as_float((v & 0x7fffu) << 13), __uint_as_float((v >> 3) & 0x0fffe000u));
-    constexpr float k2p112 = 5.192296858534828e33f;  // 2^112
-    return fmul2(t, f2pack(k2p112, k2p112));
-  } else {
-    return f2pack(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
-  }
-}
-
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
