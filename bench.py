@@ -847,7 +847,7 @@ def run_sweep(args) -> None:
 
     impls = [("b200", fa.scaled_dot_product_attention, {})]
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    if os.path.isdir(os.path.join(ref_dir, "triton_flash_attention")):
+    if not args.no_comparators and os.path.isdir(os.path.join(ref_dir, "triton_flash_attention")):
         sys.path.insert(0, ref_dir)
         import triton_flash_attention as ref
 
