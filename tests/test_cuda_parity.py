@@ -125,10 +125,17 @@ def test_delta_kernel(d):
     assert _maxabs(delta, ref) <= 1e-3
 
 
+def _rounding_floor(ref) -> float:
+    """Half an fp16 ulp of the largest |value|: one output rounding step."""
+    m = float(np.abs(ref).max())
+    return 2.0 ** (math.floor(math.log2(m)) - 11) if m > 0 else 0.0
+
+
 def test_golden_vectors():
     """The reference's own Triton outputs (tests/golden/golden.npz) against
     this build: the B200 error vs float64 must be no worse than the
-    reference kernel's (plus a small floor)."""
+    reference kernel's, plus at most one output rounding step
+    (``_rounding_floor``)."""
     import os
     g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
     names = sorted({k.split("/")[0] for k in g.files})
@@ -141,7 +148,7 @@ def test_golden_vectors():
         for key, mine in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
             ref_err = _maxabs(g[f"{name}/{key}"], ref[key])
             my_err = _maxabs(mine, ref[key])
-            assert my_err <= max(1.5 * ref_err, 2e-4), (name, key, my_err, ref_err)
+            assert my_err <= ref_err + _rounding_floor(ref[key]), (name, key, my_err, ref_err)
         # the saved LSE agrees with the reference kernel's own saved LSE; the
         # bound covers the exp2 approximations (MUFU ex2.approx and the
         # 1e-4-relative polynomial), i.e. ~1.4e-4 in log2 units
@@ -187,15 +194,17 @@ def _torch_fp32_reference(q, k, v, do, causal, group):
     return o_all, dq_all, dk, dv
 
 
-@pytest.mark.parametrize("cfg", [
-    ("C2 MHA causal B4 H16 N4096 D64", 4, 16, 16, 4096, 64, True),
-    ("C3 full N2049 D128", 1, 4, 4, 2049, 128, False),
-    ("C3 full N8192 D32", 1, 2, 2, 8192, 32, False),
-    ("C4 GQA causal N8191 D128", 1, 8, 2, 8191, 128, True),
-])
+FULL_SIZE = ([("C2 MHA causal B4 H16 N4096 D64", 4, 16, 16, 4096, 64, True),
+              ("C4 GQA causal B2 Hq32 Hkv8 N8191 D128", 2, 32, 8, 8191, 128, True)]
+             + [(f"C3 full N{n} D{d} (2 of 16 heads)", 1, 2, 2, n, d, False)
+                for d in (32, 64, 128) for n in (512, 1024, 2048, 2049, 4096, 8192)])
+
+
+@pytest.mark.parametrize("cfg", FULL_SIZE, ids=[c[0] for c in FULL_SIZE])
 def test_full_size_against_torch_fp32(cfg):
-    """BASELINE-sized shapes (C4 with fewer heads) against fp32 math on the
-    GPU: O within 2e-3, gradients within 1e-2."""
+    """The BASELINE configurations at their sequence lengths (C2 and C4 whole,
+    every C3 point on two heads) against fp32 math on the GPU: O within 2e-3,
+    gradients within 1e-2."""
     _, b, hq, hkv, n, d, causal = cfg
     torch.manual_seed(2024)
     q = torch.randn(b, hq, n, d, device="cuda", dtype=torch.float16)
