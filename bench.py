@@ -58,6 +58,9 @@ benchmark (benchmarks/benchmark_attention.py:46-53): fwd+bwd = 3.5 x
 * ``--workload masked``: boolean ``attn_mask`` forms (key padding, all
   true, random) and ``dropout_p`` at the C2 shape beside the unmasked call.
   Informational.
+* ``--workload kernels --shape B,Hq,Hkv,N,D``: each kernel alone through the
+  C ABI (forward, preprocess, Delta, fused backward, dQ, dK/dV); the command
+  the kernel profiles are captured with.  Informational.
 """
 
 from __future__ import annotations
@@ -833,6 +836,97 @@ def run_reference_gpu(args) -> None:
                                                                   / out["b200"]["ms_per_step"], 3)}), flush=True)
 
 
+def run_kernels(args) -> None:
+    """Individual kernels through the C ABI at one shape (``--shape
+    B,Hq,Hkv,N,D``, causal unless ``--full``): the forward, the backward
+    preprocess (Delta + zeroing the fp32 dQ accumulator), Delta alone, the
+    fused backward, and the separate dQ and dK/dV kernels; median of 20
+    launches each, CUDA events.  GEMM kernels report TFLOP/s of the work they
+    are credited with (forward 1x, fused backward 2.5x, dQ 1.5x, dK/dV 2x of
+    the forward count), the memory-bound ones GB/s of their algorithmic
+    bytes.  Informational, one JSON line; the command the kernel profiles
+    under profiles/ are captured with."""
+    import torch
+
+    import triton_flash_attention_b200 as fa
+    from triton_flash_attention_b200 import _abi
+
+    b, hq, hkv, n, d = (int(x) for x in args.shape.split(","))
+    causal = not args.full
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, do = (torch.randn(b, hq, n, d, device=dev, dtype=torch.float16, generator=g) for _ in range(2))
+    k, v = (torch.randn(b, hkv, n, d, device=dev, dtype=torch.float16, generator=g) for _ in range(2))
+    sc = d ** -0.5
+    st = torch.cuda.current_stream().cuda_stream
+    lib = _abi.lib()
+    o, lse = fa.attention_forward(q, k, v, causal, sc)
+    delta = torch.empty(b, hq, n, device=dev, dtype=torch.float32)
+    acc = torch.empty(b, hq, n, d, device=dev, dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    S = _abi.strides3
+    fwd_fl = fa.attention_flops(batch=b, query_heads=hq, sequence=n, head_dim=d, causal=causal, mode="forward")
+    row_bytes = b * hq * n
+
+    def fwd():
+        _abi.check(lib.fa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), b, hq, hkv, n,
+                              n, d, S(q), S(k), S(v), S(o), sc, int(causal), 0, 0, st), "fa_fwd")
+
+    def pre():
+        _abi.check(lib.fa_bwd_preprocess(o.data_ptr(), do.data_ptr(), delta.data_ptr(), acc.data_ptr(), b, hq, n, d,
+                                          S(o), S(do), st), "fa_bwd_preprocess")
+
+    def dlt():
+        _abi.check(lib.fa_bwd_delta(o.data_ptr(), do.data_ptr(), delta.data_ptr(), b, hq, n, d, S(o), S(do), st),
+                   "fa_bwd_delta")
+
+    def fused():
+        _abi.check(lib.fa_bwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                    delta.data_ptr(), acc.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, hq, hkv, n, n,
+                                    d, S(q), S(k), S(v), S(do), S(dk), S(dv), sc, int(causal), 0, 0, 0, st),
+                   "fa_bwd_fused")
+
+    def dqk():
+        _abi.check(lib.fa_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                 delta.data_ptr(), dq.data_ptr(), b, hq, hkv, n, n, d, S(q), S(k), S(v), S(do),
+                                 S(dq), sc, int(causal), 0, 0, 0, st), "fa_bwd_dq")
+
+    def dkdv():
+        _abi.check(lib.fa_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                   delta.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, hq, hkv, n, n, d, S(q), S(k),
+                                   S(v), S(do), S(dk), S(dv), sc, int(causal), 0, 0, 0, st), "fa_bwd_dkdv")
+
+    kernels = {
+        "fwd": (fwd, "TFLOP/s", fwd_fl),
+        "preprocess": (pre, "GB/s", 4 * row_bytes * d + 4 * row_bytes + 4 * row_bytes * d),
+        "delta": (dlt, "GB/s", 4 * row_bytes * d + 4 * row_bytes),
+        "fused": (fused, "TFLOP/s", fwd_fl * 5 // 2),
+        "dq": (dqk, "TFLOP/s", fwd_fl * 3 // 2),
+        "dkdv": (dkdv, "TFLOP/s", 2 * fwd_fl),
+    }
+    pre()
+    torch.cuda.synchronize()
+    out = {}
+    for name in args.kernels.split(","):
+        fn, unit, work = kernels[name]
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+        for e0, e1 in evs:
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+        us = statistics.median(a.elapsed_time(b_) for a, b_ in evs) * 1e3
+        rate = work / (us * 1e-6) / (1e12 if unit == "TFLOP/s" else 1e9)
+        out[name] = {"us": round(us, 1), unit: round(rate, 1)}
+    print(json.dumps({"workload": "kernels", "shape": {"B": b, "Hq": hq, "Hkv": hkv, "N": n, "D": d,
+                                                       "causal": causal},
+                      "dtype": "fp16", "data": "synthetic: seeded N(0,1)", "results": out,
+                      "device_status": _abi.device_status()}), flush=True)
+
+
 SWEEP = ([("C3", 4, 16, 16, n, d, False) for d in (32, 64, 128) for n in (512, 1024, 2048, 2049, 4096, 8192)]
          + [("C4", 2, 32, 8, 8191, 128, True)])
 
@@ -1106,12 +1200,18 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--deterministic", action="store_true",
                     help="time the bitwise-reproducible backward (separate dQ and dK/dV kernels)")
-    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen", "decode", "masked"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "ring", "sweep", "varlen", "decode", "masked", "kernels"],
+                    default="c2",
                     help="c2: the metric's configuration (default); ring: C5 ring context parallelism; "
                          "sweep: C3/C4 forward and forward+backward beside the reference's Triton kernel; "
                          "varlen: a packed batch of ragged sequences beside its padded dense equivalent; "
                          "decode: one query per sequence over a paged K/V cache; "
-                         "masked: boolean attn_mask forms and dropout at the C2 shape")
+                         "masked: boolean attn_mask forms and dropout at the C2 shape; "
+                         "kernels: individual kernels through the C ABI at --shape")
+    ap.add_argument("--shape", default="4,16,16,4096,64", help="kernels workload: B,Hq,Hkv,N,D")
+    ap.add_argument("--kernels", default="fwd,preprocess,delta,fused,dq,dkdv",
+                    help="kernels workload: which kernels to time")
+    ap.add_argument("--full", action="store_true", help="kernels workload: bidirectional instead of causal")
     ap.add_argument("--ring-seq", type=int, default=0, help="override C5's sequence length (ring workload)")
     ap.add_argument("--ring-steps", type=int, default=3, help="timed C5 steps (the ring key / ring workload)")
     ap.add_argument("--no-ring", action="store_true", help="skip the C5 ring key of the default line")
@@ -1135,6 +1235,8 @@ def main() -> None:
         run_decode(args)
     elif args.workload == "masked":
         run_masked(args)
+    elif args.workload == "kernels":
+        run_kernels(args)
     else:
         run_ours(args)
 
