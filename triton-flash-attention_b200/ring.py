@@ -225,14 +225,21 @@ def ring_backward(q, k, v, o, lse, do, *, causal: bool, scale: float, group=None
     # one fused pass per chunk pair (dQ, dK, dV from one visit), unless
     # deterministic algorithms ask for the bitwise-reproducible split kernels
     fused = ops.bwd_fused is not None and not torch.are_deterministic_algorithms_enabled()
-    dk_cur = torch.zeros(k_cur.shape, device=k.device, dtype=acc)
-    dv_cur = torch.zeros(v_cur.shape, device=v.device, dtype=acc)
+    # The running fp32 dK/dV sums of the block held at step s arrive from
+    # rank - 1 while this rank computes its own contribution into fresh
+    # accumulators; the two are added and sent on to rank + 1 at the end of
+    # the step, so each hand-off overlaps the next step's compute.  After the
+    # last step every rank receives its own block's complete sums.
+    gworks = None
+    g_in = g_out = None  # buffers of the hand-off in flight (kept alive until it completes)
     for step in range(world):
         src = (rank - step) % world
         kb = _chunk_ids(world, src)
         works = None
         if step + 1 < world:  # K/V for the next step travel while this one computes
             nxt_kv, works = _exchange((k_cur, v_cur), group, world, rank)
+        dk_cur = torch.zeros(k_cur.shape, device=k.device, dtype=acc)
+        dv_cur = torch.zeros(v_cur.shape, device=v.device, dtype=acc)
         for i, j, diag in visible_pairs(world, rank, src, causal):
             kj, vj = _chunk(k_cur, j, c), _chunk(v_cur, j, c)
             dk_j = _chunk(dk_cur, j, c)
@@ -244,15 +251,22 @@ def ring_backward(q, k, v, o, lse, do, *, causal: bool, scale: float, group=None
             ops.bwd_dq(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dq_acc[i], qa[i] * c, kb[j] * c)
             ops.bwd_dkdv(q_c[i], kj, vj, do_c[i], lse_c[i], delta_c[i], diag, scale, dk_j, dv_j,
                          qa[i] * c, kb[j] * c)
-        # this block's gradient accumulators move on with it (the last hop
-        # returns them to their owner)
-        if world > 1:
-            nxt_g, gworks = _exchange((dk_cur, dv_cur), group, world, rank)
+        # this block's running sums (from rank - 1) plus this rank's part move
+        # on with the block; the last hop returns them to their owner
+        if gworks is not None:
             _wait(gworks)
-            dk_cur, dv_cur = nxt_g
+            dk_cur += g_in[0]
+            dv_cur += g_in[1]
+        if world > 1:
+            g_out = (dk_cur, dv_cur)
+            g_in, gworks = _exchange(g_out, group, world, rank)
         if works is not None:
             _wait(works)
             k_cur, v_cur = nxt_kv
+    if gworks is not None:
+        _wait(gworks)
+        dk_cur, dv_cur = g_in
+    del g_out
     dq = torch.cat(dq_acc, dim=2).to(q.dtype)
     return dq, dk_cur.to(k.dtype), dv_cur.to(v.dtype)
 
