@@ -519,14 +519,20 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
             for (int c4 = 0; c4 < 16; ++c4) {
               const float4 nd = d4[c4];
               const int c = c4 * 4;
-              // dS = P (dP - Delta): P arrives packed from the P^T
-              // warpgroup; the product is formed in the operand type
-              // (measured: widening P and multiplying in fp32 made the
-              // kernel 8% slower for a few percent less error)
-              const uint32_t d01 = pack2_f2<DT>(fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y)));
-              const uint32_t d23 = pack2_f2<DT>(fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w)));
-              pk_ds[c4 * 2] = mul2<DT>(__float_as_uint(pf[c4 * 2]), d01);
-              pk_ds[c4 * 2 + 1] = mul2<DT>(__float_as_uint(pf[c4 * 2 + 1]), d23);
+              // dS = P (dP - Delta), P arriving packed from the P^T
+              // warpgroup.  bf16: P widened (two shifts), the product in
+              // fp32, one rounding.  fp16: the product in fp16 (widening an
+              // fp16 P exactly costs integer work that made the kernel 8%
+              // slower for a few percent less error, measured).
+              const uint64_t d01f = fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y));
+              const uint64_t d23f = fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w));
+              if constexpr (DT == DT_BF16) {
+                pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(widen_bf16x2(__float_as_uint(pf[c4 * 2])), d01f));
+                pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(widen_bf16x2(__float_as_uint(pf[c4 * 2 + 1])), d23f));
+              } else {
+                pk_ds[c4 * 2] = mul2<DT>(__float_as_uint(pf[c4 * 2]), pack2_f2<DT>(d01f));
+                pk_ds[c4 * 2 + 1] = mul2<DT>(__float_as_uint(pf[c4 * 2 + 1]), pack2_f2<DT>(d23f));
+              }
             }
             tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
             tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));

@@ -471,6 +471,11 @@ __device__ __forceinline__ float2 unpack2(uint32_t v) {
   }
 }
 
+// A packed bf16 pair as an fp32 pair (exact: bf16 is the top half of fp32).
+__device__ __forceinline__ uint64_t widen_bf16x2(uint32_t v) {
+  return f2pack(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
