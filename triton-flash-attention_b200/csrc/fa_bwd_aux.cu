@@ -4,7 +4,11 @@
 //    preprocess of the reference (triton_flash_attention/attention.py:237-255).
 //    Each row is read once with 16-byte loads, D/8 lanes per row, and reduced
 //    with warp shuffles; a grid-stride loop sized to the SM count keeps every
-//    SM streaming.
+//    SM streaming.  When O and dO are contiguous (the usual case) a lane's
+//    vector is at element 8 * (vector index) of both, and every lane keeps
+//    DELTA_UNROLL independent load pairs in flight: the strided path's
+//    64-bit index arithmetic and its one pair per lane left the kernel
+//    latency-bound at half the HBM rate.
 //  * fa_merge_kernel: the log-sum-exp merge of ring context parallelism
 //    (no counterpart in the reference).
 // Both take fp16 or bf16 operands (template parameter DT).
@@ -36,15 +40,51 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b) {
   return acc;
 }
 
+constexpr int DELTA_UNROLL = 4;
+
 template <int D, int DT>
 __global__ void __launch_bounds__(256) fa_delta_kernel(const uint16_t* __restrict__ o, long long o_sb,
                                                        long long o_sh, long long o_sn,
                                                        const uint16_t* __restrict__ dO, long long do_sb,
                                                        long long do_sh, long long do_sn, float* __restrict__ delta,
-                                                       float* __restrict__ zero_acc, int H, int N, long long rows) {
+                                                       float* __restrict__ zero_acc, int H, int N, long long rows,
+                                                       int contiguous) {
   constexpr int TPR = D / 8;  // lanes per row, 8 elements each
   const long long total = rows * TPR;
   const long long nthreads = (long long)gridDim.x * blockDim.x;
+  const int lane = int(threadIdx.x & 31);
+  if (contiguous) {
+    // vector idx = row * TPR + part sits at element 8 * idx of O, dO and (as
+    // fp32) of the dQ accumulator; the warp's lanes stay within whole rows
+    constexpr int U = DELTA_UNROLL;
+    for (long long base = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total;
+         base += nthreads * U) {
+      uint4 a[U], b[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long idx = base + u * nthreads + lane;
+        if (idx < total) {
+          a[u] = ld_nc_v4(o + idx * 8);
+          b[u] = ld_nc_v4(dO + idx * 8);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long idx = base + u * nthreads + lane;
+        const bool valid = idx < total;
+        float acc = valid ? dot8<DT>(a[u], b[u]) : 0.f;
+        if (valid && zero_acc) {
+          float4* z = reinterpret_cast<float4*>(zero_acc + idx * 8);
+          z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+          z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (valid && idx % TPR == 0) delta[idx / TPR] = acc;
+      }
+    }
+    return;
+  }
   for (long long base = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total;
        base += nthreads) {
     const long long idx = base + (threadIdx.x & 31);
@@ -85,18 +125,20 @@ int launch_bwd_delta_t(const uint16_t* o, long long o_sb, long long o_sh, long l
   const long long cap = (long long)sms * 8;  // 8 x 256 threads resident per SM
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  const int contiguous = o_sn == D && o_sh == (long long)N * D && o_sb == (long long)H * N * D && do_sn == D &&
+                         do_sh == (long long)N * D && do_sb == (long long)H * N * D;
   switch (D) {
     case 32:
       fa_delta_kernel<32, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                     delta, zero_acc, H, N, rows);
+                                                                     delta, zero_acc, H, N, rows, contiguous);
       break;
     case 64:
       fa_delta_kernel<64, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                     delta, zero_acc, H, N, rows);
+                                                                     delta, zero_acc, H, N, rows, contiguous);
       break;
     case 128:
       fa_delta_kernel<128, DT><<<unsigned(blocks), 256, 0, stream>>>(o, o_sb, o_sh, o_sn, dO, do_sb, do_sh, do_sn,
-                                                                      delta, zero_acc, H, N, rows);
+                                                                      delta, zero_acc, H, N, rows, contiguous);
       break;
     default:
       return FA_ERR_UNSUPPORTED_HEAD_DIM;
