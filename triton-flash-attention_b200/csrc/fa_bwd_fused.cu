@@ -12,8 +12,8 @@
 //   dV += P^T dO,  dK += dS^T Q  (kept in TMEM for the whole key tile),
 //   dQ_part = dS K                (one 128 x D partial per item),
 // and the dQ partials are added into an fp32 accumulator [B, Hq, Nq, D] in
-// global memory by TMA reduce-add (cp.reduce.async.bulk.tensor .add), scaled
-// by the softmax scale.  The order of those fp32 additions depends on the
+// global memory by vector reductions (red.global.add.v4.f32), scaled by the
+// softmax scale.  The order of those fp32 additions depends on the
 // schedule, so dQ is not bitwise reproducible run to run (dK, dV are: one
 // CTA owns a key tile and sums the query heads of its group itself).
 //
@@ -24,16 +24,24 @@
 //  * warp 3: TMA of V and the dO tiles;
 //  * warp 1: one thread issues every tcgen05.mma;
 //  * warp 2: owns the TMEM allocation;
-//  * warps 4-7: P^T = exp2(...) for whole items (fp16 / bf16 back into TMEM);
-//  * warps 8-11: dS^T, one item behind: packed into TMEM for the dK MMA and
-//    written to shared memory (128-byte swizzle) for the dQ MMA, which reads
-//    it as an MN-major A operand (dS = (dS^T)^T without a transpose);
-//  * warps 12-15: read the dQ partial from TMEM, scale it, stage it in shared
-//    memory 32 columns at a time and issue the TMA reduce-adds.
+//  * warps 4-7 and 8-11: the elementwise warpgroups; warpgroup w takes query
+//    half w (64 columns) of every item: P^T = exp2(...) (fp16 / bf16 back
+//    into TMEM), then, once dP^T is in, dS^T from the P^T it still holds in
+//    registers: packed into TMEM for the dK MMA and written to shared memory
+//    (128-byte swizzle) for the dQ MMA, which reads it as an MN-major A
+//    operand (dS = (dS^T)^T without a transpose).  Two warps per scheduler
+//    share the exponential unit during the exponentials;
+//  * warps 12-15: read the dQ partial from TMEM (a warp owns 32 query rows),
+//    scale it and turn it through a per-warp shared-memory tile, 32 columns
+//    at a time, so that each reduction instruction of the warp covers four
+//    whole 128-byte row segments; no barrier beyond the warp and nothing to
+//    wait for, the reductions complete on their own.
 // TMEM (512 columns): S^T buffers at [0,128) and [128,256) -- P^T of item g
-//   packed into columns [0,64) of buffer g & 1 and the item's dQ partial in
-//   columns [64, 64+D) once S^T was read; dP^T at [256,384) with dS^T packed
-//   into [256,288) and [320,352); dV at [384,384+D), dK at [384+D,384+2D).
+//   packed into columns [0,32) and [64,96) of buffer g & 1 (each query half
+//   into the start of its own S^T half, which its warpgroup has read) and the
+//   item's dQ partial in columns [64, 64+D) once dV read P^T; dP^T at
+//   [256,384) with dS^T packed into [256,288) and [320,352); dV at
+//   [384,384+D), dK at [384+D,384+2D).
 #include "fa_common.cuh"
 #include "fa_kernels.h"
 #include "fa_key_tiles.cuh"
@@ -71,7 +79,7 @@ struct Cfg {
   static constexpr int KV_TILE_BYTES = BM * D * 2;
   static constexpr int Q_TILE_BYTES = BQ * D * 2;
   static constexpr int DS_BYTES = BM * BQ * 2;       // two boxes of 64 query columns, 128-byte swizzle
-  static constexpr int DQ_STAGE_BYTES = BQ * 32 * 4;  // 32 fp32 columns of a dQ partial
+  static constexpr int DQ_STAGE_BYTES = 4 * 32 * 128;  // per dQ warp: 32 rows x 32 fp32 columns
   static constexpr int OFF_K = 0;                          // 2 buffers
   static constexpr int OFF_V = OFF_K + 2 * KV_TILE_BYTES;  // 2 buffers
   static constexpr int OFF_Q = OFF_V + 2 * KV_TILE_BYTES;
@@ -82,8 +90,8 @@ struct Cfg {
   static constexpr int OFF_DELTA = OFF_LSE + NST * BQ * 4;
   static constexpr int OFF_BAR = OFF_DELTA + NST * BQ * 4;
   // kv_full[2], kv_empty[2], full[NST], empty[NST], s_full[2], dp_full, p_ready[2], ds_ready, ds_free,
-  // dq_full[2], dq_empty[2], stage_full, stage_free, acc_full, acc_empty, mma_done
-  static constexpr int NUM_BARS = 2 + 2 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 2 + 2 + 2 + 1 + 1 + 1;
+  // dq_full[2], dq_empty[2], acc_full, acc_empty, mma_done
+  static constexpr int NUM_BARS = 2 + 2 + 2 * NST + 2 + 1 + 2 + 1 + 1 + 2 + 2 + 1 + 1 + 1;
   static constexpr int OFF_CTL = OFF_BAR + NUM_BARS * 8;
   static constexpr int OFF_MISC = OFF_CTL + 16;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
@@ -112,7 +120,7 @@ template <int D, int DT, bool VL, bool BITS>
 __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     fa_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                         const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                        const __grid_constant__ CUtensorMap tmap_dq, const AttnShape shp,
+                        float* __restrict__ dq_acc, const AttnShape shp,
                         const float* __restrict__ lse, const float* __restrict__ delta, void* __restrict__ dk_out,
                         const long long dk_sb, const long long dk_sh, const long long dk_sn,
                         void* __restrict__ dv_out, const long long dv_sb, const long long dv_sh,
@@ -143,11 +151,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
   uint64_t* ds_free = ds_ready + 1;  // one phase per item: the dQ MMA read dS
   uint64_t* dq_full = ds_free + 1;
   uint64_t* dq_empty = dq_full + 2;
-  // dQ staging tile, one phase per 32-column piece: written by the dQ
-  // warpgroup / read by its reduce-add
-  uint64_t* stage_full = dq_empty + 2;
-  uint64_t* stage_free = stage_full + 1;
-  uint64_t* acc_full = stage_free + 1;  // one phase per non-empty tile: dV, dK complete
+  uint64_t* acc_full = dq_empty + 2;  // one phase per non-empty tile: dV, dK complete
   uint64_t* acc_empty = acc_full + 1;  // one phase per non-empty tile: the epilogue read them
   uint64_t* mma_done = acc_empty + 1;
   CtaCtl* ctl_w = reinterpret_cast<CtaCtl*>(smem + C::OFF_CTL);
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       mbar_init(kv_full + i, 2);  // K from warp 0, V from warp 3
       mbar_init(kv_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(p_ready + i, 128);
+      mbar_init(p_ready + i, 256);  // both elementwise warpgroups
       mbar_init(dq_full + i, 1);
       mbar_init(dq_empty + i, 128);
     }
@@ -176,10 +180,8 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       mbar_init(empty + s, 1);
     }
     mbar_init(dp_full, 1);
-    mbar_init(ds_ready, 128);
+    mbar_init(ds_ready, 256);
     mbar_init(ds_free, 1);
-    mbar_init(stage_full, 128);
-    mbar_init(stage_free, 1);
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 256);
     mbar_init(mma_done, 1);
@@ -339,10 +341,9 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
           tc_fence_after();
           return r;
         };
-        // A operand columns of query rows [16ks, 16ks+16): P^T is packed
-        // densely, dS^T in two halves 64 columns apart
-        auto p_col = [](int ks) { return uint32_t(ks * 8); };
-        auto ds_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
+        // A operand columns of query rows [16ks, 16ks+16): P^T and dS^T are
+        // packed in two query halves 64 columns apart
+        auto half_col = [](int ks) { return uint32_t((ks >> 2) * 64 + (ks & 3) * 8); };
         int gi = 0, tcn = 0;
         for (int k = 0; ok; ++k) {
           const int t = snake_unit(cta, k, n_cta, n_tiles);
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
               const uint32_t pa = tmem + (g & 1) * 128;
 #pragma unroll
               for (int ks = 0; ks < BQ / 16; ++ks)
-                umma_ts(tmem + C::DV_COL, pa + p_col(ks), sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G,
+                umma_ts(tmem + C::DV_COL, pa + half_col(ks), sdesc_at(dd, mn_major_off<D>(ks)), IDESC_G,
                         (it > 0 || ks > 0) ? 1u : 0u);
             }
             if (!mbar_wait(ds_ready, uint32_t(g) & 1, ctl, 216)) { ok = false; break; }
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
               const SDesc qd = desc_mn_base<D, BQ>(q_tile(g));
 #pragma unroll
               for (int ks = 0; ks < BQ / 16; ++ks)
-                umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + ds_col(ks), sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G,
+                umma_ts(tmem + C::DK_COL, tmem + C::DP_COL + half_col(ks), sdesc_at(qd, mn_major_off<D>(ks)), IDESC_G,
                         (it > 0 || ks > 0) ? 1u : 0u);
             }
             umma_commit(empty + g % C::NST);
@@ -408,8 +409,8 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     }
   } else if (warp < 12) {
     regs_claim<SOFT_REGS>();
-    // =================== P^T (warpgroup 0) / dS^T (warpgroup 1) ===================
-    const int w = (warp - 4) / 4;  // 0: exponentials, 1: dS^T
+    // =================== P^T and dS^T, query half w ===================
+    const int w = (warp - 4) / 4;  // query half of every item
     const int wq = warp & 3;
     const int rl = wq * 32 + lane;  // key row within the tile
     const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
@@ -437,122 +438,112 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       };
       uint4 mw_next;
       if constexpr (BITS) {
-        if (w == 0 && wt.n_items > 0) mw_next = mask_words(0);
+        if (wt.n_items > 0) mw_next = mask_words(0);
       }
       for (int it = 0; it < wt.n_items && ok; ++it) {
         const int g = gi + it;
         const int s = g % C::NST;
         const int q0 = (wt.i_start + it % wt.per_head) * BQ;
-        if (w == 0) {
-          uint4 mw;
-          if constexpr (BITS) {
-            mw = mw_next;
-            if (it + 1 < wt.n_items) mw_next = mask_words(it + 1);
-          }
-          if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 220)) { ok = false; break; }
-          // the stage's -lse2/-Delta: its phase completed before S^T was issued
-          if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 221)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t tS = lane_base + uint32_t((g & 1) * 128 + 64 * hh);
-            float st[64];
-            tmem_ld64(tS, st);
-            int cmin = key_out ? 64 : 0;
-            if (shp.causal && !key_out) {
-              const long long x = cmin_base - q0 - 64 * hh;
-              cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
-            }
-            if (cmin > 0) {
-#pragma unroll
-              for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
-            }
-            if (VL && shp.window > 0 && !key_out) {
-              // sliding window: queries past this key's window do not see it
-              const long long xm = cmin_base + shp.window - 1 - q0 - 64 * hh;  // last visible column
-              if (xm < 63) {
-#pragma unroll
-                for (int c = 0; c < 64; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
-              }
-            }
-            if constexpr (BITS) {
-              const uint32_t words[2] = {hh ? mw.z : mw.x, hh ? mw.w : mw.y};
-              if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<64>(st, words);
-            }
-            const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * hh);
-            uint32_t pk_p[32];
-#pragma unroll
-            for (int c4 = 0; c4 < 16; ++c4) {
-              const float4 nl = l4[c4];
-              const int c = c4 * 4;
-              const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
-              const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
-              const uint64_t e01 = ((2 * c4) & 7) < poly_mask<D>() ? exp2_poly2(x01) : exp2_mufu2(x01);
-              const uint64_t e23 = ((2 * c4 + 1) & 7) < poly_mask<D>() ? exp2_poly2(x23) : exp2_mufu2(x23);
-              pk_p[c4 * 2] = pack2_f2<DT>(e01);
-              pk_p[c4 * 2 + 1] = pack2_f2<DT>(e23);
-            }
-            // packed densely: half hh into columns [32hh, 32hh+32), which
-            // hold S^T values already read
-            const uint32_t tP = lane_base + uint32_t((g & 1) * 128 + 32 * hh);
-            tmem_st16(tP, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
-            tmem_st16(tP + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
-          }
-          tmem_st_wait();
-          tc_fence_before();
-          mbar_arrive(p_ready + (g & 1));
-        } else {
-          if (!mbar_wait_warp(p_ready + (g & 1), uint32_t(g >> 1) & 1, ctl, 222)) { ok = false; break; }
-          if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 223)) { ok = false; break; }
-          if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 224)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * hh);
-            float dpt[64];
-            tmem_ld64(tD, dpt);
-            float pf[32];
-            tmem_ld32(lane_base + uint32_t((g & 1) * 128 + 32 * hh), pf);
-            const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * hh);
-            uint32_t pk_ds[32];
-#pragma unroll
-            for (int c4 = 0; c4 < 16; ++c4) {
-              const float4 nd = d4[c4];
-              const int c = c4 * 4;
-              // dS = P (dP - Delta), P arriving packed from the P^T
-              // warpgroup.  bf16: P widened (two shifts), the product in
-              // fp32, one rounding.  fp16: the product in fp16 (widening an
-              // fp16 P exactly costs integer work that made the kernel 8%
-              // slower for a few percent less error, measured).
-              const uint64_t d01f = fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y));
-              const uint64_t d23f = fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w));
-              if constexpr (DT == DT_BF16) {
-                pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(widen_bf16x2(__float_as_uint(pf[c4 * 2])), d01f));
-                pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(widen_bf16x2(__float_as_uint(pf[c4 * 2 + 1])), d23f));
-              } else {
-                pk_ds[c4 * 2] = mul2<DT>(__float_as_uint(pf[c4 * 2]), pack2_f2<DT>(d01f));
-                pk_ds[c4 * 2 + 1] = mul2<DT>(__float_as_uint(pf[c4 * 2 + 1]), pack2_f2<DT>(d23f));
-              }
-            }
-            tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
-            tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
-            // the dQ MMA of the previous item has read the dS tile
-            if (hh == 0 && g > 0 && !mbar_wait_warp(ds_free, uint32_t(g - 1) & 1, ctl, 225)) {
-              ok = false;
-              break;
-            }
-            const uint32_t box = ds_row + uint32_t(hh) * uint32_t(BM * 128);
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              st_shared_v4(box + ((uint32_t(c) ^ ds_swz) << 4), pk_ds[4 * c], pk_ds[4 * c + 1], pk_ds[4 * c + 2],
-                           pk_ds[4 * c + 3]);
-          }
-          if (!ok) break;
-          tmem_st_wait();
-          fence_proxy_async_smem();
-          tc_fence_before();
-          mbar_arrive(ds_ready);
+        // ---- P^T of query half w ----
+        uint4 mw;
+        if constexpr (BITS) {
+          mw = mw_next;
+          if (it + 1 < wt.n_items) mw_next = mask_words(it + 1);
         }
+        if (!mbar_wait_warp(s_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 220)) { ok = false; break; }
+        if (!mbar_wait_warp(full + s, uint32_t(g / C::NST) & 1, ctl, 221)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t pk_p[32];
+        {
+          float st[64];
+          tmem_ld64(lane_base + uint32_t((g & 1) * 128 + 64 * w), st);
+          int cmin = key_out ? 64 : 0;
+          if (shp.causal && !key_out) {
+            const long long x = cmin_base - q0 - 64 * w;
+            cmin = x <= 0 ? 0 : (x > 64 ? 64 : int(x));
+          }
+          if (cmin > 0) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) st[c] = c >= cmin ? st[c] : -INFINITY;
+          }
+          if (VL && shp.window > 0 && !key_out) {
+            // sliding window: queries past this key's window do not see it
+            const long long xm = cmin_base + shp.window - 1 - q0 - 64 * w;  // last visible column
+            if (xm < 63) {
+#pragma unroll
+              for (int c = 0; c < 64; ++c) st[c] = c <= xm ? st[c] : -INFINITY;
+            }
+          }
+          if constexpr (BITS) {
+            const uint32_t words[2] = {w ? mw.z : mw.x, w ? mw.w : mw.y};
+            if ((words[0] & words[1]) != 0xffffffffu) apply_mask_bits<64>(st, words);
+          }
+          const float4* l4 = reinterpret_cast<const float4*>(s_nlse + s * BQ + 64 * w);
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 nl = l4[c4];
+            const int c = c4 * 4;
+            const uint64_t x01 = ffma2(f2pack(st[c], st[c + 1]), c2x2, f2pack(nl.x, nl.y));
+            const uint64_t x23 = ffma2(f2pack(st[c + 2], st[c + 3]), c2x2, f2pack(nl.z, nl.w));
+            const uint64_t e01 = ((2 * c4) & 7) < poly_mask<D>() ? exp2_poly2(x01) : exp2_mufu2(x01);
+            const uint64_t e23 = ((2 * c4 + 1) & 7) < poly_mask<D>() ? exp2_poly2(x23) : exp2_mufu2(x23);
+            pk_p[c4 * 2] = pack2_f2<DT>(e01);
+            pk_p[c4 * 2 + 1] = pack2_f2<DT>(e23);
+          }
+        }
+        // packed into the first 32 columns of this warpgroup's own S^T
+        // half, which it has read (the other half may still be unread)
+        {
+          const uint32_t tP = lane_base + uint32_t((g & 1) * 128 + 64 * w);
+          tmem_st16(tP, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[0]));
+          tmem_st16(tP + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_p[16]));
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_ready + (g & 1));
+        // ---- dS^T of query half w, P from registers ----
+        if (!mbar_wait_warp(dp_full, uint32_t(g) & 1, ctl, 223)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t pk_ds[32];
+        {
+          const uint32_t tD = lane_base + uint32_t(C::DP_COL + 64 * w);
+          float dpt[64];
+          tmem_ld64(tD, dpt);
+          const float4* d4 = reinterpret_cast<const float4*>(s_ndelta + s * BQ + 64 * w);
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 nd = d4[c4];
+            const int c = c4 * 4;
+            // dS = P (dP - Delta).  bf16: P widened (two shifts), the product
+            // in fp32, one rounding.  fp16: the product in fp16 (widening an
+            // fp16 P exactly costs integer work that made the kernel 8%
+            // slower for a few percent less error, measured).
+            const uint64_t d01f = fadd2(f2pack(dpt[c], dpt[c + 1]), f2pack(nd.x, nd.y));
+            const uint64_t d23f = fadd2(f2pack(dpt[c + 2], dpt[c + 3]), f2pack(nd.z, nd.w));
+            if constexpr (DT == DT_BF16) {
+              pk_ds[c4 * 2] = pack2_f2<DT>(fmul2(widen_bf16x2(pk_p[c4 * 2]), d01f));
+              pk_ds[c4 * 2 + 1] = pack2_f2<DT>(fmul2(widen_bf16x2(pk_p[c4 * 2 + 1]), d23f));
+            } else {
+              pk_ds[c4 * 2] = mul2<DT>(pk_p[c4 * 2], pack2_f2<DT>(d01f));
+              pk_ds[c4 * 2 + 1] = mul2<DT>(pk_p[c4 * 2 + 1], pack2_f2<DT>(d23f));
+            }
+          }
+          tmem_st16(tD, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[0]));
+          tmem_st16(tD + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk_ds[16]));
+        }
+        // the dQ MMA of the previous item has read the dS tile
+        if (g > 0 && !mbar_wait_warp(ds_free, uint32_t(g - 1) & 1, ctl, 225)) { ok = false; break; }
+        {
+          const uint32_t box = ds_row + uint32_t(w) * uint32_t(BM * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            st_shared_v4(box + ((uint32_t(c) ^ ds_swz) << 4), pk_ds[4 * c], pk_ds[4 * c + 1], pk_ds[4 * c + 2],
+                         pk_ds[4 * c + 3]);
+        }
+        tmem_st_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_ready);
       }
       if (!ok) break;
       // ---- epilogue of the tile: warpgroup 0 stores dV, warpgroup 1 stores dK ----
@@ -613,14 +604,18 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
     regs_release<DQ_REGS>();
     // =================== dQ warpgroup ===================
     const int wq = warp & 3;
-    const int r = wq * 32 + lane;  // query row within the item
     const uint32_t lane_base = tmem_addr(tmem, uint32_t(wq * 32), 0);
-    const uint32_t stage_row = sbase + C::OFF_DQS + uint32_t(r) * 128u;
-    const uint32_t swz = uint32_t(r & 7);
+    // per warp: a 32-row x 128-byte tile, 16-byte chunk c of row r at
+    // chunk c ^ (r & 7) (conflict-free row writes and column-strip reads)
+    const uint32_t tile = sbase + C::OFF_DQS + uint32_t(wq) * 4096u;
+    const uint32_t my_row = tile + uint32_t(lane) * 128u;
+    const uint32_t swz = uint32_t(lane & 7);
+    // read side: lane reads chunk lane % 8 of rows 4k + lane / 8
+    const int rd_row = lane >> 3, rd_chunk = lane & 7;
     const float sc = shp.scale;
-    const bool leader = r == 0;
+    // rows of one (batch, head) plane of the accumulator
+    const long long plane_rows = VL ? shp.total_q : shp.Nq;
     int gi = 0;
-    uint32_t pieces = 0;  // staging phases so far
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int t = snake_unit(cta, k, n_cta, n_tiles);
@@ -629,7 +624,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
       for (int it = 0; it < wt.n_items; ++it) {
         const int g = gi + it;
         const int h = wt.kvh * group + it / wt.per_head;
-        const int q0 = (wt.i_start + it % wt.per_head) * BQ;
+        const int q0 = (wt.i_start + it % wt.per_head) * BQ + wq * 32;  // this warp's first query row
         if (!mbar_wait_warp(dq_full + (g & 1), uint32_t(g >> 1) & 1, ctl, 230)) { ok = false; break; }
         tc_fence_after();
         float acc[D];
@@ -638,32 +633,30 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
         if constexpr (D == 64) tmem_ld32(tq + 32, *reinterpret_cast<float(*)[32]>(&acc[32]));
         tc_fence_before();
         mbar_arrive(dq_empty + (g & 1));
+        // rows past the sequence get nothing (their partials are zero, and
+        // in a packed batch they belong to the next sequence)
+        float* plane = dq_acc + ((long long)wt.sq.tb * shp.Hq + h) * plane_rows * D;
 #pragma unroll
         for (int j = 0; j < D / 32; ++j) {
-          // the previous reduce-add has finished reading the staging tile
-          if (pieces > 0 && !mbar_wait(stage_free, (pieces - 1) & 1, ctl, 231)) { ok = false; break; }
+          __syncwarp();  // the previous strip's reads are done
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            st_shared_v4(stage_row + ((uint32_t(c) ^ swz) << 4), __float_as_uint(acc[j * 32 + 4 * c] * sc),
+            st_shared_v4(my_row + ((uint32_t(c) ^ swz) << 4), __float_as_uint(acc[j * 32 + 4 * c] * sc),
                          __float_as_uint(acc[j * 32 + 4 * c + 1] * sc), __float_as_uint(acc[j * 32 + 4 * c + 2] * sc),
                          __float_as_uint(acc[j * 32 + 4 * c + 3] * sc));
-          fence_proxy_async_smem();
-          mbar_arrive(stage_full);
-          if (leader) {
-            if (!mbar_wait(stage_full, pieces & 1, ctl, 232)) { ok = false; break; }
-            tma_reduce_add_4d(&tmap_dq, smem + C::OFF_DQS, j * 32, wt.sq.q0 + q0, h, wt.sq.tb);
-            bulk_commit_group();
-            bulk_wait_read_all();
-            mbar_arrive(stage_free);
+          __syncwarp();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int rr = kk * 4 + rd_row;
+            const float4 v = ld_shared_f4(tile + uint32_t(rr) * 128u + ((uint32_t(rd_chunk) ^ uint32_t(rr & 7)) << 4));
+            if (q0 + rr < wt.sq.nq)
+              red_add_v4(plane + (long long)(wt.sq.q0 + q0 + rr) * D + j * 32 + rd_chunk * 4, v);
           }
-          ++pieces;
         }
-        if (!ok) break;
       }
       if (!ok) break;
       gi += wt.n_items;
     }
-    if (leader) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -675,7 +668,7 @@ __global__ void __launch_bounds__(bfz::NUM_THREADS, 1)
 }
 
 template <int D, int DT, bool VL, bool BITS = false>
-int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
+int launch_bwd_fused_t(const BwdArgs& a) {
   using C = bfz::Cfg<D>;
   auto kern = fa_bwd_fused_kernel<D, DT, VL, BITS>;
   // The register split inside the kernel assumes the launch count; a build
@@ -694,7 +687,8 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
   const int sms = device_sm_count();
   const int n_cta = n_tiles < sms ? n_tiles : sms;
   kern<<<dim3(unsigned(n_cta)), bfz::NUM_THREADS, C::SMEM_BYTES, a.stream>>>(
-      a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, tmap_dq, a.shape, a.lse, a.delta, a.dk, a.dk_sb, a.dk_sh, a.dk_sn,
+      a.tmap_q, a.tmap_do, a.tmap_k, a.tmap_v, static_cast<float*>(a.dq), a.shape, a.lse, a.delta, a.dk, a.dk_sb,
+      a.dk_sh, a.dk_sn,
       a.dv, a.dv_sb, a.dv_sh, a.dv_sn, a.accumulate_fp32, n_tiles, a.mask);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
@@ -702,17 +696,17 @@ int launch_bwd_fused_t(const BwdArgs& a, const CUtensorMap& tmap_dq) {
 // Dense and packed (varlen) layouts are separate instantiations, so the
 // dense kernels carry no per-batch offset arithmetic.
 template <int D, int DT>
-int launch_bwd_fused_l(const BwdArgs& a, const CUtensorMap& tmap_dq) {
-  if (a.mask.bits) return launch_bwd_fused_t<D, DT, false, true>(a, tmap_dq);  // dense layout only
-  return a.shape.cu_q ? launch_bwd_fused_t<D, DT, true>(a, tmap_dq) : launch_bwd_fused_t<D, DT, false>(a, tmap_dq);
+int launch_bwd_fused_l(const BwdArgs& a) {
+  if (a.mask.bits) return launch_bwd_fused_t<D, DT, false, true>(a);  // dense layout only
+  return a.shape.cu_q ? launch_bwd_fused_t<D, DT, true>(a) : launch_bwd_fused_t<D, DT, false>(a);
 }
 
 int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D) {
   switch (D) {
     case 32:
-      return a.dtype == DT_BF16 ? launch_bwd_fused_l<32, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<32, DT_F16>(a, tmap_dq);
+      return a.dtype == DT_BF16 ? launch_bwd_fused_l<32, DT_BF16>(a) : launch_bwd_fused_l<32, DT_F16>(a);
     case 64:
-      return a.dtype == DT_BF16 ? launch_bwd_fused_l<64, DT_BF16>(a, tmap_dq) : launch_bwd_fused_l<64, DT_F16>(a, tmap_dq);
+      return a.dtype == DT_BF16 ? launch_bwd_fused_l<64, DT_BF16>(a) : launch_bwd_fused_l<64, DT_F16>(a);
     case 128:
       return launch_bwd_fused128(a, tmap_dq);
     default:

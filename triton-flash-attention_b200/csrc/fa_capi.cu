@@ -185,9 +185,9 @@ int preprocess_impl(const void* o, const void* dO, float* delta, float* dq_accum
 }
 
 // 4-D fp32 tensor map over the contiguous (B, H, N, D) dQ accumulator, with
-// the box and layout the fused kernel stages its partials in: at D <= 64
-// {32, 128, 1, 1} with the 128-byte swizzle, at D = 128 one warp's
-// {32, 64, 1, 1} piece without swizzle.
+// the box the fused kernel at D = 128 stages its partials in: one warp's
+// {32, 64, 1, 1} piece without swizzle.  (At D <= 64 the fused kernel adds
+// its partials with vector reductions and takes no map.)
 int make_acc_map(CUtensorMap* map, float* ptr, int B, int H, int N, int D) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return FA_ERR_DRIVER;
@@ -197,7 +197,7 @@ int make_acc_map(CUtensorMap* map, float* ptr, int B, int H, int N, int D) {
   cuuint32_t box[4] = {32, cuuint32_t(fused_item_rows(D)), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   D <= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TENSOR_MAP;
 }
@@ -300,8 +300,8 @@ int fused_impl(const void* q, const void* k, const void* v, const void* dO, cons
   if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, D, do_strides, bq, dtype))) return rc;
   if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, D, k_strides, dkdv_cfg::BM, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, D, v_strides, dkdv_cfg::BM, dtype))) return rc;
-  CUtensorMap tmap_dq;
-  if ((rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, D))) return rc;
+  CUtensorMap tmap_dq = {};
+  if (D == 128 && (rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, D))) return rc;
   a.shape = make_shape(B, Hq, Hkv, Nq, Nk, softmax_scale, causal, q_offset, k_offset);
   a.lse = lse;
   a.delta = delta;
@@ -433,8 +433,8 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
     if ((rc = make_map(&a.tmap_do, dO, 1, Hq, total_q, D, sq.v, fused_item_rows(D), dtype))) return rc;
     if ((rc = make_map(&a.tmap_k, k, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
     if ((rc = make_map(&a.tmap_v, v, 1, Hkv, total_k, D, sk.v, dkdv_cfg::BM, dtype))) return rc;
-    CUtensorMap tmap_dq;
-    if ((rc = make_acc_map(&tmap_dq, dq_accum, 1, Hq, total_q, D))) return rc;
+    CUtensorMap tmap_dq = {};
+    if (D == 128 && (rc = make_acc_map(&tmap_dq, dq_accum, 1, Hq, total_q, D))) return rc;
     a.dq = dq_accum;
     a.dq_sb = a.dq_sh = a.dq_sn = 0;
     if ((rc = launch_bwd_fused(a, tmap_dq, D))) return rc;
@@ -653,8 +653,8 @@ int bwd_dense_impl(const void* q, const void* k, const void* v, const void* o, c
     if ((rc = make_map(&a.tmap_do, dO, B, Hq, Nq, W, do_strides, dkdv_cfg::BQ_WIDE, dtype, 1, Dv))) return rc;
     if ((rc = make_map(&a.tmap_k, k, B, Hkv, Nk, W, k_strides, dkdv_cfg::BM, dtype, 1, D))) return rc;
     if ((rc = make_map(&a.tmap_v, v, B, Hkv, Nk, W, v_strides, dkdv_cfg::BM, dtype, 1, Dv))) return rc;
-    CUtensorMap tmap_dq;
-    if ((rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, W))) return rc;
+    CUtensorMap tmap_dq = {};
+    if (W == 128 && (rc = make_acc_map(&tmap_dq, dq_accum, B, Hq, Nq, W))) return rc;
     a.dq = dq_accum;
     a.dq_sb = a.dq_sh = a.dq_sn = 0;
     if ((rc = launch_bwd_fused(a, tmap_dq, W))) return rc;

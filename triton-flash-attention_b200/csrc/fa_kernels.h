@@ -72,7 +72,9 @@ int launch_bwd_delta(const void* o, long long o_sb, long long o_sh, long long o_
                      long long do_sb, long long do_sh, long long do_sn, float* delta, float* zero_acc, int B, int H,
                      int N, int D, int dtype, cudaStream_t stream);
 // Fused dK/dV + dQ backward (every D; D = 128 runs fa_bwd_fused128.cu, with
-// no boolean mask or dropout); tmap_dq maps the fp32 accumulator.
+// no boolean mask or dropout).  The fp32 dQ accumulator is a.dq; the D = 128
+// kernel reduce-adds into it through tmap_dq, the D <= 64 kernels add into it
+// directly (tmap_dq unused).
 int launch_bwd_fused(const BwdArgs& a, const CUtensorMap& tmap_dq, int D);
 int launch_bwd_fused128(const BwdArgs& a, const CUtensorMap& tmap_dq);
 // acc_w: the accumulator's row width (0: D); dq receives its first D columns.
