@@ -82,7 +82,7 @@ CAUSAL = True
 WORKLOAD = "C2: MHA causal fp16 fwd+bwd B4 H16 N4096 D64"
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 launch (--set full capture of this command)
 DKDV_TRAFFIC_BYTES = 191_409_664 + 38_601_472
-FUSED_TRAFFIC_BYTES = 638_977_792 + 326_238_208
+FUSED_TRAFFIC_BYTES = 684_556_544 + 343_758_848
 
 
 def flops_step() -> int:
