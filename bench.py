@@ -1142,52 +1142,69 @@ def run_decode(args) -> None:
     group's 4 query heads share a query tile, so each K/V page is read once
     per group).  Decode is bound by reading the cache: the line reports the
     achieved HBM bandwidth (unique K/V bytes / time) against the measured
-    copy peak.  Informational, one JSON line."""
+    copy peak.  The ``few_sequences`` key times 2 sequences of 65,536 cached
+    tokens (the same 512 MiB of cache), whose 16 (sequence, K/V head) units
+    leave most SMs idle, so the call splits each unit's keys (split-KV, count
+    from ``varlen.kv_splits``); both keys also time the call with
+    ``num_splits=1``.  Informational, one JSON line."""
     import numpy as np
     import torch
 
     import triton_flash_attention_b200 as fa
+    from triton_flash_attention_b200 import varlen
 
     dev = torch.device("cuda", 0)
-    pages_per = DECODE_CTX // DECODE_PAGE
-    n_pages = DECODE_B * pages_per
-    rng = np.random.default_rng(5)
-    table = torch.tensor(rng.permutation(n_pages).reshape(DECODE_B, pages_per), dtype=torch.int32, device=dev)
-    g = torch.Generator(device=dev).manual_seed(6)
-    kc, vc = (torch.randn(n_pages, DECODE_PAGE, DECODE_HKV, DECODE_D, device=dev, dtype=torch.float16, generator=g)
-              for _ in range(2))
-    q = torch.randn(DECODE_B, DECODE_HQ, DECODE_D, device=dev, dtype=torch.float16, generator=g)
-    cu = torch.arange(DECODE_B + 1, dtype=torch.int32, device=dev)
-    sk = torch.full((DECODE_B,), DECODE_CTX, dtype=torch.int32, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
     steps = max(1, min(args.steps, 50))
-
-    def step():
-        fa.scaled_dot_product_attention_paged(q, kc, vc, table, cu, sk, 1, DECODE_CTX, is_causal=True,
-                                              enable_gqa=True)
-
-    with torch.no_grad():
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    kv_bytes = 2 * DECODE_B * DECODE_CTX * DECODE_HKV * DECODE_D * 2
     peaks = read_peaks()
-    gbs = kv_bytes / (ms * 1e-3) / 1e9
+
+    def measure(n_seq, ctx):
+        pages_per = ctx // DECODE_PAGE
+        n_pages = n_seq * pages_per
+        rng = np.random.default_rng(5)
+        table = torch.tensor(rng.permutation(n_pages).reshape(n_seq, pages_per), dtype=torch.int32, device=dev)
+        g = torch.Generator(device=dev).manual_seed(6)
+        kc, vc = (torch.randn(n_pages, DECODE_PAGE, DECODE_HKV, DECODE_D, device=dev, dtype=torch.float16,
+                              generator=g) for _ in range(2))
+        q = torch.randn(n_seq, DECODE_HQ, DECODE_D, device=dev, dtype=torch.float16, generator=g)
+        cu = torch.arange(n_seq + 1, dtype=torch.int32, device=dev)
+        sk = torch.full((n_seq,), ctx, dtype=torch.int32, device=dev)
+
+        def timed(num_splits):
+            def step():
+                fa.scaled_dot_product_attention_paged(q, kc, vc, table, cu, sk, 1, ctx, is_causal=True,
+                                                      enable_gqa=True, num_splits=num_splits)
+
+            with torch.no_grad():
+                for _ in range(args.warmup):
+                    step()
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    step()
+                e1.record()
+                torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / steps
+
+        ms, ms_unsplit = timed(None), timed(1)
+        kv_bytes = 2 * n_seq * ctx * DECODE_HKV * DECODE_D * 2
+        gbs = kv_bytes / (ms * 1e-3) / 1e9
+        return {"sequences": n_seq, "context": ctx, "ms_per_step": round(ms, 4),
+                "kv_splits": varlen.kv_splits(n_seq * DECODE_HKV, ctx // 128, sms),
+                "unsplit_ms_per_step": round(ms_unsplit, 4), "kv_bytes_per_step": kv_bytes,
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"]}}
+
+    main_cfg = measure(DECODE_B, DECODE_CTX)
+    few = measure(2, DECODE_CTX * DECODE_B // 2)
     print(json.dumps({
-        "workload": "decode", "sequences": DECODE_B, "context": DECODE_CTX, "query_heads": DECODE_HQ,
-        "kv_heads": DECODE_HKV, "head_dim": DECODE_D, "page_size": DECODE_PAGE, "dtype": "fp16",
-        "data": "synthetic: seeded N(0,1) cache and queries, shuffled page table",
-        "ms_per_step": round(ms, 4), "kv_bytes_per_step": kv_bytes,
-        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"]},
-        "note": "L2 (126 MB) is smaller than the 512 MiB cache; no flush needed",
+        "workload": "decode", "query_heads": DECODE_HQ, "kv_heads": DECODE_HKV,
+        "head_dim": DECODE_D, "page_size": DECODE_PAGE, "dtype": "fp16",
+        "data": "synthetic: seeded N(0,1) cache and queries, shuffled page table", **main_cfg,
+        "few_sequences": few,
+        "note": "L2 (126 MB) is smaller than either case's 512 MiB cache; no flush needed",
     }), flush=True)
 
 

@@ -260,6 +260,41 @@ FA_API int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void* v_c
                       int num_pages, int page_size, int max_pages_per_seq, int D,
                       float softmax_scale, int causal, int window, void* stream);
 
+/* Split-KV form of fa_fwd_paged for decode: when the (sequence, K/V head)
+ * units are fewer than the SMs, each unit's key tiles are cut into `splits`
+ * equal ranges of whole 128-key tiles, so that splits x units CTAs' worth of
+ * work stream the cache.  Range s writes its partial output, normalised by
+ * its own row sums, to o_part + s * total_q * Hq * D (o_part is
+ * (splits, total_q, Hq, D), contiguous) and its base-2 log-sum-exp to
+ * lse_part + s * Hq * total_q (lse_part is (splits, Hq, total_q) fp32); a
+ * range that sees no key of a row writes 0 and -inf.  fa_combine_splits then
+ * merges them.  Requires GQA packing (Hq / Hkv a power of two from 2 to 64,
+ * max_seqlen_q * Hq / Hkv <= 256) and no window; 1 <= splits <=
+ * min(FA_MAX_KV_SPLITS, key tiles).  No counterpart in the reference (no
+ * paged path there). */
+#define FA_MAX_KV_SPLITS 64
+FA_API int fa_fwd_paged_split(const void* q, const void* k_cache, const void* v_cache, void* o_part,
+                       float* lse_part, const int* cu_seqlens_q, const int* seqlens_k,
+                       const int* block_table, int B, int Hq, int Hkv, int max_seqlen_q,
+                       int max_seqlen_k, int total_q, int num_pages, int page_size,
+                       int max_pages_per_seq, int D, float softmax_scale, int causal, int splits,
+                       void* stream);
+FA_API int fa_fwd_paged_split_bf16(const void* q, const void* k_cache, const void* v_cache,
+                            void* o_part, float* lse_part, const int* cu_seqlens_q,
+                            const int* seqlens_k, const int* block_table, int B, int Hq, int Hkv,
+                            int max_seqlen_q, int max_seqlen_k, int total_q, int num_pages,
+                            int page_size, int max_pages_per_seq, int D, float softmax_scale,
+                            int causal, int splits, void* stream);
+
+/* Combine the split partials of fa_fwd_paged_split: with
+ * L = log2 sum_s 2^lse_part[s], o = sum_s o_part[s] 2^(lse_part[s] - L)
+ * (rounded once to the operand type) and lse = L; rows every range missed
+ * get 0 and -inf.  o is (total_q, H, D) contiguous, lse (H, total_q). */
+FA_API int fa_combine_splits(const void* o_part, const float* lse_part, void* o, float* lse,
+                      int splits, int total_q, int H, int D, void* stream);
+FA_API int fa_combine_splits_bf16(const void* o_part, const float* lse_part, void* o, float* lse,
+                           int splits, int total_q, int H, int D, void* stream);
+
 /* Size of the scratch array fa_bwd_fused_noalloc uses: 32 MiB per device. */
 #define FA_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -116,3 +116,18 @@ def test_varlen_and_paged_entry_points_reject_before_any_cuda_call():
             == _abi.FA_ERR_BAD_SHAPE, page
     assert lib.fa_fwd_paged(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, 64, 5, 96, 0.1, 1, 0, None) \
         == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
+    # fa_fwd_paged_split(q, kc, vc, o_part, lse_part, cu_q, seqlens_k, table, B, Hq, Hkv, max_q, max_k,
+    #                    total_q, num_pages, page_size, max_pages_per_seq, D, scale, causal, splits, stream):
+    # 300 keys are 3 key tiles, so at most 3 ranges; splitting needs GQA packing
+    for splits in (0, 4, 65):
+        assert lib.fa_fwd_paged_split(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, 64, 5, 64, 0.1, 1, splits,
+                                      None) == _abi.FA_ERR_BAD_SHAPE, splits
+    assert lib.fa_fwd_paged_split(p, p, p, p, p, p, p, p, 2, 4, 4, 1, 300, 2, 10, 64, 5, 64, 0.1, 1, 2, None) \
+        == _abi.FA_ERR_BAD_SHAPE
+    assert lib.fa_fwd_paged_split(p, p, p, p, p, p, p, p, 2, 4, 2, 1, 300, 2, 10, 64, 5, 96, 0.1, 1, 2, None) \
+        == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
+    # fa_combine_splits(o_part, lse_part, o, lse, splits, total_q, H, D, stream)
+    assert lib.fa_combine_splits(p, p, p, p, 0, 2, 4, 64, None) == _abi.FA_ERR_BAD_SHAPE
+    assert lib.fa_combine_splits(p, p, p, p, 65, 2, 4, 64, None) == _abi.FA_ERR_BAD_SHAPE
+    assert lib.fa_combine_splits(p, p, p, p, 2, 2, 4, 48, None) == _abi.FA_ERR_UNSUPPORTED_HEAD_DIM
+    assert lib.fa_combine_splits(p, p, 18, p, 2, 2, 4, 64, None) == _abi.FA_ERR_MISALIGNED

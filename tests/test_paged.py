@@ -13,12 +13,15 @@ partly filled, GQA and every head dim.
 
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import pytest
 import torch
 
 import triton_flash_attention_b200 as fa
 from oracle import fa2_oracle as orc
+from triton_flash_attention_b200 import varlen
 
 
 def _case(lens_q, lens_k, page, hq, hkv, d, seed, dtype=torch.float16):
@@ -40,13 +43,13 @@ def _case(lens_q, lens_k, page, hq, hkv, d, seed, dtype=torch.float16):
     return q, kc, vc, table, cu_q, np.asarray(lens_k, dtype=np.int32)
 
 
-def _run(q, kc, vc, table, cu_q, seqlens_k, causal):
+def _run(q, kc, vc, table, cu_q, seqlens_k, causal, num_splits=None):
     dev = "cuda"
     with torch.no_grad():
         return fa.paged_attention_forward(
             q.to(dev), kc.to(dev), vc.to(dev), torch.from_numpy(table).to(dev), torch.from_numpy(cu_q).to(dev),
             torch.from_numpy(seqlens_k).to(dev), max(int(np.diff(cu_q).max()), 1), max(int(seqlens_k.max()), 1),
-            causal, q.shape[-1] ** -0.5)
+            causal, q.shape[-1] ** -0.5, num_splits=num_splits)
 
 
 def _maxabs(a, b):
@@ -98,6 +101,35 @@ def test_validation():
         fa.scaled_dot_product_attention_paged(q.requires_grad_(), kc, kc, bt, cu, sk, 4, 20)
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         fa.scaled_dot_product_attention_paged(q.detach(), kc, kc, bt, cu, sk, 4, 20)
+    for bad in (0, 65, True, 2.0):
+        with pytest.raises(ValueError, match="num_splits"):
+            fa.scaled_dot_product_attention_paged(q.detach(), kc, kc, bt, cu, sk, 4, 20, num_splits=bad)
+
+
+def test_kv_splits_choice():
+    """The split count minimises ceil(units * s / sms) / s (the persistent
+    forward's waves per unit of keys), taking the smallest s within 1 %."""
+    for units, tiles, sms in [(32, 64, 148), (16, 64, 148), (70, 64, 148), (60, 8, 148), (64, 4, 148)]:
+        s = varlen.kv_splits(units, tiles, sms)
+        top = max(1, min(varlen.MAX_KV_SPLITS, tiles // varlen.MIN_TILES_PER_SPLIT))
+        assert 1 <= s <= top
+        cost = [math.ceil(units * x / sms) / x for x in range(1, top + 1)]
+        assert cost[s - 1] <= min(cost) * 1.01
+        assert all(c > min(cost) * 1.01 for c in cost[: s - 1])
+    assert varlen.kv_splits(16, 64, 148) == 9  # 144 pieces, one wave
+    assert varlen.kv_splits(32, 64, 148) == 9  # 288 pieces, two waves
+    # units filling more than half the SMs are not split
+    assert varlen.kv_splits(75, 64, 148) == 1 and varlen.kv_splits(128, 64, 148) == 1
+    assert varlen.kv_splits(32, 3, 148) == 1  # one range per unit keeps at least two key tiles
+
+
+def test_gqa_pack_rule():
+    """The Python side's packing rule equals the C library's: a power-of-two
+    group of 2 to 64 heads with max_seqlen_q * group <= 256."""
+    assert varlen.gqa_pack(32, 8, 1) == 4
+    assert varlen.gqa_pack(32, 8, 64) == 4 and varlen.gqa_pack(32, 8, 65) == 0
+    assert varlen.gqa_pack(32, 32, 1) == 0 and varlen.gqa_pack(24, 8, 1) == 0
+    assert varlen.gqa_pack(128, 1, 1) == 0 and varlen.gqa_pack(64, 1, 4) == 64
 
 
 # ---------------------------------------------------------------- GPU
@@ -218,3 +250,47 @@ def test_paged_sliding_window(lens_q, window):
                                    seqlens_k, causal=True, window=window)
     assert _maxabs(o.float().cpu(), ref["o"]) <= 2e-3
     assert _maxabs(lse.cpu().numpy(), ref["lse2"]) <= 1e-3
+
+
+# Split-KV (decode): each unit's keys cut into ranges merged by log-sum-exp.
+SPLIT_CASES = [
+    # lens_q, lens_k, page, hq, hkv, d, causal, splits
+    ([1, 1, 1, 1, 1], [4000, 5, 1000, 129, 2300], 64, 32, 8, 128, True, 8),
+    ([1, 1, 1], [700, 256, 33], 16, 8, 2, 64, True, 3),
+    ([1, 1], [1300, 600], 128, 8, 4, 32, False, 5),
+    ([4, 3], [1000, 300], 32, 16, 4, 128, True, 4),  # several queries: the causal limit crosses the ranges
+    ([1, 1, 1, 1], [8192, 8192, 1, 4096], 64, 32, 8, 128, True, None),  # automatic count
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", SPLIT_CASES)
+def test_paged_split_kv_against_float64(case):
+    lens_q, lens_k, page, hq, hkv, d, causal, splits = case
+    q, kc, vc, table, cu_q, seqlens_k = _case(lens_q, lens_k, page, hq, hkv, d, seed=sum(lens_k) + 7)
+    o, lse = _run(q, kc, vc, table, cu_q, seqlens_k, causal, num_splits=splits)
+    o1, lse1 = _run(q, kc, vc, table, cu_q, seqlens_k, causal, num_splits=1)
+    torch.cuda.synchronize()
+    ref = orc.sdpa_paged_reference(q.float().numpy(), kc.float().numpy(), vc.float().numpy(), table, cu_q,
+                                   seqlens_k, causal=causal)
+    assert _maxabs(o.float().cpu(), ref["o"]) <= 2e-3
+    assert _maxabs(o.float().cpu(), o1.float().cpu()) <= 2e-3
+    lse = lse.cpu().numpy()
+    finite = np.isfinite(ref["lse2"])
+    assert np.array_equal(np.isfinite(lse), finite)
+    assert _maxabs(lse[finite], ref["lse2"][finite]) <= 1e-3
+    assert _maxabs(lse[finite], lse1.cpu().numpy()[finite]) <= 1e-3
+    assert fa._abi.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_paged_split_kv_bf16():
+    lens_q, lens_k = [1, 1, 1], [3000, 77, 1500]
+    q, kc, vc, table, cu_q, seqlens_k = _case(lens_q, lens_k, 64, 16, 4, 64, seed=5, dtype=torch.bfloat16)
+    o, _ = _run(q, kc, vc, table, cu_q, seqlens_k, True, num_splits=6)
+    o1, _ = _run(q, kc, vc, table, cu_q, seqlens_k, True, num_splits=1)
+    ref = orc.sdpa_paged_reference(q.float().numpy(), kc.float().numpy(), vc.float().numpy(), table, cu_q,
+                                   seqlens_k, causal=True)
+    err, err1 = _maxabs(o.float().cpu(), ref["o"]), _maxabs(o1.float().cpu(), ref["o"])
+    # one more bf16 rounding (the partials) than the unsplit forward
+    assert err <= 2 * err1 + 4e-3, (err, err1)

@@ -54,7 +54,11 @@ SIGNATURES.update({
     "fa_bwd_varlen": (_i, [_p] * 13 + [_i] * 8 + [_f, _i, _i, _i, _p]),
 })
 SIGNATURES["fa_fwd_paged"] = (_i, [_p] * 8 + [_i] * 10 + [_f, _i, _i, _p])
-SIGNATURES.update({name + "_bf16": SIGNATURES[name] for name in ("fa_fwd_varlen", "fa_bwd_varlen", "fa_fwd_paged")})
+SIGNATURES["fa_fwd_paged_split"] = (_i, [_p] * 8 + [_i] * 10 + [_f, _i, _i, _p])
+SIGNATURES["fa_combine_splits"] = (_i, [_p] * 4 + [_i] * 4 + [_p])
+SIGNATURES.update({name + "_bf16": SIGNATURES[name]
+                   for name in ("fa_fwd_varlen", "fa_bwd_varlen", "fa_fwd_paged", "fa_fwd_paged_split",
+                                "fa_combine_splits")})
 SIGNATURES.update({
     "fa_fwd_vdim": (_i, [_p] * 5 + [_i] * 7 + [_s] * 4 + [_f, _i, _p]),
     "fa_bwd_vdim": (_i, [_p] * 11 + [_i] * 7 + [_s] * 8 + [_f, _i, _i, _p]),

@@ -249,6 +249,73 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(float* __restrict__ o_acc
   }
 }
 
+// Split-KV combine: o (rows x D, operand type) and lse <- the S partials
+// o_part (S x rows x D), lse_part (S x lse_stride): with L = log2 sum_s
+// 2^lse_s, o = sum_s o_s 2^(lse_s - L), lse = L.  Row `row` = q * H + h of
+// the packed (total_q, H, D) layout has its statistics at h * total_q + q.
+template <int DT>
+__global__ void __launch_bounds__(256) fa_combine_kernel(const uint16_t* __restrict__ o_part,
+                                                         const float* __restrict__ lse_part,
+                                                         uint16_t* __restrict__ o, float* __restrict__ lse, int S,
+                                                         int total_q, int H, int D) {
+  const int vec_per_row = D / 8;
+  const long long rows = (long long)total_q * H;
+  const long long total = rows * vec_per_row;
+  const long long lse_stride = rows;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long row = idx / vec_per_row;
+    const int part = int(idx % vec_per_row);
+    const long long li = (long long)(row % H) * total_q + row / H;
+    float mx = -INFINITY;
+    for (int s = 0; s < S; ++s) mx = fmaxf(mx, lse_part[s * lse_stride + li]);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float L = -INFINITY;
+    if (mx != -INFINITY) {
+      float tot = 0.f;
+      for (int s = 0; s < S; ++s) {
+        const float wgt = exp2f(lse_part[s * lse_stride + li] - mx);
+        tot += wgt;
+        const uint4 pk = *reinterpret_cast<const uint4*>(o_part + (s * rows + row) * D + part * 8);
+        const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 p = unpack2<DT>(w4[i]);
+          acc[2 * i] += wgt * p.x;
+          acc[2 * i + 1] += wgt * p.y;
+        }
+      }
+      const float inv = 1.f / tot;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= inv;
+      L = mx + log2f(tot);
+    }
+    uint4 out;
+    out.x = pack2<DT>(acc[0], acc[1]);
+    out.y = pack2<DT>(acc[2], acc[3]);
+    out.z = pack2<DT>(acc[4], acc[5]);
+    out.w = pack2<DT>(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(o + row * D + part * 8) = out;
+    if (part == 0) lse[li] = L;
+  }
+}
+
+int launch_combine_splits(const void* o_part, const float* lse_part, void* o, float* lse, int S, int total_q, int H,
+                          int D, int dtype, cudaStream_t stream) {
+  if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  const int sms = device_sm_count();
+  long long blocks = ((long long)total_q * H * (D / 8) + 255) / 256;
+  if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
+  if (blocks < 1) blocks = 1;
+  const uint16_t* p16 = static_cast<const uint16_t*>(o_part);
+  uint16_t* o16 = static_cast<uint16_t*>(o);
+  if (dtype == DT_BF16)
+    fa_combine_kernel<DT_BF16><<<unsigned(blocks), 256, 0, stream>>>(p16, lse_part, o16, lse, S, total_q, H, D);
+  else
+    fa_combine_kernel<DT_F16><<<unsigned(blocks), 256, 0, stream>>>(p16, lse_part, o16, lse, S, total_q, H, D);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
                          int D, int dtype, cudaStream_t stream) {
   if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;

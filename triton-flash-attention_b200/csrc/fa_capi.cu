@@ -467,7 +467,7 @@ int bwd_varlen_impl(const void* q, const void* k, const void* v, const void* o, 
 int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void* o, float* lse, const int* cu_q,
                    const int* seqlens_k, const int* block_table, int B, int Hq, int Hkv, int max_q, int max_k,
                    int total_q, int num_pages, int page_size, int bt_stride, int D, float softmax_scale, int causal,
-                   int window, void* stream, int dtype) {
+                   int window, void* stream, int dtype, int splits = 1) {
   if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || max_q <= 0 || max_k <= 0 || total_q <= 0 ||
       num_pages <= 0 || bt_stride <= 0)
@@ -485,6 +485,11 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   FwdArgs a;
   const int pr = page_size < 128 ? page_size : 128;
   const int pack = gqa_pack(Hq, Hkv, max_q);
+  // split-KV: GQA-packed query tiles and no window; o and lse hold the
+  // splits' partials, (splits, total_q, Hq, D) and (splits, Hq, total_q)
+  const int key_tiles = (max_k + 127) / 128;
+  if (splits < 1 || splits > FA_MAX_KV_SPLITS || splits > key_tiles) return FA_ERR_BAD_SHAPE;
+  if (splits > 1 && (pack < 2 || window > 0)) return FA_ERR_BAD_SHAPE;
   if ((rc = make_q_map(&a.tmap_q, q, 1, Hq, total_q, D, sq.v, dtype, pack))) return rc;
   if ((rc = make_map(&a.tmap_k, k_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
   if ((rc = make_map(&a.tmap_v, v_cache, 1, Hkv, num_pages * page_size, D, sk.v, pr, dtype))) return rc;
@@ -503,8 +508,24 @@ int fwd_paged_impl(const void* q, const void* k_cache, const void* v_cache, void
   a.o_sh = sq.v[1];
   a.o_sn = sq.v[2];
   a.lse = lse;
+  if (splits > 1) {
+    a.split.n = splits;
+    a.split.tiles = (key_tiles + splits - 1) / splits;
+    a.split.o_stride = (long long)total_q * Hq * D;
+    a.split.lse_stride = (long long)Hq * total_q;
+  }
   a.stream = static_cast<cudaStream_t>(stream);
   return launch_fwd(a, D);
+}
+
+int combine_impl(const void* o_part, const float* lse_part, void* o, float* lse, int splits, int total_q, int H, int D,
+                 void* stream, int dtype) {
+  if (!supported_d(D)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (splits < 1 || splits > FA_MAX_KV_SPLITS || total_q <= 0 || H <= 0) return FA_ERR_BAD_SHAPE;
+  if (!o_part || !lse_part || !o || !lse) return FA_ERR_BAD_SHAPE;
+  if (!aligned16(o_part) || !aligned16(o)) return FA_ERR_MISALIGNED;
+  return launch_combine_splits(o_part, lse_part, o, lse, splits, total_q, H, D, dtype,
+                               static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -846,6 +867,34 @@ extern "C" int fa_fwd_paged_bf16(const void* q, const void* k_cache, const void*
   return fwd_paged_impl(q, k_cache, v_cache, o, lse, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv, max_seqlen_q,
                         max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D, softmax_scale, causal,
                         window, stream, DT_BF16);
+}
+
+extern "C" int fa_fwd_paged_split(const void* q, const void* k_cache, const void* v_cache, void* o_part,
+                                  float* lse_part, const int* cu_seqlens_q, const int* seqlens_k,
+                                  const int* block_table, int B, int Hq, int Hkv, int max_seqlen_q, int max_seqlen_k,
+                                  int total_q, int num_pages, int page_size, int max_pages_per_seq, int D,
+                                  float softmax_scale, int causal, int splits, void* stream) {
+  return fwd_paged_impl(q, k_cache, v_cache, o_part, lse_part, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv,
+                        max_seqlen_q, max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D,
+                        softmax_scale, causal, 0, stream, DT_F16, splits);
+}
+extern "C" int fa_fwd_paged_split_bf16(const void* q, const void* k_cache, const void* v_cache, void* o_part,
+                                       float* lse_part, const int* cu_seqlens_q, const int* seqlens_k,
+                                       const int* block_table, int B, int Hq, int Hkv, int max_seqlen_q,
+                                       int max_seqlen_k, int total_q, int num_pages, int page_size,
+                                       int max_pages_per_seq, int D, float softmax_scale, int causal, int splits,
+                                       void* stream) {
+  return fwd_paged_impl(q, k_cache, v_cache, o_part, lse_part, cu_seqlens_q, seqlens_k, block_table, B, Hq, Hkv,
+                        max_seqlen_q, max_seqlen_k, total_q, num_pages, page_size, max_pages_per_seq, D,
+                        softmax_scale, causal, 0, stream, DT_BF16, splits);
+}
+extern "C" int fa_combine_splits(const void* o_part, const float* lse_part, void* o, float* lse, int splits,
+                                 int total_q, int H, int D, void* stream) {
+  return combine_impl(o_part, lse_part, o, lse, splits, total_q, H, D, stream, DT_F16);
+}
+extern "C" int fa_combine_splits_bf16(const void* o_part, const float* lse_part, void* o, float* lse, int splits,
+                                      int total_q, int H, int D, void* stream) {
+  return combine_impl(o_part, lse_part, o, lse, splits, total_q, H, D, stream, DT_BF16);
 }
 
 extern "C" int fa_device_status(int reset) {

@@ -116,6 +116,17 @@ struct DropArgs {
   uint32_t seed_lo = 0, seed_hi = 0;
 };
 
+// Split-KV forward (a kernel parameter of its own): the key tiles of every
+// unit are cut into n ranges of `tiles` key tiles; range s writes its partial
+// O (normalised by its own row sums) at o + s * o_stride and its base-2
+// log-sum-exp at lse + s * lse_stride, for a combine pass to merge.
+struct SplitArgs {
+  int n = 1;
+  int tiles = 0;
+  long long o_stride = 0;
+  long long lse_stride = 0;
+};
+
 __host__ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
   x ^= x >> 16;
   x *= 0x7feb352du;

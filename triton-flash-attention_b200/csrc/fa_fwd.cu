@@ -111,17 +111,25 @@ struct Cfg {
 // Key tiles: the unit streams key tiles kt0 .. kt0 + n_max - 1 (local index
 // j = 0 .. n_max - 1); tile t is active for local j in [js[t], n_kv[t])
 // (js = 0 and kt0 = 0 unless a sliding window hides leading keys).
+// With SPLIT, unit u is key range u / (units without the split) of unit
+// u % (that count), and its key tiles are cut to that range.
 struct Unit {
   int b, h, kvh, row0, rows, kt0, js[QT], n_kv[QT], n_max;
+  int split;
   Seq sq;
 };
-template <bool PACK, bool WIN>
-__device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
+template <bool PACK, bool WIN, bool SPLIT = false>
+__device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u, const SplitArgs& sp) {
   const int G = PACK ? shp.pack_g : 1;
   const int rows = BM / G;  // query rows per head in a tile
   const int BH = shp.B * (G > 1 ? shp.Hkv : shp.Hq);
   const int n_qblk = (shp.Nq + QT * rows - 1) / (QT * rows);
   Unit w;
+  w.split = 0;
+  if (SPLIT) {
+    w.split = u / (BH * n_qblk);
+    u -= w.split * (BH * n_qblk);
+  }
   const int bh = u % BH;
   if (PACK) {
     w.b = bh / shp.Hkv;
@@ -141,6 +149,11 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
   for (int t = 0; t < QT; ++t) {
     end[t] = kv_tiles_for_rows(shp, w.sq, w.row0 + t * rows, rows, BN);
     first[t] = WIN ? kv_first_tile(shp, w.sq, w.row0 + t * rows, BN) : 0;
+    if (SPLIT) {
+      const int lo = w.split * sp.tiles;
+      first[t] = first[t] > lo ? first[t] : lo;
+      end[t] = end[t] < lo + sp.tiles ? end[t] : lo + sp.tiles;
+    }
     if (first[t] >= end[t]) first[t] = end[t] = 0;  // no visible key
     else w.kt0 = first[t] < w.kt0 ? first[t] : w.kt0;
   }
@@ -158,12 +171,12 @@ __device__ __forceinline__ Unit unit_of(const AttnShape& shp, int u) {
 
 }  // namespace fwd
 
-template <int D, int DT, bool PACK, bool WIN, bool BITS, bool DROP>
+template <int D, int DT, bool PACK, bool WIN, bool BITS, bool DROP, bool SPLIT>
 __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const AttnShape shp, uint16_t* __restrict__ o_ptr,
                   const long long o_sb, const long long o_sh, const long long o_sn, float* __restrict__ lse_ptr,
-                  const int n_units, const MaskBits mk, const DropArgs dr) {
+                  const int n_units, const MaskBits mk, const DropArgs dr, const SplitArgs sp) {
   using namespace fwd;
   using C = Cfg<D>;
   using G = TileGeom<D>;
@@ -257,7 +270,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of<PACK, WIN>(shp, ui);
+          const Unit w = unit_of<PACK, WIN, SPLIT>(shp, ui, sp);
           if (w.n_max == 0) continue;
           if (is_k) {
             const int qb = uc % C::QB;
@@ -323,7 +336,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
         for (int k = 0; ok; ++k) {
           const int ui = snake_unit(cta, k, n_cta, n_units);
           if (ui >= n_units) break;
-          const Unit w = unit_of<PACK, WIN>(shp, ui);
+          const Unit w = unit_of<PACK, WIN, SPLIT>(shp, ui, sp);
           if (w.n_max == 0) continue;
           const int qb = uc % C::QB;
           if (!mbar_wait(q_full + qb, uint32_t(uc / C::QB) & 1, ctl, 10)) { ok = false; break; }
@@ -459,7 +472,7 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
     for (int k = 0; ok; ++k) {
       const int ui = snake_unit(cta, k, n_cta, n_units);
       if (ui >= n_units) break;
-      const Unit w = unit_of<PACK, WIN>(shp, ui);
+      const Unit w = unit_of<PACK, WIN, SPLIT>(shp, ui, sp);
       // query row (within the batch) and head of this thread's tile row
       const int r = w.row0 + t * w.rows + (PACK ? row_local % w.rows : row_local);
       const int hq = w.h + (PACK ? row_local / w.rows : 0);
@@ -648,7 +661,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       const bool row_ok = r < w.sq.nq;
       const float inv_l = (l > 0.f ? 1.f / l : 0.f) * (DROP ? dr.r : 1.f);
-      uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)hq * o_sh + (long long)(w.sq.q0 + r) * o_sn;
+      uint16_t* orow = o_ptr + (long long)w.sq.tb * o_sb + (long long)hq * o_sh + (long long)(w.sq.q0 + r) * o_sn +
+                       (SPLIT ? w.split * sp.o_stride : 0);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
@@ -677,7 +691,8 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
       }
       if (nt > 0) ++oc;
       if (row_ok) {
-        lse_ptr[row_stat_index(shp, w.sq, w.b, hq, r)] = l > 0.f ? m + lg2(l) : -INFINITY;
+        lse_ptr[row_stat_index(shp, w.sq, w.b, hq, r) + (SPLIT ? w.split * sp.lse_stride : 0)] =
+            l > 0.f ? m + lg2(l) : -INFINITY;
       }
     }
   }
@@ -690,11 +705,11 @@ __global__ void __launch_bounds__(fwd::NUM_THREADS, 1)
   }
 }
 
-template <int D, int DT, bool PACK, bool WIN, bool BITS = false, bool DROP = false>
+template <int D, int DT, bool PACK, bool WIN, bool BITS = false, bool DROP = false, bool SPLIT = false>
 int launch_fwd_t(const FwdArgs& a) {
   using C = fwd::Cfg<D>;
   const int smem = C::SMEM_BYTES;
-  auto kern = fa_fwd_kernel<D, DT, PACK, WIN, BITS, DROP>;
+  auto kern = fa_fwd_kernel<D, DT, PACK, WIN, BITS, DROP, SPLIT>;
   // The register split inside the kernel assumes the launch count; a build
   // that allocated a different number must not run (an increase that does
   // not fit would wait forever).
@@ -709,11 +724,12 @@ int launch_fwd_t(const FwdArgs& a) {
   const int G = a.shape.pack_g > 1 ? a.shape.pack_g : 1;
   const int rows = fwd::QT * (fwd::BM / G);
   const int n_qblk = (a.shape.Nq + rows - 1) / rows;
-  const int n_units = n_qblk * a.shape.B * (G > 1 ? a.shape.Hkv : a.shape.Hq);
+  const int n_units = n_qblk * a.shape.B * (G > 1 ? a.shape.Hkv : a.shape.Hq) * (SPLIT ? a.split.n : 1);
   const int sms = device_sm_count();
   const int n_cta = n_units < sms ? n_units : sms;
   kern<<<dim3(unsigned(n_cta)), fwd::NUM_THREADS, smem, a.stream>>>(a.tmap_q, a.tmap_k, a.tmap_v, a.shape, static_cast<uint16_t*>(a.o),
-                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units, a.mask, a.drop);
+                                                                    a.o_sb, a.o_sh, a.o_sn, a.lse, n_units, a.mask, a.drop,
+                                                                    a.split);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -721,6 +737,8 @@ int launch_fwd_t(const FwdArgs& a) {
 // masks, are separate instantiations.
 template <int D, int DT>
 int launch_fwd_l(const FwdArgs& a) {
+  // split-KV: GQA-packed, no mask, window or dropout (checked by the caller)
+  if (a.split.n > 1) return launch_fwd_t<D, DT, true, false, false, false, true>(a);
   if (a.drop.t) return launch_fwd_t<D, DT, false, false, false, true>(a);  // dense, unpacked, no mask or window
   if (a.mask.bits) return launch_fwd_t<D, DT, false, false, true>(a);  // dense, unpacked, no window
   if (a.shape.window > 0)

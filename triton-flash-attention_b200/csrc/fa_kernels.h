@@ -23,6 +23,7 @@ struct FwdArgs {
   float* lse;
   MaskBits mask;  // dense boolean mask (bits == nullptr: none)
   DropArgs drop;  // attention dropout (t == 0: none)
+  SplitArgs split;  // split-KV partial outputs (n == 1: none)
   cudaStream_t stream;
 };
 
@@ -85,6 +86,8 @@ int launch_dq_convert(const float* acc, void* dq, long long sb, long long sh, lo
 // roundup(Nq, 128) / 32) uint32 words, contiguous.
 int launch_mask_pack(const void* mask, long long sb, long long sh, long long sq, long long sk, int Bm, int Hm, int Nq,
                      int Nk, uint32_t* bits, uint32_t* bits_t, cudaStream_t stream);
+int launch_combine_splits(const void* o_part, const float* lse_part, void* o, float* lse, int S, int total_q, int H,
+                          int D, int dtype, cudaStream_t stream);
 int launch_merge_partial(float* o_acc, float* lse_acc, const void* o_part, const float* lse_part, long long rows,
                          int D, int dtype, cudaStream_t stream);
 

@@ -184,20 +184,89 @@ def scaled_dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seql
                                      max_seqlen_k, is_causal, softmax_scale, window)
 
 
+# Most key-range splits of the paged forward's split-KV form, and the fewest
+# 128-key tiles a range keeps.
+MAX_KV_SPLITS = 16
+MIN_TILES_PER_SPLIT = 2
+_sm_count: dict[int, int] = {}
+
+
+def gqa_pack(hq: int, hkv: int, max_seqlen_q: int) -> int:
+    """Query heads the forward packs into one 128-row query tile (0: none),
+    as the C library decides: a power-of-two group of 2 to 64 heads whose
+    rows fit 256."""
+    g = hq // hkv
+    if g < 2 or g > 64 or g & (g - 1) or max_seqlen_q * g > 256:
+        return 0
+    return g
+
+
+def kv_splits(units: int, key_tiles: int, sms: int) -> int:
+    """How many key ranges the paged forward cuts each unit's keys into.
+
+    The persistent forward runs ``units * s`` equal pieces over ``sms`` CTAs,
+    so its time goes as ``ceil(units * s / sms) / s`` units' worth of keys.
+    This returns the smallest ``s`` within 1 % of the best such time for
+    ``s <= MAX_KV_SPLITS`` with at least ``MIN_TILES_PER_SPLIT`` key tiles
+    per range.  Each range pays a query load, an output store and a combine
+    pass, and a unit's 128-row tiles cost the same whatever the split, so
+    splitting is kept for units that leave more than half the SMs idle
+    (measured: 128 units on 148 SMs ran 8 % slower in 8 ranges); otherwise 1."""
+    if units <= 0 or 2 * units > sms:
+        return 1
+    top = max(1, min(MAX_KV_SPLITS, key_tiles // MIN_TILES_PER_SPLIT))
+    cost = {s: math.ceil(units * s / sms) / s for s in range(1, top + 1)}
+    best = min(cost.values())
+    return min(s for s, c in cost.items() if c <= best * 1.01)
+
+
+def _sms(device: torch.device) -> int:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _sm_count:
+        _sm_count[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return _sm_count[index]
+
+
 def paged_attention_forward(q, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k, max_seqlen_q: int,
-                            max_seqlen_k: int, causal: bool, softmax_scale: float, window: int = 0):
+                            max_seqlen_k: int, causal: bool, softmax_scale: float, window: int = 0,
+                            num_splits: int | None = None):
     """Forward over a paged K/V cache: returns ``(o, lse2)`` like
-    ``varlen_attention_forward``."""
+    ``varlen_attention_forward``.
+
+    With GQA packing and no window, few (sequence, K/V head) units leave SMs
+    idle (decode of a few sequences): the keys of each unit are then cut
+    into ``num_splits`` ranges (``kv_splits`` when None), each range's
+    partial output goes to scratch, and ``fa_combine_splits`` merges them by
+    their log-sum-exps."""
     total_q, hq, d = q.shape
     num_pages, page_size, hkv = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
     batch = cu_seqlens_q.numel() - 1
+    key_tiles = (int(max_seqlen_k) + 127) // 128
+    pack = gqa_pack(hq, hkv, int(max_seqlen_q))
+    if num_splits is None:
+        n_qblk = -(-int(max_seqlen_q) // (256 // pack)) if pack else 0
+        num_splits = kv_splits(batch * hkv * n_qblk, key_tiles, _sms(q.device)) if pack and not window else 1
     o = torch.empty_like(q)
     lse = torch.empty((hq, total_q), device=q.device, dtype=torch.float32)
+    stream = _stream_handle(q.device)
+    if num_splits > 1:
+        o_part = torch.empty((num_splits, total_q, hq, d), device=q.device, dtype=q.dtype)
+        lse_part = torch.empty((num_splits, hq, total_q), device=q.device, dtype=torch.float32)
+        rc = _abi.entry("fa_fwd_paged_split", q.dtype)(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o_part.data_ptr(), lse_part.data_ptr(),
+            cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), block_table.data_ptr(), batch, hq, hkv,
+            int(max_seqlen_q), int(max_seqlen_k), total_q, num_pages, page_size, block_table.shape[1], d,
+            float(softmax_scale), 1 if causal else 0, int(num_splits), stream)
+        _abi.check(rc, "fa_fwd_paged_split")
+        rc = _abi.entry("fa_combine_splits", q.dtype)(o_part.data_ptr(), lse_part.data_ptr(), o.data_ptr(),
+                                                      lse.data_ptr(), int(num_splits), total_q, hq, d, stream)
+        _abi.check(rc, "fa_combine_splits")
+        return o, lse
     rc = _abi.entry("fa_fwd_paged", q.dtype)(
         q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), lse.data_ptr(),
         cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), block_table.data_ptr(), batch, hq, hkv,
         int(max_seqlen_q), int(max_seqlen_k), total_q, num_pages, page_size, block_table.shape[1], d,
-        float(softmax_scale), 1 if causal else 0, int(window), _stream_handle(q.device))
+        float(softmax_scale), 1 if causal else 0, int(window), stream)
     _abi.check(rc, "fa_fwd_paged")
     return o, lse
 
@@ -205,7 +274,8 @@ def paged_attention_forward(q, k_cache, v_cache, block_table, cu_seqlens_q, seql
 def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_seqlens_q, seqlens_k,
                                        max_seqlen_q: int, max_seqlen_k: int, *, is_causal: bool = False,
                                        scale: float | None = None, enable_gqa: bool = False,
-                                       window_size: int | None = None) -> torch.Tensor:
+                                       window_size: int | None = None,
+                                       num_splits: int | None = None) -> torch.Tensor:
     """Attention of packed queries over a paged K/V cache (forward only).
 
     ``query``: ``(total_q, Hq, D)`` with ``cu_seqlens_q`` int32 prefix sums;
@@ -215,7 +285,10 @@ def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_
     counts.  Cache rows past a sequence's length must be finite (a zeroed
     cache is).  ``is_causal`` aligns the mask bottom-right, so a sequence's
     queries are its last ``nq`` positions (decode: one query sees every
-    key)."""
+    key).  ``num_splits`` cuts each (sequence, K/V head) unit's keys into
+    that many ranges merged by log-sum-exp (split-KV; GQA-packed queries and
+    no window); None picks it from the SM count (``kv_splits``), 1 turns it
+    off."""
     if not isinstance(is_causal, bool):
         raise TypeError("is_causal must be a bool")
     if not isinstance(enable_gqa, bool):
@@ -242,6 +315,9 @@ def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_
         raise ValueError("block_table and seqlens_k must have one row per sequence of cu_seqlens_q")
     if any(t.requires_grad for t in (query, k_cache, v_cache)) and torch.is_grad_enabled():
         raise RuntimeError("the paged K/V path is forward only; run it under torch.no_grad()")
+    if num_splits is not None and (isinstance(num_splits, bool) or not isinstance(num_splits, int) or
+                                   not 1 <= num_splits <= 64):
+        raise ValueError("num_splits must be an int from 1 to 64 or None")
     # the varlen checks on (query, one page of the cache seen as keys)
     kv_view = k_cache[0]
     window = _window_arg(window_size, is_causal)
@@ -250,5 +326,5 @@ def scaled_dot_product_attention_paged(query, k_cache, v_cache, block_table, cu_
     softmax_scale = float(scale) if scale is not None else query.shape[-1] ** -0.5
     o, _ = paged_attention_forward(query.contiguous(), k_cache.contiguous(), v_cache.contiguous(),
                                    block_table.contiguous(), cu_seqlens_q.contiguous(), seqlens_k.contiguous(),
-                                   max_seqlen_q, max_seqlen_k, is_causal, softmax_scale, window)
+                                   max_seqlen_q, max_seqlen_k, is_causal, softmax_scale, window, num_splits)
     return o
