@@ -269,6 +269,26 @@ def dist_setup(n_gpus: int):
     return rank, world, local
 
 
+def gpu_local_cpus(dev) -> set[int] | None:
+    """The host CPUs on the GPU's NUMA node (sysfs ``local_cpulist`` of its
+    PCI function), restricted to those this process may run on; None when
+    unknown."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        path = f"/sys/bus/pci/devices/{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0/local_cpulist"
+        cpus = set()
+        with open(path) as f:
+            for part in f.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def barrier_max(world: int, value: float) -> float:
     if world == 1:
         return value
@@ -583,6 +603,13 @@ def run_ours(args) -> None:
     # scaled_dot_product_attention / autograd.  The copies of neighbouring
     # steps overlap the compute (input copies on one stream into two device
     # buffers, output copies on another), as a data pipeline would run it.
+    # The pinned buffers are allocated, and the section runs, on the GPU's
+    # NUMA node, as a NUMA-aware loader would place them (the process's
+    # previous CPU set is restored afterwards).
+    prev_cpus = os.sched_getaffinity(0)
+    local_cpus = gpu_local_cpus(dev)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
     hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
     outs = [torch.empty(B, H, N, D, dtype=torch.float16).pin_memory() for _ in range(4)]
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
@@ -637,6 +664,8 @@ def run_ours(args) -> None:
     e2e_ms = barrier_max(world, s2.elapsed_time(e2) / e2e_steps)
     e2e_value = world * fl / (e2e_ms * 1e-3) / 1e12
     del bufs, outs, hq, hk, hv, hdo
+    os.sched_setaffinity(0, prev_cpus)
+    e2e_host = {"numa_local_cpus": len(local_cpus) if local_cpus else None, "process_cpus": len(prev_cpus)}
 
     # ---------------- the same step through other implementations (1 GPU)
     comp = None
@@ -695,7 +724,7 @@ def run_ours(args) -> None:
                                  "while the host enqueues the timed steps (not timed)"},
             "pct_of_peak": round(100.0 * value / world / peaks["bf16_tflops"], 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4), "host": e2e_host,
                     "copies": "pinned host buffers; copies of neighbouring steps overlap the compute"},
             "backward": "fused dK/dV + dQ (dQ summed by fp32 reduce-adds)" if fused
                         else "deterministic: separate dQ and dK/dV kernels",
